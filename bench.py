@@ -1,0 +1,398 @@
+"""Benchmark of ma_deform_attn on B200: device-timed microseconds per call, roofline, CPU baseline, end to end.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1h] [--mode auto] [--impl ours|reference]
+    python bench.py --sweep [--dtype ...]        # the fused/project crossover table that fits FUSED_LIMIT_SM100
+
+A step is one ma_deform_attn call on one batch of the workload (default c1h: RT-DETR 640x640 decoder layer, float16,
+B=1 image per GPU, Q=300, C=256, H=8, D=32, L=3, P=4). Timing follows upstream bench/bench.py:40-61 (calls captured
+in a CUDA graph, device-timed with CUDA events), with one change: every call reads a different input set from a pool
+whose total size exceeds twice the 126 MB L2, so each call's memory comes from HBM ("l2": "rotating inputs > 2x L2").
+With --gpus N under torchrun each rank runs its own images (batch sharding, no collective in the data path), the
+timed region is bracketed by barriers and synchronisation, and the slowest rank's time is reported.
+
+--impl reference times the CPU implementation of the same call: upstream's algorithm (nn.Linear + grid_sample, the
+oracle's torch_port on torch's CPU operators) with all host threads, on rank 0 only.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from marearts_tinydeform_b200 import _native, choose_mode, ma_deform_attn, workloads  # noqa: E402
+
+L2_BYTES = 126 * 2 ** 20
+METRIC = 'µs per ma_deform_attn call (device-timed) and achieved HBM GB/s vs peak'
+
+
+def peaks():
+    path = os.path.join(ROOT, 'MEASURED_PEAKS.json')
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p['hbm_gbs']), 'measured'
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 'fallback'
+
+
+def committed_traffic(kernel, config):
+    """DRAM bytes per launch from the committed ncu summary (profiles/traffic.json), or None."""
+    try:
+        with open(os.path.join(ROOT, 'profiles', 'traffic.json')) as f:
+            return json.load(f).get(f'{kernel}@{config}')
+    except (OSError, ValueError):
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi samples (SM clock, throttle reasons) taken every 100 ms while the timed region runs."""
+
+    QUERY = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+             'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+             'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, index):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.index}', f'--query-gpu={self.QUERY}',
+                                          '--format=csv,noheader,nounits', '-lms', '100'],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(',')])
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['nvidia-smi unavailable'], 'samples': 0}
+        sm = [float(r[1]) for r in self.rows if r[1].replace('.', '').isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace('.', '').isdigit()]
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.lower() == 'active'})
+        return {'sm_mhz': statistics.median(sm) if sm else None, 'sm_max_mhz': max(mx) if mx else None,
+                'reasons': reasons, 'samples': len(self.rows)}
+
+
+def input_pool(cfg_name, B, device, min_bytes):
+    """Distinct input sets (memory, loc, attn per set; weights shared) totalling at least min_bytes."""
+    base = workloads.make_inputs(cfg_name, seed=0, B=B, device=device)
+    per_set = sum(t.numel() * t.element_size() for t in (base[0], base[5], base[6]))
+    n = max(2, -(-min_bytes // per_set))
+    g = torch.Generator(device=device).manual_seed(1234)
+    pool = []
+    B_, Q_, H_, L_, P_ = base[6].shape
+    for i in range(n):
+        mem = torch.randn(base[0].shape, generator=g, device=device).to(base[0].dtype)
+        loc = torch.rand(base[5].shape, generator=g, device=device).to(base[5].dtype)
+        logits = torch.randn(B_, Q_, H_, L_ * P_, generator=g, device=device)
+        attn = logits.softmax(-1).view(base[6].shape).to(base[6].dtype)
+        pool.append((mem, loc, attn))
+    pool[0] = (base[0], base[5], base[6])
+    return base, pool
+
+
+def graph_time_us(fn, steps, warmup):
+    """Device time per call of `fn(i)`, i = 0 .. steps-1, captured as one CUDA graph (upstream bench.py:40-61)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i in range(max(warmup, 3)):
+            fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    before = _native.launch_count()
+    with torch.cuda.graph(g):
+        for i in range(steps):
+            fn(i)
+    launches = _native.launch_count() - before
+    g.replay()
+    torch.cuda.synchronize()
+    return g, launches
+
+
+def time_graph(g, steps, reps=1):
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = float('inf')
+    for _ in range(reps):
+        torch.cuda.synchronize()
+        start.record()
+        g.replay()
+        end.record()
+        end.synchronize()
+        best = min(best, start.elapsed_time(end) * 1e3 / steps)
+    return best
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device('cuda', local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier_max(value, world):
+    if world == 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device='cuda')
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_time_us(cfg_name, budget_s=10.0, max_calls=50):
+    """The CPU path (oracle torch_port = upstream's nn.Linear + grid_sample) on all host threads, bounded."""
+    from oracle import deform_oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    args = workloads.make_inputs(cfg_name, seed=0)
+    with torch.inference_mode():
+        for _ in range(2):
+            deform_oracle.torch_port(*args)
+        times, t_end = [], time.perf_counter() + budget_s
+        while len(times) < max_calls and time.perf_counter() < t_end:
+            t0 = time.perf_counter()
+            deform_oracle.torch_port(*args)
+            times.append(time.perf_counter() - t0)
+    return statistics.median(times) * 1e6, threads, len(times)
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get('RANK', '0'))
+    if rank != 0:
+        return
+    us, threads, n = cpu_time_us(args.config, budget_s=max(5.0, min(60.0, 0.05 * (args.steps + args.warmup))),
+                                 max_calls=args.steps + args.warmup)
+    cfg = workloads.CONFIGS[args.config]
+    line = {
+        'metric': METRIC, 'value': round(us, 2), 'unit': 'us', 'impl': 'reference', 'n_gpus': args.gpus,
+        'steps': n, 'warmup': 2, 'ms_per_step': round(us / 1e3, 4), 'higher_is_better': False,
+        'scaling': 'weak', 'vs_baseline': None, 'dtype': str(cfg['dtype']).replace('torch.', ''),
+        'data': 'synthetic (seeded, BASELINE config shapes)',
+        'config': config_dict(args.config, 1, args.mode, 'CPU'),
+        'cpu_baseline': {'value': round(us, 2), 'unit': 'us', 'cores': threads, 'kind': 'port',
+                         'sample': f'{n} calls of {args.config} (B=1), median, torch CPU ops, {threads} threads'},
+        'e2e': {'value': round(us, 2), 'unit': 'us', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(name, world, mode, where='GPU'):
+    c = workloads.CONFIGS[name]
+    return {'workload': f'{name}: B={c["B"]} per {where}, Q={c["Q"]}, C={c["C"]}, H={c["H"]}, D={c["D"]}, '
+                        f'levels={c["levels"]}, P={c["P"]}',
+            'global_batch': c['B'] * world, 'queries': c['Q'], 'mode': mode,
+            'parallelism': f'batch-shard x{world}' if world > 1 else 'single GPU',
+            'l2': 'rotating inputs > 2x L2 (126 MB) between calls'}
+
+
+def kernel_bytes(kind, B, Q, N, C, H, D, L, P, e, bias=True):
+    HD = H * D
+    if kind == 'fused':
+        return workloads.algorithmic_bytes(B, Q, N, C, H, D, L, P, e, bias)
+    if kind == 'proj':
+        return e * (B * N * C + HD * C + (HD if bias else 0) + B * N * HD)
+    if kind == 'sample':
+        return e * (B * N * HD + 3 * B * Q * H * L * P + B * Q * HD)
+    raise ValueError(kind)
+
+
+def run_ours(args):
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device('cuda', local)
+    _native.load()
+    cfg = workloads.CONFIGS[args.config]
+    B = cfg['B']
+    base, pool = input_pool(args.config, B, dev, 2 * L2_BYTES)
+    W, bias, shapes, starts = base[1], base[2], base[3], base[4]
+    mode = args.mode if args.mode != 'auto' else choose_mode(base[0], W, base[5])
+    N, C, H, D, L, P, Q = base[0].shape[1], cfg['C'], cfg['H'], cfg['D'], len(cfg['levels']), cfg['P'], cfg['Q']
+    e = base[0].element_size()
+    outs = [torch.empty(B, Q, H * D, dtype=base[0].dtype, device=dev) for _ in range(2)]
+
+    def call(i):
+        mem, loc, attn = pool[i % len(pool)]
+        return ma_deform_attn(mem, W, bias, shapes, starts, loc, attn, mode=args.mode)
+
+    with torch.inference_mode():
+        g, launches = graph_time_us(call, args.steps, args.warmup)
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize()
+        with ClockSampler(local) as clocks:
+            time.sleep(0.25)
+            t_call = time_graph(g, args.steps, reps=max(1, args.reps))
+        t_call = barrier_max(t_call, world)
+        del g
+
+        # per-kernel times of the path the call took (same rotation, same stream), for the roofline
+        kernels = {}
+        if mode == 'fused':
+            kernels['fused'] = t_call
+        else:
+            hm = [_native.value_proj(pool[j][0], W, bias, H, head_major=True) for j in range(len(pool))]
+            gp, _ = graph_time_us(lambda i: _native.value_proj(pool[i % len(pool)][0], W, bias, H, head_major=True),
+                                  args.steps, args.warmup)
+            kernels['proj'] = time_graph(gp, args.steps, reps=max(1, args.reps))
+            del gp
+            gs, _ = graph_time_us(lambda i: _native.sample_head_major(hm[i % len(pool)], shapes, starts,
+                                                                      pool[i % len(pool)][1], pool[i % len(pool)][2]),
+                                  args.steps, args.warmup)
+            kernels['sample'] = time_graph(gs, args.steps, reps=max(1, args.reps))
+            del gs, hm
+        top = max(kernels, key=kernels.get)
+        hbm, peak_kind = peaks()
+        alg = kernel_bytes(top, B, Q, N, C, H, D, L, P, e, bias is not None)
+        achieved = alg / (kernels[top] * 1e-6) / 1e9
+
+        # hot-L2 time (upstream's method: one input set replayed)
+        gh, _ = graph_time_us(lambda i: ma_deform_attn(base[0], W, bias, shapes, starts, base[5], base[6],
+                                                       mode=args.mode), args.steps, args.warmup)
+        t_hot = barrier_max(time_graph(gh, args.steps, reps=3), world)
+        del gh
+
+        # end to end through the public API: pinned host inputs copied in, result copied out, every step
+        host = [t.cpu().pin_memory() for t in (base[0], W, bias, shapes, starts, base[5], base[6]) if t is not None]
+        h2d = sum(t.numel() * t.element_size() for t in host)
+        out_host = torch.empty((B, Q, H * D), dtype=base[0].dtype).pin_memory()
+        d2h = out_host.numel() * out_host.element_size()
+        e2e_steps = max(10, min(args.steps, 200))
+
+        def e2e_step():
+            dev_in = [t.to(dev, non_blocking=True) for t in host]
+            if bias is None:
+                dev_in.insert(2, None)
+            out = ma_deform_attn(*dev_in, mode=args.mode)
+            out_host.copy_(out, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(e2e_steps):
+            e2e_step()
+        end.record()
+        end.synchronize()
+        t_e2e = barrier_max(start.elapsed_time(end) * 1e3 / e2e_steps, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        us, threads, n = cpu_time_us(args.config)
+        cpu = {'value': round(us, 2), 'unit': 'us', 'cores': threads, 'kind': 'port',
+               'sample': f'{n} calls of {args.config} (B=1) on torch CPU ops (oracle torch_port), median'}
+    if rank == 0:
+        line = {
+            'metric': METRIC, 'value': round(t_call, 3), 'unit': 'us', 'n_gpus': world, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': round(t_call / 1e3, 6), 'higher_is_better': False,
+            'scaling': 'weak', 'vs_baseline': None, 'dtype': str(cfg['dtype']).replace('torch.', ''),
+            'data': 'synthetic (seeded, BASELINE config shapes)', 'config': config_dict(args.config, world, mode),
+            'mode': mode, 'queries_per_s': round(B * Q * world / (t_call * 1e-6), 1),
+            'hot_l2_us': round(t_hot, 3), 'kernel_us': {k: round(v, 3) for k, v in kernels.items()},
+            'roofline': {'bound': 'hbm', 'kernel': top, 'achieved': round(achieved, 1), 'peak': hbm,
+                         'unit': 'GB/s', 'frac': round(achieved / hbm, 4), 'peak_source': peak_kind,
+                         'algorithmic_bytes': alg, 'traffic': committed_traffic(top, args.config)},
+            'cpu_baseline': cpu,
+            'e2e': {'value': round(t_e2e, 2), 'unit': 'us', 'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h},
+            'gpu_launches': launches,
+            'clocks': clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_sweep(args):
+    """Fused vs project over upstream's sweep grid (bench/results/rtx4090.md) and the c5 grid; prints a table."""
+    torch.cuda.set_device(0)
+    _native.load()
+    rows = []
+    grids = [('c1', dtype, B, Q) for dtype in args.dtype for B in (1, 4, 8) for Q in (50, 100, 200, 300, 600, 900)]
+    grids += [('c5', dtype, B, Q) for dtype in args.dtype for B in workloads.C5_BATCHES for Q in workloads.C5_QUERIES]
+    grids += [('c4', dtype, B, Q) for dtype in args.dtype for B in (1, 8) for Q in (300, 900)]
+    with torch.inference_mode():
+        for cfg, dname, B, Q in grids:
+            dtype = getattr(torch, dname)
+            a = workloads.make_inputs(cfg, seed=0, B=B, Q=Q, dtype=dtype, device='cuda')
+            t = {}
+            for mode in ('fused', 'project'):
+                g, _ = graph_time_us(lambda i, m=mode: ma_deform_attn(*a, mode=m), 50, 3)
+                t[mode] = time_graph(g, 50, reps=5)
+                del g
+            pick = choose_mode(a[0], a[1], a[5])
+            c = workloads.CONFIGS[cfg]
+            N, L, P, D = a[0].shape[1], len(c['levels']), c['P'], c['D']
+            ratio = Q * L * P * 4 / (N * D)
+            row = {'config': cfg, 'dtype': dname, 'B': B, 'Q': Q, 'ratio': ratio, 'fused_us': t['fused'],
+                   'project_us': t['project'], 'auto': pick, 'auto_us': t[pick],
+                   'best': min(t, key=t.get), 'auto_within_10pct': t[pick] <= 1.1 * min(t.values())}
+            rows.append(row)
+            print(json.dumps(row), flush=True)
+            del a
+            torch.cuda.empty_cache()
+    ok = sum(r['auto_within_10pct'] for r in rows)
+    print(json.dumps({'sweep_cases': len(rows), 'auto_within_10pct': ok}), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=200)
+    ap.add_argument('--warmup', type=int, default=5)
+    ap.add_argument('--reps', type=int, default=5)
+    ap.add_argument('--config', default='c1h', choices=sorted(workloads.CONFIGS))
+    ap.add_argument('--mode', default='auto', choices=('auto', 'fused', 'project'))
+    ap.add_argument('--impl', default='ours', choices=('ours', 'reference'))
+    ap.add_argument('--no-cpu', action='store_true')
+    ap.add_argument('--sweep', action='store_true')
+    ap.add_argument('--dtype', nargs='+', default=['float16', 'bfloat16', 'float32'])
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == 'reference':
+        run_reference_arm(args)
+    elif args.sweep:
+        run_sweep(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == '__main__':
+    main()

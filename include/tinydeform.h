@@ -1,0 +1,126 @@
+/*
+ * tinydeform.h -- C ABI of the B200 (sm_100a) ma_deform_attn library (libtinydeform / _tinydeform.so).
+ *
+ * The library computes value projection + multi-scale deformable attention for DETR-style decoders:
+ *
+ *   value[b, n, :]      = memory[b, n, :] @ value_weight^T + value_bias          ([B, N, H*D])
+ *   out[b, q, h*D + d]  = sum over levels l, points p, bilinear corners k of
+ *                         attention_weights[b,q,h,l,p] * bilinear_k * value[b, token_k, h*D + d]
+ *
+ * with bilinear sampling at (x*w_l - 0.5, y*h_l - 0.5) (grid_sample, align_corners=False) and zero padding:
+ * corners outside a level's map contribute nothing.
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor pointers are DEVICE pointers on the current CUDA device, dense row-major (contiguous).
+ *   - spatial_shapes is int64 [L, 2] (height, width); level_start_index is int64 [L]. Both stay on the device and
+ *     are read by the kernels, so a call never synchronises with the host and can be captured in a CUDA graph.
+ *   - dtype is one of TD_F32, TD_F16, TD_BF16, TD_F64; every float tensor of a call has that dtype. Accumulation
+ *     is float32 (float64 for TD_F64).
+ *   - stream is a cudaStream_t (NULL = legacy default stream). Kernels are queued on it; nothing is synchronised.
+ *   - Return 0 (TD_OK) on success. Otherwise a TD_ERR_* code and, when err is not NULL, a NUL-terminated message
+ *     in err[0 .. err_len). Argument errors are detected before any launch; launch errors are read with
+ *     cudaGetLastError before returning.
+ *   - No entry point allocates device memory. td_project_forward takes a caller-provided workspace.
+ */
+#ifndef TINYDEFORM_H_
+#define TINYDEFORM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TD_API __attribute__((visibility("default")))
+#else
+#define TD_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum td_dtype { TD_F32 = 0, TD_F16 = 1, TD_BF16 = 2, TD_F64 = 3 };
+
+enum td_status {
+    TD_OK = 0,
+    TD_ERR_ARG = 1,         /* a size, pointer or dtype violates the contract; nothing was launched */
+    TD_ERR_CUDA = 2,        /* a CUDA runtime call or kernel launch failed */
+    TD_ERR_WORKSPACE = 3    /* the workspace is NULL or smaller than td_project_workspace_bytes() */
+};
+
+/* Limits of the operator contract (upstream csrc/ma_deform_fused.cu:27-28 and :241,:264). */
+#define TD_MAX_LEVEL_POINTS 64   /* L * P per head */
+#define TD_MAX_CHANNELS 8192     /* C for the fused order */
+
+/*
+ * Fused order: gather the bilinear corners of full C-wide memory rows per (batch, query, head), then project the
+ * weighted sum with that head's value_weight rows, plus value_bias * (sum of in-map corner weights).
+ * Replaces upstream fused_forward (csrc/ma_deform_fused.cu:291-325), called from
+ * marearts_tinydeform/__init__.py:74-76.
+ *   memory [B, N, C]; value_weight [HD, C]; value_bias [HD] or NULL; sampling_locations [B, Q, H, L, P, 2];
+ *   attention_weights [B, Q, H, L, P]; out [B, Q, HD] (written).  HD % H == 0, D = HD / H.
+ */
+TD_API int td_fused_forward(int dtype, const void* memory, const void* value_weight, const void* value_bias,
+                     const int64_t* spatial_shapes, const int64_t* level_start_index,
+                     const void* sampling_locations, const void* attention_weights, void* out,
+                     int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H, int64_t HD, int64_t L, int64_t P,
+                     void* stream, char* err, size_t err_len);
+
+/*
+ * Project order, sampling half: sample an already projected value [B, N, HD] (bias included).
+ * Replaces upstream sample_forward (csrc/ma_deform_fused.cu:327-350), called from
+ * marearts_tinydeform/__init__.py:78-79.  heads must equal H.
+ */
+TD_API int td_sample_forward(int dtype, const void* value, int64_t heads, const int64_t* spatial_shapes,
+                      const int64_t* level_start_index, const void* sampling_locations,
+                      const void* attention_weights, void* out,
+                      int64_t B, int64_t Q, int64_t N, int64_t HD, int64_t H, int64_t L, int64_t P,
+                      void* stream, char* err, size_t err_len);
+
+/*
+ * Project order, projection half: value = memory @ value_weight^T + value_bias, written either as [B, N, HD]
+ * (head_major = 0, the nn.Linear layout) or head-major [B, H, N, D] (head_major = 1, the layout the sampler of
+ * td_project_forward reads). Replaces the F.linear call of upstream marearts_tinydeform/__init__.py:77.
+ */
+TD_API int td_value_proj(int dtype, const void* memory, const void* value_weight, const void* value_bias, void* value,
+                  int64_t B, int64_t N, int64_t C, int64_t H, int64_t HD, int head_major,
+                  void* stream, char* err, size_t err_len);
+
+/*
+ * Sampling of a projected value at explicit element strides: value element (b, token, head, d) is at
+ * b * s_img + token * s_tok + head * s_head + d. td_sample_forward is the case (N*HD, HD, D); the head-major value
+ * td_project_forward samples is (H*N*D, D, N*D). Generalises upstream sample_forward
+ * (csrc/ma_deform_fused.cu:327-350) so each half of the project order can be run and timed on its own.
+ */
+TD_API int td_sample_strided(int dtype, const void* value, int64_t s_img, int64_t s_tok, int64_t s_head,
+                             const int64_t* spatial_shapes, const int64_t* level_start_index,
+                             const void* sampling_locations, const void* attention_weights, void* out,
+                             int64_t B, int64_t Q, int64_t N, int64_t H, int64_t D, int64_t L, int64_t P,
+                             void* stream, char* err, size_t err_len);
+
+/* Bytes of device workspace td_project_forward needs (the projected value, head-major, plus alignment slack). */
+TD_API size_t td_project_workspace_bytes(int dtype, int64_t B, int64_t N, int64_t HD);
+
+/*
+ * Project order, whole: td_value_proj (head-major) into the workspace, then the per-head sampler on it.
+ * Replaces upstream marearts_tinydeform/__init__.py:77-79 (F.linear + _C.sample_forward).
+ */
+TD_API int td_project_forward(int dtype, const void* memory, const void* value_weight, const void* value_bias,
+                       const int64_t* spatial_shapes, const int64_t* level_start_index,
+                       const void* sampling_locations, const void* attention_weights, void* out,
+                       int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H, int64_t HD, int64_t L, int64_t P,
+                       void* workspace, size_t workspace_bytes, void* stream, char* err, size_t err_len);
+
+/* Device facts used by the auto picker and the bench: SM count and compute capability of `device`. */
+TD_API int td_device_info(int device, int* sm_count, int* cc_major, int* cc_minor, char* err, size_t err_len);
+
+/* Number of kernels this library has queued since it was loaded (host-side counter; graph replays not counted). */
+TD_API uint64_t td_launch_count(void);
+
+/* Library version string, e.g. "0.1.1+b200". */
+TD_API const char* td_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TINYDEFORM_H_ */

@@ -1,0 +1,248 @@
+"""ctypes binding of the C ABI in include/tinydeform.h, plus the tensor-level argument contract.
+
+The checks here raise ``RuntimeError`` under the same conditions as upstream's TORCH_CHECKs
+(``csrc/ma_deform_fused.cu:236-266, :298-308, :333``); the library repeats the size checks and returns a status
+that is turned into ``RuntimeError`` as well. Tensors are made contiguous (a device copy only when they are not),
+the output is allocated from torch's caching allocator, and kernels run on torch's current stream of the memory's
+device, so calls are stream-ordered and can be captured in CUDA graphs.
+"""
+
+import ctypes
+import os
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, '_tinydeform.so')
+
+TD_F32, TD_F16, TD_BF16, TD_F64 = 0, 1, 2, 3
+DTYPE_CODE = {torch.float32: TD_F32, torch.float16: TD_F16, torch.bfloat16: TD_BF16, torch.float64: TD_F64}
+MAX_LEVEL_POINTS = 64
+MAX_CHANNELS = 8192
+INT32_MAX = 2 ** 31 - 1
+
+# exported symbol -> (restype, argtypes); the list is also what tests check the .so against
+_i64, _vp, _ip, _sz, _cp = ctypes.c_int64, ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.c_char_p
+SIGNATURES = {
+    'td_fused_forward': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                               _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _cp, _sz]),
+    'td_sample_forward': (_ip, [_ip, _vp, _i64, _vp, _vp, _vp, _vp, _vp,
+                                _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _cp, _sz]),
+    'td_sample_strided': (_ip, [_ip, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp,
+                                _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _cp, _sz]),
+    'td_value_proj': (_ip, [_ip, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _ip, _vp, _cp, _sz]),
+    'td_project_workspace_bytes': (_sz, [_ip, _i64, _i64, _i64]),
+    'td_project_forward': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                 _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp, _cp, _sz]),
+    'td_device_info': (_ip, [_ip, ctypes.POINTER(_ip), ctypes.POINTER(_ip), ctypes.POINTER(_ip), _cp, _sz]),
+    'td_launch_count': (ctypes.c_uint64, []),
+    'td_version': (ctypes.c_char_p, []),
+}
+
+_lib = None
+_load_error = None
+
+
+def load(path=LIB_PATH):
+    """Load the library (once) and declare every signature. Raises RuntimeError when it is missing."""
+    global _lib, _load_error
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        _load_error = f'{path} is not built (run python -m marearts_tinydeform_b200.build)'
+        raise RuntimeError('marearts-tinydeform-b200 was installed without its CUDA library: ' + _load_error)
+    try:
+        lib = ctypes.CDLL(path)
+    except OSError as exc:
+        _load_error = str(exc)
+        raise RuntimeError('marearts-tinydeform-b200 could not load its CUDA library: ' + _load_error) from exc
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def available():
+    try:
+        load()
+        return True
+    except RuntimeError:
+        return False
+
+
+def _call(fn, *args):
+    err = ctypes.create_string_buffer(512)
+    rc = fn(*args, err, ctypes.sizeof(err))
+    if rc != 0:
+        raise RuntimeError(f'{fn.__name__} failed ({rc}): {err.value.decode(errors="replace")}')
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def check_geometry(ref, spatial_shapes, level_start_index, sampling_locations, attention_weights):
+    """Upstream check_geometry (csrc/ma_deform_fused.cu:236-266); returns B, Q, H, L, P."""
+    if not ref.is_cuda:
+        raise RuntimeError('inputs must be CUDA tensors')
+    if ref.dim() != 3:
+        raise RuntimeError('memory / value must be [B, N, C]')
+    if ref.size(1) > INT32_MAX:
+        raise RuntimeError('too many memory tokens')
+    if sampling_locations.dim() != 6 or sampling_locations.size(5) != 2:
+        raise RuntimeError('sampling_locations must be [B, Q, H, L, P, 2]')
+    if attention_weights.dim() != 5:
+        raise RuntimeError('attention_weights must be [B, Q, H, L, P]')
+    if tuple(attention_weights.shape) != tuple(sampling_locations.shape[:5]):
+        raise RuntimeError('attention_weights must be [B, Q, H, L, P] like sampling_locations')
+    B, Q, H, L, P = sampling_locations.shape[:5]
+    if ref.size(0) != B:
+        raise RuntimeError('batch size mismatch')
+    if H <= 0:
+        raise RuntimeError('need at least one head')
+    if L * P > MAX_LEVEL_POINTS:
+        raise RuntimeError(f'levels x points must be <= {MAX_LEVEL_POINTS}')
+    if spatial_shapes.dtype != torch.long or spatial_shapes.dim() != 2 or spatial_shapes.size(0) != L \
+            or spatial_shapes.size(1) != 2:
+        raise RuntimeError('spatial_shapes must be int64 [L, 2]')
+    if level_start_index.dtype != torch.long or level_start_index.dim() != 1 or level_start_index.size(0) != L:
+        raise RuntimeError('level_start_index must be int64 [L]')
+    for t in (sampling_locations, attention_weights, spatial_shapes, level_start_index):
+        if t.device != ref.device:
+            raise RuntimeError('all tensors must be on the same device')
+    for t in (sampling_locations, attention_weights):
+        if t.dtype != ref.dtype:
+            raise RuntimeError('all float tensors must have the same dtype')
+    if ref.dtype not in DTYPE_CODE:
+        raise RuntimeError(f'unsupported dtype {ref.dtype}')
+    if B * Q * H > INT32_MAX:
+        raise RuntimeError('too many (batch, query, head) rows')
+    return B, Q, H, L, P
+
+
+def check_projection(memory, value_weight, value_bias, heads):
+    """Upstream weight / bias checks (csrc/ma_deform_fused.cu:297-308); returns HD."""
+    C = memory.size(2)
+    if value_weight.dim() != 2 or value_weight.size(1) != C:
+        raise RuntimeError('value_weight must be [H * D, C] with C = memory.size(2)')
+    HD = value_weight.size(0)
+    if HD % heads != 0:
+        raise RuntimeError('value_weight rows must be a multiple of the head count')
+    if value_weight.device != memory.device or value_weight.dtype != memory.dtype:
+        raise RuntimeError('value_weight must have the device and dtype of memory')
+    if value_bias is not None and (value_bias.device != memory.device or value_bias.dtype != memory.dtype
+                                   or value_bias.dim() != 1 or value_bias.size(0) != HD):
+        raise RuntimeError('value_bias must be [H * D] like value_weight, same device and dtype')
+    return HD
+
+
+def _dense(*ts):
+    return [None if t is None else t.contiguous() for t in ts]
+
+
+def fused_forward(memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                  sampling_locations, attention_weights):
+    """Fused order (upstream _C.fused_forward, csrc/ma_deform_fused.cu:291-325) through td_fused_forward."""
+    lib = load()
+    B, Q, H, L, P = check_geometry(memory, spatial_shapes, level_start_index, sampling_locations, attention_weights)
+    HD = check_projection(memory, value_weight, value_bias, H)
+    N, C = memory.size(1), memory.size(2)
+    if C > MAX_CHANNELS:
+        raise RuntimeError(f'channels must be <= {MAX_CHANNELS}')
+    mem, w, b, shp, st, loc, att = _dense(memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                                          sampling_locations, attention_weights)
+    out = torch.empty((B, Q, HD), dtype=memory.dtype, device=memory.device)
+    if B * Q == 0:
+        return out
+    with torch.cuda.device(memory.device):
+        _call(lib.td_fused_forward, DTYPE_CODE[memory.dtype], _ptr(mem), _ptr(w), _ptr(b), _ptr(shp), _ptr(st),
+              _ptr(loc), _ptr(att), _ptr(out), B, Q, N, C, H, HD, L, P, _stream(memory.device))
+    return out
+
+
+def project_forward(memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                    sampling_locations, attention_weights):
+    """Project order (upstream __init__.py:77-79: F.linear + _C.sample_forward) through td_project_forward."""
+    lib = load()
+    B, Q, H, L, P = check_geometry(memory, spatial_shapes, level_start_index, sampling_locations, attention_weights)
+    HD = check_projection(memory, value_weight, value_bias, H)
+    N, C = memory.size(1), memory.size(2)
+    mem, w, b, shp, st, loc, att = _dense(memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                                          sampling_locations, attention_weights)
+    out = torch.empty((B, Q, HD), dtype=memory.dtype, device=memory.device)
+    if B * Q == 0:
+        return out
+    code = DTYPE_CODE[memory.dtype]
+    ws_bytes = lib.td_project_workspace_bytes(code, B, N, HD)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=memory.device)
+    with torch.cuda.device(memory.device):
+        _call(lib.td_project_forward, code, _ptr(mem), _ptr(w), _ptr(b), _ptr(shp), _ptr(st), _ptr(loc), _ptr(att),
+              _ptr(out), B, Q, N, C, H, HD, L, P, _ptr(ws), ws_bytes, _stream(memory.device))
+    return out
+
+
+def sample_forward(value, heads, spatial_shapes, level_start_index, sampling_locations, attention_weights):
+    """Sampling of a projected value [B, N, H*D] (upstream _C.sample_forward, csrc/ma_deform_fused.cu:327-350)."""
+    lib = load()
+    B, Q, H, L, P = check_geometry(value, spatial_shapes, level_start_index, sampling_locations, attention_weights)
+    N, HD = value.size(1), value.size(2)
+    if heads != H or HD % H != 0:
+        raise RuntimeError('value must be [B, N, H * D] with H = sampling_locations.size(2)')
+    v, shp, st, loc, att = _dense(value, spatial_shapes, level_start_index, sampling_locations, attention_weights)
+    out = torch.empty((B, Q, HD), dtype=value.dtype, device=value.device)
+    if B * Q == 0:
+        return out
+    with torch.cuda.device(value.device):
+        _call(lib.td_sample_forward, DTYPE_CODE[value.dtype], _ptr(v), heads, _ptr(shp), _ptr(st), _ptr(loc),
+              _ptr(att), _ptr(out), B, Q, N, HD, H, L, P, _stream(value.device))
+    return out
+
+
+def sample_head_major(value_hm, spatial_shapes, level_start_index, sampling_locations, attention_weights):
+    """Sampling of a head-major value [B, H, N, D] (the layout td_project_forward uses) via td_sample_strided."""
+    lib = load()
+    B, H, N, D = value_hm.shape
+    check_geometry(value_hm.view(B, H * N, D), spatial_shapes, level_start_index, sampling_locations,
+                   attention_weights)
+    Q = sampling_locations.size(1)
+    L, P = sampling_locations.shape[3:5]
+    v, shp, st, loc, att = _dense(value_hm, spatial_shapes, level_start_index, sampling_locations, attention_weights)
+    out = torch.empty((B, Q, H * D), dtype=value_hm.dtype, device=value_hm.device)
+    if B * Q == 0:
+        return out
+    with torch.cuda.device(value_hm.device):
+        _call(lib.td_sample_strided, DTYPE_CODE[v.dtype], _ptr(v), H * N * D, D, N * D, _ptr(shp), _ptr(st),
+              _ptr(loc), _ptr(att), _ptr(out), B, Q, N, H, D, L, P, _stream(v.device))
+    return out
+
+
+def value_proj(memory, value_weight, value_bias, heads, head_major=False):
+    """value = memory @ value_weight.T + value_bias as [B, N, HD], or head-major [B, H, N, D], via td_value_proj."""
+    lib = load()
+    if not memory.is_cuda or memory.dim() != 3:
+        raise RuntimeError('memory must be a CUDA [B, N, C] tensor')
+    HD = check_projection(memory, value_weight, value_bias, heads)
+    B, N, C = memory.shape
+    mem, w, b = _dense(memory, value_weight, value_bias)
+    shape = (B, heads, N, HD // heads) if head_major else (B, N, HD)
+    value = torch.empty(shape, dtype=memory.dtype, device=memory.device)
+    if B * N == 0:
+        return value
+    with torch.cuda.device(memory.device):
+        _call(lib.td_value_proj, DTYPE_CODE[memory.dtype], _ptr(mem), _ptr(w), _ptr(b), _ptr(value), B, N, C,
+              heads, HD, 1 if head_major else 0, _stream(memory.device))
+    return value
+
+
+def launch_count():
+    return int(load().td_launch_count())
+
+
+def version():
+    return load().td_version().decode()

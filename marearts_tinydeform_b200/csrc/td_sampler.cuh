@@ -1,0 +1,112 @@
+// td_sampler.cuh -- project order, sampling half: out[b,q,h,:] = sum_s w_s * value[b, tok_s, h, :].
+//
+// Same result as upstream sample_kernel (csrc/ma_deform_fused.cu:212-233), laid out for B200:
+//   * one warp per (batch, query, head) row; the row's levels x points x 4 corners are computed once, by lanes in
+//     parallel, into shared memory;
+//   * the head slice of a corner row (D * e bytes) is read as G 16-byte vectors by G lanes, so one warp keeps 32/G
+//     corner rows in flight at a time, and the corner groups are summed with xor shuffles at the end;
+//   * value is addressed through (image, token, head) strides, so the same kernel reads the nn.Linear layout
+//     [B, N, H*D] and the head-major [B, H, N, D] layout the projection kernel writes (x-adjacent corners are then
+//     adjacent D-rows in memory).
+// The generic kernel (any D, alignment or dtype, float64 included) keeps upstream's lanes-over-D mapping.
+#pragma once
+
+#include "td_common.cuh"
+
+namespace td {
+
+template <typename T>
+struct SampleArgs {
+    const T* value;
+    const T* loc;
+    const T* attn;
+    T* out;
+    const int64_t* shapes;
+    const int64_t* starts;
+    long long rows;                 // B * Q * H
+    long long s_img, s_tok, s_head; // value strides in elements
+    long long n_tok;                // N
+    int Q, H, D, L, P;
+    int G;                          // lanes per corner row = D * sizeof(T) / 16 (vector kernel only)
+};
+
+constexpr int kSampleWarps = 8;
+
+// Vector kernel: needs D * sizeof(T) % 16 == 0, D * sizeof(T) <= 512, 16-byte aligned value/out and strides.
+template <typename T>
+__global__ void __launch_bounds__(kSampleWarps * 32) sample_vec_kernel(const SampleArgs<T> a) {
+    using A = typename Elem<T>::acc;
+    using CT = typename Coord<T>::type;
+    constexpr int V = Elem<T>::kVec;
+    __shared__ Level lv[kMaxLevels];
+    __shared__ int s_tok[kSampleWarps][kMaxCorners];
+    __shared__ CT s_wt[kSampleWarps][kMaxCorners];
+    load_levels(a.shapes, a.starts, a.L, lv);
+    __syncthreads();
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long row = (long long)blockIdx.x * kSampleWarps + warp;
+    if (row >= a.rows) return;  // whole warp leaves; only warp-level syncs follow
+    const int LP = a.L * a.P, S = 4 * LP;
+    for (int j = lane; j < LP; j += 32)
+        row_corners(a.loc, a.attn, lv, LP, a.P, a.n_tok, row, j, &s_tok[warp][4 * j], &s_wt[warp][4 * j]);
+    __syncwarp();
+
+    const int h = int(row % a.H);
+    const long long b = row / ((long long)a.Q * a.H);
+    const T* vb = a.value + b * a.s_img + (long long)h * a.s_head;
+    const int G = a.G, CG = 32 / G, cg = lane / G, v = lane - cg * G;
+    A acc[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) acc[i] = A(0);
+#pragma unroll 4
+    for (int s = cg; s < S; s += CG) {
+        const int t = s_tok[warp][s];
+        if (t >= 0) {
+            A x[V];
+            load16<T>(vb + (long long)t * a.s_tok + v * V, x);
+            const A w = A(s_wt[warp][s]);
+#pragma unroll
+            for (int i = 0; i < V; ++i) acc[i] = fma(w, x[i], acc[i]);
+        }
+    }
+    for (int o = G; o < 32; o <<= 1) {
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+    }
+    if (cg == 0) store16<T>(a.out + row * a.D + v * V, acc);
+}
+
+// Generic kernel: lanes over the head's D channels, scalar loads.
+template <typename T>
+__global__ void __launch_bounds__(kSampleWarps * 32) sample_generic_kernel(const SampleArgs<T> a) {
+    using A = typename Elem<T>::acc;
+    using CT = typename Coord<T>::type;
+    __shared__ Level lv[kMaxLevels];
+    __shared__ int s_tok[kSampleWarps][kMaxCorners];
+    __shared__ CT s_wt[kSampleWarps][kMaxCorners];
+    load_levels(a.shapes, a.starts, a.L, lv);
+    __syncthreads();
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long row = (long long)blockIdx.x * kSampleWarps + warp;
+    if (row >= a.rows) return;
+    const int LP = a.L * a.P, S = 4 * LP;
+    for (int j = lane; j < LP; j += 32)
+        row_corners(a.loc, a.attn, lv, LP, a.P, a.n_tok, row, j, &s_tok[warp][4 * j], &s_wt[warp][4 * j]);
+    __syncwarp();
+
+    const int h = int(row % a.H);
+    const long long b = row / ((long long)a.Q * a.H);
+    const T* vb = a.value + b * a.s_img + (long long)h * a.s_head;
+    for (int d = lane; d < a.D; d += 32) {
+        A acc = A(0);
+        for (int s = 0; s < S; ++s) {
+            const int t = s_tok[warp][s];
+            if (t >= 0) acc = fma(A(s_wt[warp][s]), to_acc(vb[(long long)t * a.s_tok + d]), acc);
+        }
+        a.out[row * a.D + d] = from_acc<T>(acc);
+    }
+}
+
+}  // namespace td

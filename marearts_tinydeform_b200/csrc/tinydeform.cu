@@ -1,0 +1,323 @@
+// tinydeform.cu -- the C ABI (include/tinydeform.h): argument contract, kernel choice and launches.
+//
+// The argument contract mirrors upstream's check_geometry and weight/bias checks (csrc/ma_deform_fused.cu:235-266,
+// :298-308, :333): levels x points <= 64, C <= 8192, N and B*Q*H within int32, HD a multiple of H. Tensor-level
+// checks (ranks, dtypes, devices) live in the Python mirror, which only ever passes dense device pointers here.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+#include "../../include/tinydeform.h"
+#include "td_common.cuh"
+#include "td_fused_simt.cuh"
+#include "td_gemm_simt.cuh"
+#include "td_sampler.cuh"
+
+namespace td {
+namespace {
+
+std::atomic<uint64_t> g_launches{0};
+
+int fail(char* err, size_t err_len, int code, const char* fmt, ...) {
+    if (err != nullptr && err_len > 0) {
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(err, err_len, fmt, ap);
+        va_end(ap);
+    }
+    return code;
+}
+
+int check_launch(char* err, size_t err_len, const char* what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    return TD_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+size_t dtype_size(int dtype) {
+    switch (dtype) {
+        case TD_F32: return 4;
+        case TD_F16: return 2;
+        case TD_BF16: return 2;
+        case TD_F64: return 8;
+        default: return 0;
+    }
+}
+
+// Per-device facts, read once per device (the first call on a device should come before any graph capture,
+// although every call made here is also legal during capture).
+struct DeviceFacts {
+    int sm_count = 0, major = 0, minor = 0, smem_optin = 0;
+};
+
+constexpr int kMaxDevices = 64;
+std::once_flag g_dev_once[kMaxDevices];
+DeviceFacts g_dev[kMaxDevices];
+
+int device_facts(DeviceFacts* out, char* err, size_t err_len) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices) return fail(err, err_len, TD_ERR_CUDA, "device index %d out of range", dev);
+    std::call_once(g_dev_once[dev], [dev] {
+        DeviceFacts f;
+        cudaDeviceGetAttribute(&f.sm_count, cudaDevAttrMultiProcessorCount, dev);
+        cudaDeviceGetAttribute(&f.major, cudaDevAttrComputeCapabilityMajor, dev);
+        cudaDeviceGetAttribute(&f.minor, cudaDevAttrComputeCapabilityMinor, dev);
+        cudaDeviceGetAttribute(&f.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        g_dev[dev] = f;
+    });
+    *out = g_dev[dev];
+    if (out->sm_count <= 0) return fail(err, err_len, TD_ERR_CUDA, "could not query device %d", dev);
+    return TD_OK;
+}
+
+// Shared geometry checks (upstream check_geometry, csrc/ma_deform_fused.cu:236-266).
+int check_geometry(int64_t B, int64_t Q, int64_t N, int64_t H, int64_t L, int64_t P, char* err, size_t err_len) {
+    if (B < 0 || Q < 0 || N < 0 || L < 0 || P < 0)
+        return fail(err, err_len, TD_ERR_ARG, "sizes must be non-negative");
+    if (N > INT32_MAX) return fail(err, err_len, TD_ERR_ARG, "too many memory tokens");
+    if (H <= 0) return fail(err, err_len, TD_ERR_ARG, "need at least one head");
+    if (L > kMaxLevels || L * P > TD_MAX_LEVEL_POINTS)
+        return fail(err, err_len, TD_ERR_ARG, "levels x points must be <= %d", TD_MAX_LEVEL_POINTS);
+    if (double(B) * double(Q) * double(H) > double(INT32_MAX))
+        return fail(err, err_len, TD_ERR_ARG, "too many (batch, query, head) rows");
+    return TD_OK;
+}
+
+template <typename T>
+int launch_sampler(const T* value, long long s_img, long long s_tok, long long s_head, const int64_t* shapes,
+                   const int64_t* starts, const T* loc, const T* attn, T* out, int64_t B, int64_t Q, int64_t N,
+                   int64_t H, int64_t D, int64_t L, int64_t P, cudaStream_t stream, char* err, size_t err_len) {
+    SampleArgs<T> a;
+    a.value = value; a.loc = loc; a.attn = attn; a.out = out; a.shapes = shapes; a.starts = starts;
+    a.rows = B * Q * H; a.s_img = s_img; a.s_tok = s_tok; a.s_head = s_head; a.n_tok = N;
+    a.Q = int(Q); a.H = int(H); a.D = int(D); a.L = int(L); a.P = int(P);
+    const long long row_bytes = D * (long long)sizeof(T);
+    a.G = int(row_bytes / 16);
+    // the corner groups of a warp are summed with an xor butterfly, so G must be a power of two dividing 32
+    const bool vec = row_bytes % 16 == 0 && row_bytes <= 512 && (a.G & (a.G - 1)) == 0 && aligned16(value) &&
+                     aligned16(out) &&
+                     (s_img * (long long)sizeof(T)) % 16 == 0 && (s_tok * (long long)sizeof(T)) % 16 == 0 &&
+                     (s_head * (long long)sizeof(T)) % 16 == 0;
+    const unsigned grid = unsigned((a.rows + kSampleWarps - 1) / kSampleWarps);
+    if (vec) {
+        sample_vec_kernel<T><<<grid, kSampleWarps * 32, 0, stream>>>(a);
+    } else {
+        sample_generic_kernel<T><<<grid, kSampleWarps * 32, 0, stream>>>(a);
+    }
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return check_launch(err, err_len, vec ? "sample_vec_kernel" : "sample_generic_kernel");
+}
+
+template <typename T>
+int launch_fused(const T* memory, const T* weight, const T* bias, const int64_t* shapes, const int64_t* starts,
+                 const T* loc, const T* attn, T* out, int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H,
+                 int64_t D, int64_t L, int64_t P, cudaStream_t stream, char* err, size_t err_len) {
+    using A = typename Elem<T>::acc;
+    DeviceFacts f;
+    if (int rc = device_facts(&f, err, err_len)) return rc;
+    const int S = int(4 * L * P);
+    // rows per CTA: up to 16 queries of one (batch, head), fewer when that leaves SMs idle or m does not fit
+    int R = kFusedMaxRows;
+    while (R > 1 && B * H * ((Q + R - 1) / R) < 2LL * f.sm_count) R >>= 1;
+    const size_t smem_cap = size_t(f.smem_optin) - 2048;
+    while (R > 1 && fused_simt_smem<T>(R, int(C), S) > smem_cap) R >>= 1;
+    const size_t smem = fused_simt_smem<T>(R, int(C), S);
+    if (smem > smem_cap) return fail(err, err_len, TD_ERR_ARG, "channels too large for shared memory");
+    FusedArgs<T> a;
+    a.memory = memory; a.weight = weight; a.bias = bias; a.loc = loc; a.attn = attn; a.out = out;
+    a.shapes = shapes; a.starts = starts; a.n_tok = N;
+    a.B = int(B); a.Q = int(Q); a.C = int(C); a.H = int(H); a.D = int(D); a.L = int(L); a.P = int(P);
+    a.R = R; a.q_tiles = int((Q + R - 1) / R);
+    a.vec = (C % Elem<T>::kVec == 0) && aligned16(memory);
+    (void)sizeof(A);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(fused_simt_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             int(smem));
+        if (e != cudaSuccess)
+            return fail(err, err_len, TD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    }
+    const long long grid = B * H * (long long)a.q_tiles;
+    fused_simt_kernel<T><<<unsigned(grid), kFusedThreads, smem, stream>>>(a);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return check_launch(err, err_len, "fused_simt_kernel");
+}
+
+template <typename T>
+int launch_proj(const T* memory, const T* weight, const T* bias, T* value, int64_t B, int64_t N, int64_t C,
+                int64_t H, int64_t HD, int head_major, cudaStream_t stream, char* err, size_t err_len) {
+    ProjArgs<T> a;
+    a.memory = memory; a.weight = weight; a.bias = bias; a.value = value;
+    a.M = B * N; a.n_tok = N; a.C = int(C); a.HD = int(HD); a.H = int(H); a.D = int(HD / H);
+    a.head_major = head_major;
+    const dim3 grid(unsigned((a.M + kGemmBM - 1) / kGemmBM), unsigned((HD + kGemmBN - 1) / kGemmBN));
+    proj_simt_kernel<T><<<grid, kGemmThreads, 0, stream>>>(a);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return check_launch(err, err_len, "proj_simt_kernel");
+}
+
+template <typename F>
+int dispatch(int dtype, F&& f) {
+    switch (dtype) {
+        case TD_F32: return f(float{});
+        case TD_F16: return f(__half{});
+        case TD_BF16: return f(__nv_bfloat16{});
+        case TD_F64: return f(double{});
+        default: return -1;
+    }
+}
+
+}  // namespace
+}  // namespace td
+
+using namespace td;
+
+extern "C" {
+
+int td_fused_forward(int dtype, const void* memory, const void* value_weight, const void* value_bias,
+                     const int64_t* spatial_shapes, const int64_t* level_start_index,
+                     const void* sampling_locations, const void* attention_weights, void* out,
+                     int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H, int64_t HD, int64_t L, int64_t P,
+                     void* stream, char* err, size_t err_len) {
+    if (dtype_size(dtype) == 0) return fail(err, err_len, TD_ERR_ARG, "unsupported dtype code %d", dtype);
+    if (int rc = check_geometry(B, Q, N, H, L, P, err, err_len)) return rc;
+    if (C <= 0 || HD <= 0) return fail(err, err_len, TD_ERR_ARG, "channels and value_weight rows must be positive");
+    if (HD % H != 0) return fail(err, err_len, TD_ERR_ARG, "value_weight rows must be a multiple of the head count");
+    if (C > TD_MAX_CHANNELS) return fail(err, err_len, TD_ERR_ARG, "channels must be <= %d", TD_MAX_CHANNELS);
+    if (B * Q == 0) return TD_OK;
+    if (!memory || !value_weight || !sampling_locations || !attention_weights || !out ||
+        (L * P > 0 && (!spatial_shapes || !level_start_index)))
+        return fail(err, err_len, TD_ERR_ARG, "null tensor pointer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t D = HD / H;
+    return dispatch(dtype, [&](auto tag) {
+        using T = decltype(tag);
+        return launch_fused<T>(static_cast<const T*>(memory), static_cast<const T*>(value_weight),
+                               static_cast<const T*>(value_bias), spatial_shapes, level_start_index,
+                               static_cast<const T*>(sampling_locations), static_cast<const T*>(attention_weights),
+                               static_cast<T*>(out), B, Q, N, C, H, D, L, P, s, err, err_len);
+    });
+}
+
+int td_sample_forward(int dtype, const void* value, int64_t heads, const int64_t* spatial_shapes,
+                      const int64_t* level_start_index, const void* sampling_locations,
+                      const void* attention_weights, void* out,
+                      int64_t B, int64_t Q, int64_t N, int64_t HD, int64_t H, int64_t L, int64_t P,
+                      void* stream, char* err, size_t err_len) {
+    if (dtype_size(dtype) == 0) return fail(err, err_len, TD_ERR_ARG, "unsupported dtype code %d", dtype);
+    if (int rc = check_geometry(B, Q, N, H, L, P, err, err_len)) return rc;
+    if (heads != H || HD <= 0 || HD % H != 0)
+        return fail(err, err_len, TD_ERR_ARG, "value must be [B, N, H * D] with H = sampling_locations.size(2)");
+    if (B * Q == 0) return TD_OK;
+    if (!value || !sampling_locations || !attention_weights || !out ||
+        (L * P > 0 && (!spatial_shapes || !level_start_index)))
+        return fail(err, err_len, TD_ERR_ARG, "null tensor pointer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t D = HD / H;
+    return dispatch(dtype, [&](auto tag) {
+        using T = decltype(tag);
+        return launch_sampler<T>(static_cast<const T*>(value), N * HD, HD, D, spatial_shapes, level_start_index,
+                                 static_cast<const T*>(sampling_locations), static_cast<const T*>(attention_weights),
+                                 static_cast<T*>(out), B, Q, N, H, D, L, P, s, err, err_len);
+    });
+}
+
+int td_value_proj(int dtype, const void* memory, const void* value_weight, const void* value_bias, void* value,
+                  int64_t B, int64_t N, int64_t C, int64_t H, int64_t HD, int head_major,
+                  void* stream, char* err, size_t err_len) {
+    if (dtype_size(dtype) == 0) return fail(err, err_len, TD_ERR_ARG, "unsupported dtype code %d", dtype);
+    if (B < 0 || N < 0 || C <= 0 || H <= 0 || HD <= 0 || HD % H != 0)
+        return fail(err, err_len, TD_ERR_ARG, "value_proj needs B, N >= 0, C, H, HD > 0 and HD %% H == 0");
+    if (N > INT32_MAX || C > INT32_MAX || HD > INT32_MAX) return fail(err, err_len, TD_ERR_ARG, "size too large");
+    if (B * N == 0) return TD_OK;
+    if (!memory || !value_weight || !value) return fail(err, err_len, TD_ERR_ARG, "null tensor pointer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return dispatch(dtype, [&](auto tag) {
+        using T = decltype(tag);
+        return launch_proj<T>(static_cast<const T*>(memory), static_cast<const T*>(value_weight),
+                              static_cast<const T*>(value_bias), static_cast<T*>(value), B, N, C, H, HD,
+                              head_major ? 1 : 0, s, err, err_len);
+    });
+}
+
+int td_sample_strided(int dtype, const void* value, int64_t s_img, int64_t s_tok, int64_t s_head,
+                      const int64_t* spatial_shapes, const int64_t* level_start_index,
+                      const void* sampling_locations, const void* attention_weights, void* out,
+                      int64_t B, int64_t Q, int64_t N, int64_t H, int64_t D, int64_t L, int64_t P,
+                      void* stream, char* err, size_t err_len) {
+    if (dtype_size(dtype) == 0) return fail(err, err_len, TD_ERR_ARG, "unsupported dtype code %d", dtype);
+    if (int rc = check_geometry(B, Q, N, H, L, P, err, err_len)) return rc;
+    if (D <= 0 || s_img < 0 || s_tok < 0 || s_head < 0)
+        return fail(err, err_len, TD_ERR_ARG, "head size must be positive and strides non-negative");
+    if (B * Q == 0) return TD_OK;
+    if (!value || !sampling_locations || !attention_weights || !out ||
+        (L * P > 0 && (!spatial_shapes || !level_start_index)))
+        return fail(err, err_len, TD_ERR_ARG, "null tensor pointer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return dispatch(dtype, [&](auto tag) {
+        using T = decltype(tag);
+        return launch_sampler<T>(static_cast<const T*>(value), s_img, s_tok, s_head, spatial_shapes,
+                                 level_start_index, static_cast<const T*>(sampling_locations),
+                                 static_cast<const T*>(attention_weights), static_cast<T*>(out), B, Q, N, H, D, L,
+                                 P, s, err, err_len);
+    });
+}
+
+size_t td_project_workspace_bytes(int dtype, int64_t B, int64_t N, int64_t HD) {
+    const size_t e = dtype_size(dtype);
+    if (e == 0 || B < 0 || N < 0 || HD < 0) return 0;
+    return size_t(B) * size_t(N) * size_t(HD) * e + 256;
+}
+
+int td_project_forward(int dtype, const void* memory, const void* value_weight, const void* value_bias,
+                       const int64_t* spatial_shapes, const int64_t* level_start_index,
+                       const void* sampling_locations, const void* attention_weights, void* out,
+                       int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H, int64_t HD, int64_t L, int64_t P,
+                       void* workspace, size_t workspace_bytes, void* stream, char* err, size_t err_len) {
+    if (dtype_size(dtype) == 0) return fail(err, err_len, TD_ERR_ARG, "unsupported dtype code %d", dtype);
+    if (int rc = check_geometry(B, Q, N, H, L, P, err, err_len)) return rc;
+    if (C <= 0 || HD <= 0) return fail(err, err_len, TD_ERR_ARG, "channels and value_weight rows must be positive");
+    if (HD % H != 0) return fail(err, err_len, TD_ERR_ARG, "value_weight rows must be a multiple of the head count");
+    if (B * Q == 0) return TD_OK;
+    if (!memory || !value_weight || !sampling_locations || !attention_weights || !out ||
+        (L * P > 0 && (!spatial_shapes || !level_start_index)))
+        return fail(err, err_len, TD_ERR_ARG, "null tensor pointer");
+    const size_t need = td_project_workspace_bytes(dtype, B, N, HD);
+    if (workspace == nullptr || workspace_bytes < need)
+        return fail(err, err_len, TD_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need,
+                    workspace_bytes);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t D = HD / H;
+    // head-major value at the first 256-byte boundary of the workspace
+    void* value = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+    return dispatch(dtype, [&](auto tag) {
+        using T = decltype(tag);
+        T* v = static_cast<T*>(value);
+        if (int rc = launch_proj<T>(static_cast<const T*>(memory), static_cast<const T*>(value_weight),
+                                    static_cast<const T*>(value_bias), v, B, N, C, H, HD, 1, s, err, err_len))
+            return rc;
+        return launch_sampler<T>(v, H * N * D, D, N * D, spatial_shapes, level_start_index,
+                                 static_cast<const T*>(sampling_locations), static_cast<const T*>(attention_weights),
+                                 static_cast<T*>(out), B, Q, N, H, D, L, P, s, err, err_len);
+    });
+}
+
+int td_device_info(int device, int* sm_count, int* cc_major, int* cc_minor, char* err, size_t err_len) {
+    cudaError_t e = cudaDeviceGetAttribute(sm_count, cudaDevAttrMultiProcessorCount, device);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(cc_major, cudaDevAttrComputeCapabilityMajor, device);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(cc_minor, cudaDevAttrComputeCapabilityMinor, device);
+    if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "device %d: %s", device, cudaGetErrorString(e));
+    return TD_OK;
+}
+
+uint64_t td_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+const char* td_version(void) { return "0.1.1+b200"; }
+
+}  // extern "C"

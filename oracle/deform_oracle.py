@@ -1,0 +1,188 @@
+"""CPU oracle for ma_deform_attn -- TEST INFRASTRUCTURE ONLY.
+
+Nothing in the product imports this module. Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline and
+reference legs use it, and only as the checker or as the timed CPU baseline, never as the thing measured or shipped.
+
+It restates upstream's definition of the operator, ``ma_deform_attn_reference`` (marearts_tinydeform/reference.py
+:13-40 of MareArts/marearts-tinydeform v0.1.1):
+  * value = memory @ W^T + b                                             (reference.py:28)
+  * per level, grid_sample(value, 2 * loc - 1, bilinear, zeros, align_corners=False)  (reference.py:29-37)
+  * the attention-weighted sum over levels x points                      (reference.py:38-40)
+
+Two forms:
+  ``ma_deform_attn_oracle``  numpy, float64, explicit bilinear corners: the parity checker.
+  ``torch_port``             the same steps on torch's CPU operators (F.linear + F.grid_sample) in the input dtype:
+                             the timed CPU baseline (it runs the exact operators upstream's CPU path runs).
+Both are pinned against golden vectors written by upstream's own ma_deform_attn_reference
+(tests/golden/make_golden.py, checked by tests/test_oracle_golden.py).
+
+Sampling rule: grid_sample with align_corners=False maps g = 2 * loc - 1 to pixel x = ((g + 1) * w - 1) / 2 =
+loc * w - 0.5; corner (x0 + dx, y0 + dy) of x0 = floor(x) has weight (dx ? fx : 1 - fx) * (dy ? fy : 1 - fy) and
+contributes only inside the map (zero padding). For finite locations, clamping x to [-2, w + 1] first changes
+nothing; for NaN / +-inf it makes the oracle follow upstream's CUDA kernel (csrc/ma_deform_fused.cu:87-89: such
+points sample nothing), where grid_sample itself returns NaN.
+"""
+
+import numpy as np
+
+
+def _np(t):
+    """torch tensor / numpy array / None -> float64 or int64 numpy array."""
+    if t is None:
+        return None
+    if hasattr(t, 'detach'):
+        t = t.detach().cpu()
+        if t.dtype.is_floating_point:
+            t = t.double()
+        t = t.numpy()
+    t = np.asarray(t)
+    return t.astype(np.float64) if t.dtype.kind == 'f' else t.astype(np.int64)
+
+
+def project(memory, weight, bias):
+    """value = memory @ weight.T + bias in float64 (reference.py:28, F.linear)."""
+    value = _np(memory) @ _np(weight).T
+    if bias is not None:
+        value = value + _np(bias)
+    return value
+
+
+def level_corners(loc_xy, attn, height, width, start, n_tok):
+    """Corner tokens and weights of every point of one level (reference.py:30-37 restated).
+
+    loc_xy [..., 2] (x, y in [0, 1]); attn [...] -> tok [..., 4] int64 (-1 = outside), wt [..., 4] float64.
+    """
+    def pixel(v, size):
+        p = v * size - 0.5
+        p = np.where(np.isnan(p), -2.0, p)
+        return np.clip(p, -2.0, size + 1.0)
+
+    x = pixel(loc_xy[..., 0], width)
+    y = pixel(loc_xy[..., 1], height)
+    x0, y0 = np.floor(x), np.floor(y)
+    fx, fy = x - x0, y - y0
+    x0, y0 = x0.astype(np.int64), y0.astype(np.int64)
+    toks, wts = [], []
+    for dy in (0, 1):
+        for dx in (0, 1):
+            xi, yi = x0 + dx, y0 + dy
+            tok = start + yi * width + xi
+            inside = (xi >= 0) & (xi < width) & (yi >= 0) & (yi < height) & (tok >= 0) & (tok < n_tok)
+            w = attn * (fx if dx else 1.0 - fx) * (fy if dy else 1.0 - fy)
+            toks.append(np.where(inside, tok, -1))
+            wts.append(np.where(inside, w, 0.0))
+    return np.stack(toks, -1), np.stack(wts, -1)
+
+
+def sample(value, n_head, spatial_shapes, level_start_index, sampling_locations, attention_weights):
+    """Multi-scale deformable sampling of value [B, N, H*D] -> [B, Q, H*D] in float64 (reference.py:29-40)."""
+    value = _np(value)
+    shapes, starts = _np(spatial_shapes), _np(level_start_index)
+    loc, attn = _np(sampling_locations), _np(attention_weights)
+    B, N, HD = value.shape
+    _, Q, H, L, P, _ = loc.shape
+    assert H == n_head
+    D = HD // H
+    v = value.reshape(B, N, H, D)
+    out = np.zeros((B, Q, H, D))
+    bi = np.arange(B).reshape(B, 1, 1, 1)
+    hi = np.arange(H).reshape(1, 1, H, 1)
+    for lvl in range(L):
+        tok, wt = level_corners(loc[:, :, :, lvl], attn[:, :, :, lvl], int(shapes[lvl, 0]), int(shapes[lvl, 1]),
+                                int(starts[lvl]), N)                      # [B, Q, H, P, 4]
+        for k in range(4):
+            t = tok[..., k]
+            rows = v[bi, np.maximum(t, 0), hi]                         # [B, Q, H, P, D]
+            out += np.einsum('bqhp,bqhpd->bqhd', wt[..., k], np.where((t >= 0)[..., None], rows, 0.0))
+    return out.reshape(B, Q, HD)
+
+
+def ma_deform_attn_oracle(memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                          sampling_locations, attention_weights):
+    """Upstream ma_deform_attn_reference (reference.py:13-40) in float64 numpy: [B, Q, H*D]."""
+    H = sampling_locations.shape[2]
+    value = project(memory, value_weight, value_bias)
+    return sample(value, H, spatial_shapes, level_start_index, sampling_locations, attention_weights)
+
+
+def fused_order(memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                sampling_locations, attention_weights):
+    """The same result in the fused order (upstream csrc/ma_deform_fused.cu:6-14):
+    out[d] = W[hD + d] . (sum_s w_s memory[t_s]) + b[hD + d] * sum_s w_s.  Used as an independent property check."""
+    mem, W = _np(memory), _np(value_weight)
+    b = None if value_bias is None else _np(value_bias)
+    shapes, starts = _np(spatial_shapes), _np(level_start_index)
+    loc, attn = _np(sampling_locations), _np(attention_weights)
+    B, N, C = mem.shape
+    _, Q, H, L, P, _ = loc.shape
+    D = W.shape[0] // H
+    m = np.zeros((B, Q, H, C))
+    wsum = np.zeros((B, Q, H))
+    bi = np.arange(B).reshape(B, 1, 1, 1)
+    for lvl in range(L):
+        tok, wt = level_corners(loc[:, :, :, lvl], attn[:, :, :, lvl], int(shapes[lvl, 0]), int(shapes[lvl, 1]),
+                                int(starts[lvl]), N)
+        for k in range(4):
+            t = tok[..., k]
+            rows = np.where((t >= 0)[..., None], mem[bi, np.maximum(t, 0)], 0.0)   # [B, Q, H, P, C]
+            m += np.einsum('bqhp,bqhpc->bqhc', wt[..., k], rows)
+            wsum += wt[..., k].sum(-1)
+    Wh = W.reshape(H, D, C)
+    out = np.einsum('bqhc,hdc->bqhd', m, Wh)
+    if b is not None:
+        out += wsum[..., None] * b.reshape(H, D)
+    return out.reshape(B, Q, H * D)
+
+
+def oracle_rows(memory, value_weight, value_bias, spatial_shapes, level_start_index, sampling_locations,
+                attention_weights, queries):
+    """Oracle output for selected (b, q) pairs only: [len(queries), H*D] float64.
+
+    Projects only the memory rows those queries touch, so full-size configs can be spot-checked in seconds.
+    """
+    mem, W = _np(memory), _np(value_weight)
+    b = None if value_bias is None else _np(value_bias)
+    shapes, starts = _np(spatial_shapes), _np(level_start_index)
+    loc, attn = _np(sampling_locations), _np(attention_weights)
+    B, N, C = mem.shape
+    _, Q, H, L, P, _ = loc.shape
+    D = W.shape[0] // H
+    out = np.zeros((len(queries), H * D))
+    for i, (bb, qq) in enumerate(queries):
+        acc = np.zeros((H, D))
+        for lvl in range(L):
+            tok, wt = level_corners(loc[bb, qq, :, lvl], attn[bb, qq, :, lvl], int(shapes[lvl, 0]),
+                                    int(shapes[lvl, 1]), int(starts[lvl]), N)   # [H, P, 4]
+            for h in range(H):
+                t, w = tok[h].ravel(), wt[h].ravel()
+                keep = t >= 0
+                if not keep.any():
+                    continue
+                rows = mem[bb, t[keep]] @ W[h * D:(h + 1) * D].T                 # [k, D]
+                if b is not None:
+                    rows = rows + b[h * D:(h + 1) * D]
+                acc[h] += w[keep] @ rows
+        out[i] = acc.reshape(-1)
+    return out
+
+
+def torch_port(memory, value_weight, value_bias, spatial_shapes, level_start_index,
+               sampling_locations, attention_weights):
+    """reference.py:13-40 on torch's CPU operators, in the inputs' dtype (the timed CPU baseline)."""
+    import torch
+    import torch.nn.functional as F
+
+    B, N, _ = memory.shape
+    _, Q, H, L, P, _ = sampling_locations.shape
+    value = F.linear(memory, value_weight, value_bias)
+    D = value.shape[-1] // H
+    grid = (2 * sampling_locations - 1).transpose(1, 2).reshape(B * H, Q, L, P, 2)
+    heads = value.view(B, N, H, D).permute(0, 2, 3, 1).reshape(B * H, D, N)
+    parts = []
+    for lvl in range(L):
+        h, w, s = int(spatial_shapes[lvl, 0]), int(spatial_shapes[lvl, 1]), int(level_start_index[lvl])
+        img = heads[:, :, s:s + h * w].reshape(B * H, D, h, w)
+        parts.append(F.grid_sample(img, grid[:, :, lvl], mode='bilinear', padding_mode='zeros', align_corners=False))
+    a = attention_weights.transpose(1, 2).reshape(B * H, 1, Q, L * P)
+    out = (torch.cat(parts, -1) * a).sum(-1)
+    return out.view(B, H * D, Q).transpose(1, 2).contiguous()

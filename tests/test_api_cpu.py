@@ -1,0 +1,71 @@
+"""The drop-in API on CPU: names, the CPU route to the reference, the auto picker and its per-GPU tables."""
+
+import pytest
+import torch
+
+import marearts_tinydeform
+import marearts_tinydeform_b200 as td
+from cases import make
+from marearts_tinydeform import choose_mode, ma_deform_attn, ma_deform_attn_reference
+
+
+def test_upstream_import_name_serves_this_package():
+    for name in ('ma_deform_attn', 'ma_deform_attn_reference', 'choose_mode', 'FUSED_LIMIT', 'FUSED_LIMIT_SM75',
+                 '_limits', 'MODES', '__version__'):
+        assert getattr(marearts_tinydeform, name) is getattr(td, name)
+    assert td.MODES == ('auto', 'fused', 'project')
+    assert marearts_tinydeform.__all__ == ['ma_deform_attn', 'ma_deform_attn_reference', 'choose_mode']
+
+
+def test_cpu_path_is_reference():
+    args = make(1, 10, 2, 8, 16, [(6, 7), (3, 4)], 2)
+    with torch.inference_mode():
+        assert torch.equal(ma_deform_attn(*args), ma_deform_attn_reference(*args))
+        for mode in td.MODES:
+            assert torch.equal(ma_deform_attn(*args, mode=mode), ma_deform_attn_reference(*args))
+
+
+def test_bad_mode_is_a_value_error():
+    args = make(1, 4, 2, 8, 16, [(6, 7)], 2)
+    with pytest.raises(ValueError):
+        ma_deform_attn(*args, mode='nope')
+
+
+def test_reference_supports_autograd():
+    args = make(1, 6, 2, 8, 16, [(6, 7), (3, 4)], 2)
+    args[0].requires_grad_(True)
+    args[1].requires_grad_(True)
+    ma_deform_attn_reference(*args).square().sum().backward()
+    assert args[0].grad is not None and args[1].grad is not None
+
+
+def test_auto_picks_fused_for_few_queries():
+    few = make(1, 50, 8, 32, 256, [(80, 80), (40, 40), (20, 20)], 4)
+    many = make(8, 900, 8, 32, 256, [(80, 80), (40, 40), (20, 20)], 4)
+    assert choose_mode(few[0], few[1], few[5]) == 'fused'
+    assert choose_mode(many[0], many[1], many[5]) == 'project'
+
+
+def test_auto_limits_follow_the_gpu_generation():
+    get = torch.cuda.get_device_capability
+    try:
+        for cap, table in (((8, 9), td.FUSED_LIMIT), ((7, 5), td.FUSED_LIMIT_SM75), ((10, 0), td.FUSED_LIMIT_SM100),
+                           ((9, 0), td.FUSED_LIMIT)):
+            torch.cuda.get_device_capability = lambda device=None, cap=cap: cap
+            assert td._limits.__wrapped__(0) is table
+    finally:
+        torch.cuda.get_device_capability = get
+
+
+def test_auto_tables_cover_every_dtype():
+    for table in (td.FUSED_LIMIT, td.FUSED_LIMIT_SM75, td.FUSED_LIMIT_SM100):
+        for dtype in (torch.float32, torch.float16, torch.bfloat16):
+            a, b = table[dtype]
+            assert a >= 0 and b >= 0
+
+
+def test_tensor_contract_rejects_cpu_tensors_in_the_native_path():
+    from marearts_tinydeform_b200 import _native
+    args = make(1, 4, 2, 8, 16, [(6, 7)], 2)
+    with pytest.raises(RuntimeError, match='CUDA'):
+        _native.check_geometry(args[0], args[3], args[4], args[5], args[6])
