@@ -99,7 +99,7 @@ class ClockSampler:
 
 def input_pool(cfg_name, B, device, min_bytes):
     """Distinct input sets (memory, loc, attn per set; weights shared) totalling at least min_bytes."""
-    base = workloads.make_inputs(cfg_name, seed=0, B=B, device=device)
+    base = workloads.make_inputs(cfg_name, seed=0, B=B, device=device, generate_on_device=True)
     per_set = sum(t.numel() * t.element_size() for t in (base[0], base[5], base[6]))
     n = max(2, -(-min_bytes // per_set))
     g = torch.Generator(device=device).manual_seed(1234)
@@ -350,7 +350,7 @@ def run_sweep(args):
     with torch.inference_mode():
         for cfg, dname, B, Q in grids:
             dtype = getattr(torch, dname)
-            a = workloads.make_inputs(cfg, seed=0, B=B, Q=Q, dtype=dtype, device='cuda')
+            a = workloads.make_inputs(cfg, seed=0, B=B, Q=Q, dtype=dtype, device='cuda', generate_on_device=True)
             t = {}
             for mode in ('fused', 'project'):
                 g, _ = graph_time_us(lambda i, m=mode: ma_deform_attn(*a, mode=m), 50, 3)

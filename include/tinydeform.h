@@ -110,6 +110,21 @@ TD_API int td_project_forward(int dtype, const void* memory, const void* value_w
                        int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H, int64_t HD, int64_t L, int64_t P,
                        void* workspace, size_t workspace_bytes, void* stream, char* err, size_t err_len);
 
+/*
+ * Kernel policy for every later call in this process: TD_POLICY_BEST (default) uses the tcgen05 tensor-core
+ * kernels wherever the shapes allow; TD_POLICY_CUDA_CORES keeps every call on the CUDA-core kernels (parity tests
+ * run both). No counterpart in upstream, which has only CUDA-core kernels. Returns the previous policy.
+ */
+enum td_policy { TD_POLICY_BEST = 0, TD_POLICY_CUDA_CORES = 1 };
+TD_API int td_set_kernel_policy(int policy);
+
+/*
+ * Reads the library's device error word on the current device (0 = no error), and clears it when `clear` is set.
+ * The tensor-core kernels bound every wait; a wait that gives up (about one second) stores a non-zero code here
+ * instead of hanging. Synchronises with the device. No counterpart in upstream.
+ */
+TD_API int td_device_error(int clear, unsigned int* code, char* err, size_t err_len);
+
 /* Device facts used by the auto picker and the bench: SM count and compute capability of `device`. */
 TD_API int td_device_info(int device, int* sm_count, int* cc_major, int* cc_minor, char* err, size_t err_len);
 

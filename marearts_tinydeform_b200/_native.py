@@ -34,6 +34,8 @@ SIGNATURES = {
     'td_project_workspace_bytes': (_sz, [_ip, _i64, _i64, _i64]),
     'td_project_forward': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                  _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp, _cp, _sz]),
+    'td_set_kernel_policy': (_ip, [_ip]),
+    'td_device_error': (_ip, [_ip, ctypes.POINTER(ctypes.c_uint), _cp, _sz]),
     'td_device_info': (_ip, [_ip, ctypes.POINTER(_ip), ctypes.POINTER(_ip), ctypes.POINTER(_ip), _cp, _sz]),
     'td_launch_count': (ctypes.c_uint64, []),
     'td_version': (ctypes.c_char_p, []),
@@ -238,6 +240,24 @@ def value_proj(memory, value_weight, value_bias, heads, head_major=False):
         _call(lib.td_value_proj, DTYPE_CODE[memory.dtype], _ptr(mem), _ptr(w), _ptr(b), _ptr(value), B, N, C,
               heads, HD, 1 if head_major else 0, _stream(memory.device))
     return value
+
+
+POLICY_BEST, POLICY_CUDA_CORES = 0, 1
+
+
+def set_kernel_policy(policy):
+    """POLICY_BEST (tcgen05 where the shapes allow, the default) or POLICY_CUDA_CORES; returns the previous one."""
+    prev = load().td_set_kernel_policy(policy)
+    if prev < 0:
+        raise ValueError(f'unknown kernel policy {policy}')
+    return prev
+
+
+def device_error(clear=True):
+    """The library's device error word on the current device (0 = fine); synchronises."""
+    code = ctypes.c_uint(0)
+    _call(load().td_device_error, 1 if clear else 0, ctypes.byref(code))
+    return code.value
 
 
 def launch_count():

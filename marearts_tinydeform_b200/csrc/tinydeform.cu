@@ -3,23 +3,29 @@
 // The argument contract mirrors upstream's check_geometry and weight/bias checks (csrc/ma_deform_fused.cu:235-266,
 // :298-308, :333): levels x points <= 64, C <= 8192, N and B*Q*H within int32, HD a multiple of H. Tensor-level
 // checks (ranks, dtypes, devices) live in the Python mirror, which only ever passes dense device pointers here.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
+#include <type_traits>
 
 #include "../../include/tinydeform.h"
 #include "td_common.cuh"
 #include "td_fused_simt.cuh"
+#include "td_fused_tc.cuh"
 #include "td_gemm_simt.cuh"
+#include "td_gemm_tc.cuh"
 #include "td_sampler.cuh"
 
 namespace td {
 namespace {
 
 std::atomic<uint64_t> g_launches{0};
+std::atomic<int> g_policy{TD_POLICY_BEST};
 
 int fail(char* err, size_t err_len, int code, const char* fmt, ...) {
     if (err != nullptr && err_len > 0) {
@@ -115,6 +121,30 @@ int launch_sampler(const T* value, long long s_img, long long s_tok, long long s
     return check_launch(err, err_len, vec ? "sample_vec_kernel" : "sample_generic_kernel");
 }
 
+int tensor_map_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows, char* err,
+                  size_t err_len);
+template <typename K>
+int allow_smem(K kernel, size_t bytes, std::atomic<uint64_t>& done, char* err, size_t err_len);
+
+template <typename T>
+int launch_fused_tc(const T* memory, const T* weight, const T* bias, const int64_t* shapes, const int64_t* starts,
+                    const T* loc, const T* attn, T* out, int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H,
+                    int64_t D, int64_t L, int64_t P, int RQ, size_t smem, cudaStream_t stream, char* err,
+                    size_t err_len) {
+    static std::atomic<uint64_t> smem_done{0};
+    CUtensorMap map_w;
+    if (int rc = tensor_map_2d(&map_w, weight, uint64_t(C), uint64_t(H * D), uint32_t(D), err, err_len)) return rc;
+    if (int rc = allow_smem(fused_tc_kernel<T>, smem, smem_done, err, err_len)) return rc;
+    FusedTcArgs<T> a;
+    a.memory = memory; a.bias = bias; a.loc = loc; a.attn = attn; a.out = out; a.shapes = shapes; a.starts = starts;
+    a.n_tok = N; a.B = int(B); a.Q = int(Q); a.C = int(C); a.H = int(H); a.D = int(D); a.L = int(L); a.P = int(P);
+    a.RQ = RQ; a.q_tiles = int((Q + RQ - 1) / RQ);
+    const long long grid = B * H * (long long)a.q_tiles;
+    fused_tc_kernel<T><<<unsigned(grid), kFtcThreads, smem, stream>>>(map_w, a);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return check_launch(err, err_len, "fused_tc_kernel");
+}
+
 template <typename T>
 int launch_fused(const T* memory, const T* weight, const T* bias, const int64_t* shapes, const int64_t* starts,
                  const T* loc, const T* attn, T* out, int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H,
@@ -122,6 +152,20 @@ int launch_fused(const T* memory, const T* weight, const T* bias, const int64_t*
     using A = typename Elem<T>::acc;
     DeviceFacts f;
     if (int rc = device_facts(&f, err, err_len)) return rc;
+    if constexpr (std::is_same<T, __half>::value || std::is_same<T, __nv_bfloat16>::value) {
+        // tcgen05 path: N = D a multiple of 16, whole 64-wide K blocks, 16-byte aligned rows and outputs
+        if (g_policy.load(std::memory_order_relaxed) == TD_POLICY_BEST && D % 16 == 0 && D <= 256 && C % 64 == 0 &&
+            aligned16(memory) && aligned16(weight) && aligned16(out)) {
+            const int S = int(4 * L * P);
+            // queries per CTA: the largest of 32, 16, 8 that still gives two CTAs per SM
+            int RQ = 32;
+            while (RQ > 8 && B * H * ((Q + RQ - 1) / RQ) < 2LL * f.sm_count) RQ >>= 1;
+            const size_t smem = FusedTcLayout(RQ, int(C), int(D), S).bytes;
+            if (smem <= size_t(f.smem_optin) - 1024)
+                return launch_fused_tc<T>(memory, weight, bias, shapes, starts, loc, attn, out, B, Q, N, C, H, D, L,
+                                          P, RQ, smem, stream, err, err_len);
+        }
+    }
     const int S = int(4 * L * P);
     // rows per CTA: up to 16 queries of one (batch, head), fewer when that leaves SMs idle or m does not fit
     int R = kFusedMaxRows;
@@ -149,9 +193,90 @@ int launch_fused(const T* memory, const T* weight, const T* bias, const int64_t*
     return check_launch(err, err_len, "fused_simt_kernel");
 }
 
+// cuTensorMapEncodeTiled, reached through the runtime so the library does not link libcuda directly.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2-D row-major tensor of 16-bit elements [rows, cols], 128-byte-swizzled boxes of box_rows x 64 elements.
+int tensor_map_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows, char* err,
+                  size_t err_len) {
+    auto encode = tensor_map_encoder();
+    if (encode == nullptr) return fail(err, err_len, TD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {uint32_t(kTcBK), box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(err, err_len, TD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+    return TD_OK;
+}
+
+// Raise a kernel's dynamic shared memory limit once per device.
+template <typename K>
+int allow_smem(K kernel, size_t bytes, std::atomic<uint64_t>& done, char* err, size_t err_len) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = uint64_t(1) << (dev & 63);
+    if (done.load(std::memory_order_acquire) & bit) return TD_OK;
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+    if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    done.fetch_or(bit, std::memory_order_acq_rel);
+    return TD_OK;
+}
+
+template <typename T, int BN>
+int launch_proj_tc(const T* memory, const T* weight, const T* bias, T* value, int64_t M, int64_t N, int64_t C,
+                   int64_t H, int64_t HD, int head_major, cudaStream_t stream, char* err, size_t err_len) {
+    using Lay = ProjTcLayout<BN>;
+    static std::atomic<uint64_t> smem_done{0};
+    CUtensorMap map_a, map_b;
+    if (int rc = tensor_map_2d(&map_a, memory, uint64_t(C), uint64_t(M), kTcBM, err, err_len)) return rc;
+    if (int rc = tensor_map_2d(&map_b, weight, uint64_t(C), uint64_t(HD), BN, err, err_len)) return rc;
+    if (int rc = allow_smem(proj_tc_kernel<T, BN>, Lay::kSmemBytes, smem_done, err, err_len)) return rc;
+    ProjTcArgs<T> a;
+    a.bias = bias; a.value = value; a.M = M; a.n_tok = N; a.C = int(C); a.HD = int(HD); a.H = int(H);
+    a.D = int(HD / H); a.head_major = head_major; a.k_blocks = int((C + kTcBK - 1) / kTcBK);
+    const dim3 grid(unsigned((M + kTcBM - 1) / kTcBM), unsigned((HD + BN - 1) / BN));
+    proj_tc_kernel<T, BN><<<grid, 128, Lay::kSmemBytes, stream>>>(map_a, map_b, a);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return check_launch(err, err_len, "proj_tc_kernel");
+}
+
 template <typename T>
 int launch_proj(const T* memory, const T* weight, const T* bias, T* value, int64_t B, int64_t N, int64_t C,
                 int64_t H, int64_t HD, int head_major, cudaStream_t stream, char* err, size_t err_len) {
+    if constexpr (std::is_same<T, __half>::value || std::is_same<T, __nv_bfloat16>::value) {
+        // tcgen05 path: 16-byte aligned rows for TMA, K at least one 64-wide block, 8-column groups per head
+        const int64_t D = HD / H;
+        const bool tc = g_policy.load(std::memory_order_relaxed) == TD_POLICY_BEST && C >= kTcBK && C % 8 == 0 &&
+                        HD % 16 == 0 && D % 8 == 0 && aligned16(memory) && aligned16(weight) && aligned16(value);
+        if (tc) {
+            DeviceFacts f;
+            if (int rc = device_facts(&f, err, err_len)) return rc;
+            const int64_t M = B * N, m_tiles = (M + kTcBM - 1) / kTcBM;
+            // one N tile when that still fills the SMs twice over; else 128 (or 64) wide tiles for more CTAs
+            if (HD > 128 && HD <= 256 && m_tiles >= 2LL * f.sm_count)
+                return launch_proj_tc<T, 256>(memory, weight, bias, value, M, N, C, H, HD, head_major, stream, err,
+                                              err_len);
+            if (HD > 64)
+                return launch_proj_tc<T, 128>(memory, weight, bias, value, M, N, C, H, HD, head_major, stream, err,
+                                              err_len);
+            return launch_proj_tc<T, 64>(memory, weight, bias, value, M, N, C, H, HD, head_major, stream, err,
+                                         err_len);
+        }
+    }
     ProjArgs<T> a;
     a.memory = memory; a.weight = weight; a.bias = bias; a.value = value;
     a.M = B * N; a.n_tok = N; a.C = int(C); a.HD = int(HD); a.H = int(H); a.D = int(HD / H);
@@ -313,6 +438,23 @@ int td_device_info(int device, int* sm_count, int* cc_major, int* cc_minor, char
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(cc_major, cudaDevAttrComputeCapabilityMajor, device);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(cc_minor, cudaDevAttrComputeCapabilityMinor, device);
     if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "device %d: %s", device, cudaGetErrorString(e));
+    return TD_OK;
+}
+
+int td_set_kernel_policy(int policy) {
+    if (policy != TD_POLICY_BEST && policy != TD_POLICY_CUDA_CORES) return -1;
+    return g_policy.exchange(policy);
+}
+
+int td_device_error(int clear, unsigned int* code, char* err, size_t err_len) {
+    unsigned int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v));
+    if (e == cudaSuccess && clear) {
+        const unsigned int zero = 0;
+        e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
+    }
+    if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "device error word: %s", cudaGetErrorString(e));
+    if (code != nullptr) *code = v;
     return TD_OK;
 }
 

@@ -49,30 +49,33 @@ def n_tokens(levels):
     return sum(h * w for h, w in levels)
 
 
-def make_inputs(name, seed=0, device='cpu', **overrides):
+def make_inputs(name, seed=0, device='cpu', generate_on_device=False, **overrides):
     """Seeded inputs of config `name` (keys of CONFIGS), with any field overridden (B, Q, dtype, ...).
 
     Returns (memory, value_weight, value_bias, spatial_shapes, level_start_index, sampling_locations,
-    attention_weights) on `device`.
+    attention_weights) on `device`. By default the numbers come from a CPU generator (identical on every machine);
+    generate_on_device=True draws them with a generator on `device` instead (fast, for timing only).
     """
     cfg = dict(CONFIGS[name])
     cfg.update(overrides)
     B, Q, C, H, D, P = cfg['B'], cfg['Q'], cfg['C'], cfg['H'], cfg['D'], cfg['P']
     levels, dtype = cfg['levels'], cfg['dtype']
     L, N, HD = len(levels), n_tokens(levels), H * D
-    g = torch.Generator().manual_seed(seed)
-    memory = torch.randn(B, N, C, generator=g) * cfg.get('memory_std', 1.0)
+    gdev = torch.device(device) if generate_on_device else torch.device('cpu')
+    g = torch.Generator(device=gdev).manual_seed(seed)
+    kw = dict(generator=g, device=gdev)
+    memory = torch.randn(B, N, C, **kw) * cfg.get('memory_std', 1.0)
     if cfg.get('weight', 'xavier') == 'normal':
-        weight = torch.randn(HD, C, generator=g) / math.sqrt(C)
+        weight = torch.randn(HD, C, **kw) / math.sqrt(C)
     else:
         bound = math.sqrt(6.0 / (HD + C))
-        weight = (torch.rand(HD, C, generator=g) * 2 - 1) * bound
-    bias = (torch.rand(HD, generator=g) * 2 - 1) * 0.05
+        weight = (torch.rand(HD, C, **kw) * 2 - 1) * bound
+    bias = (torch.rand(HD, **kw) * 2 - 1) * 0.05
     if 'bias_on_odd_seeds' in cfg and seed % 2 == 1:
         bias = None
     lo, hi = cfg.get('loc_range', (0.0, 1.0))
-    loc = torch.rand(B, Q, H, L, P, 2, generator=g) * (hi - lo) + lo
-    attn = torch.randn(B, Q, H, L * P, generator=g).softmax(-1).view(B, Q, H, L, P)
+    loc = torch.rand(B, Q, H, L, P, 2, **kw) * (hi - lo) + lo
+    attn = torch.randn(B, Q, H, L * P, **kw).softmax(-1).view(B, Q, H, L, P)
     shapes, starts = level_tensors(levels)
     out = [memory.to(dtype), weight.to(dtype), None if bias is None else bias.to(dtype), shapes, starts,
            loc.to(dtype), attn.to(dtype)]

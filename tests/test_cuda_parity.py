@@ -19,6 +19,15 @@ TOL = {torch.float32: (2e-5, 1e-4), torch.float16: (3e-3, 3e-3), torch.bfloat16:
 MODES = ('fused', 'project', 'auto')
 
 
+@pytest.fixture(params=['tensor-cores', 'cuda-cores'])
+def policy(request, cuda):
+    """Run a test once with the default kernels (tcgen05 where shapes allow) and once on CUDA cores only."""
+    code = _native.POLICY_BEST if request.param == 'tensor-cores' else _native.POLICY_CUDA_CORES
+    prev = _native.set_kernel_policy(code)
+    yield request.param
+    _native.set_kernel_policy(prev)
+
+
 def oracle(args):
     return torch.from_numpy(O.ma_deform_attn_oracle(*[t if t is None else t.cpu() for t in args]))
 
@@ -41,11 +50,11 @@ def test_cuda_float32(cuda):
 
 
 @pytest.mark.parametrize('dtype', [torch.float16, torch.bfloat16])
-def test_cuda_half_and_bfloat16(cuda, dtype):
+def test_cuda_half_and_bfloat16(policy, dtype):
     for name, *shape in CASES:
         for bias in (True, False):
             args = make(*shape, dtype=dtype, bias=bias, seed=1)
-            check(f'{name} {dtype} bias={bias}', to(args, cuda), oracle(upcast(args)), *TOL[dtype])
+            check(f'{name} {dtype} bias={bias} {policy}', to(args, 'cuda'), oracle(upcast(args)), *TOL[dtype])
 
 
 def test_cuda_float64(cuda):
@@ -62,11 +71,11 @@ def test_head_rows_that_are_not_a_power_of_two_vectors(cuda):
         check(f'D={D} {dtype}', to(args, cuda), oracle(upcast(args)), *TOL[dtype])
 
 
-def test_golden_vectors_through_cuda(cuda):
+def test_golden_vectors_through_cuda(policy):
     from test_oracle_golden import CASES as GOLDEN
     for key, dtype, inputs, expected, _ in GOLDEN:
         atol, rtol = TOL[dtype]
-        check(f'golden {key}', to(inputs, cuda), expected.double(), atol, rtol)
+        check(f'golden {key} {policy}', to(inputs, 'cuda'), expected.double(), atol, rtol)
 
 
 def test_unaligned_memory(cuda):
@@ -163,7 +172,8 @@ def test_rejects_bad_input(cuda):
         ma_deform_attn(*args, mode='nope')
 
 
-def test_sample_forward_and_value_proj(cuda):
+def test_sample_forward_and_value_proj(policy):
+    cuda = 'cuda'
     """The two halves of the project order through their own entry points (td_value_proj, td_sample_forward)."""
     for dtype in (torch.float32, torch.float16, torch.bfloat16):
         args = make(2, 37, 8, 32, 256, [(12, 13), (6, 7), (3, 4)], 4, dtype=dtype, seed=3)
@@ -216,12 +226,12 @@ def test_modes_agree_and_are_linear_in_attention(cuda):
 
 
 @pytest.mark.parametrize('name', ['c1', 'c1h', 'c2', 'c3'])
-def test_baseline_configs_full_size(cuda, name):
+def test_baseline_configs_full_size(policy, name):
     """BASELINE configs c1-c3 at full size against the full oracle."""
     for seed in (0, 1):
         args = workloads.make_inputs(name, seed=seed)
         dtype = args[0].dtype
-        check(f'{name} seed {seed}', to(args, cuda), oracle(upcast(args)), *TOL[dtype])
+        check(f'{name} seed {seed} {policy}', to(args, 'cuda'), oracle(upcast(args)), *TOL[dtype])
 
 
 def _spot_check(name, args, dtype, n=24, seed=0):
@@ -250,8 +260,26 @@ def test_c4_dino_full_size(cuda):
 
 
 @pytest.mark.parametrize('dtype', [torch.float32, torch.float16, torch.bfloat16])
-def test_c5_stress_sweep(cuda, dtype):
+def test_c5_stress_sweep(policy, dtype):
     """The stress config at the operator limits (L*P = 64, C = 512, D = 64) over its batch/query sweep."""
     for B, Q in ((1, 50), (4, 300), (8, 900), (64, 100)):
         args = workloads.make_inputs('c5', seed=B + Q, B=B, Q=Q, dtype=dtype)
         _spot_check(f'c5 B{B} Q{Q} {dtype}', args, dtype, n=12, seed=B)
+
+
+def test_tensor_core_shapes(policy):
+    """Shapes at the edges of the tcgen05 paths: D = 16 / 48 / 64 / 128, C = 64 .. 768, query tiles with a ragged
+    last tile, token counts that are not a multiple of the 128-row GEMM tile."""
+    for dtype in (torch.float16, torch.bfloat16):
+        for B, Q, H, D, C, levels, P in ((1, 7, 4, 16, 64, [(5, 7)], 4), (2, 33, 2, 48, 96 * 2, [(9, 9), (4, 5)], 4),
+                                         (1, 129, 4, 64, 256, [(11, 13), (6, 6)], 2),
+                                         (1, 40, 2, 128, 256, [(12, 12)], 8), (3, 17, 6, 64, 768, [(7, 9)], 4)):
+            args = make(B, Q, H, D, C, levels, P, dtype=dtype, seed=D + C)
+            check(f'tc shapes B{B} Q{Q} H{H} D{D} C{C} {dtype} {policy}', to(args, 'cuda'), oracle(upcast(args)),
+                  *TOL[dtype])
+
+
+def test_device_error_word_is_clear(cuda):
+    """No bounded wait in any tensor-core kernel gave up during the tests above."""
+    torch.cuda.synchronize()
+    assert _native.device_error(clear=True) == 0
