@@ -73,6 +73,38 @@ __device__ __forceinline__ void load16<double>(const double* p, double* o) {
     o[0] = v.x; o[1] = v.y;
 }
 
+// Widen a raw 16-byte vector (already loaded) to kVec accumulators.
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4& v, typename Elem<T>::acc* o);
+
+template <>
+__device__ __forceinline__ void unpack16<float>(const uint4& v, float* o) {
+    o[0] = __uint_as_float(v.x); o[1] = __uint_as_float(v.y); o[2] = __uint_as_float(v.z); o[3] = __uint_as_float(v.w);
+}
+template <>
+__device__ __forceinline__ void unpack16<__half>(const uint4& v, float* o) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        o[2 * i] = f.x; o[2 * i + 1] = f.y;
+    }
+}
+template <>
+__device__ __forceinline__ void unpack16<__nv_bfloat16>(const uint4& v, float* o) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+        o[2 * i] = f.x; o[2 * i + 1] = f.y;
+    }
+}
+template <>
+__device__ __forceinline__ void unpack16<double>(const uint4& v, double* o) {
+    o[0] = __hiloint2double(int(v.y), int(v.x));
+    o[1] = __hiloint2double(int(v.w), int(v.z));
+}
+
 // Narrow kVec accumulators to T and store them as one 16-byte vector.
 template <typename T>
 __device__ __forceinline__ void store16(T* p, const typename Elem<T>::acc* v);

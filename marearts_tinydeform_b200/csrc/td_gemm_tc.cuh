@@ -40,7 +40,8 @@ struct ProjTcLayout {
     static constexpr uint32_t kTileBytes = kTcStages * kStageBytes;
     static constexpr uint32_t kBarOffset = kTileBytes;                 // full[S], empty[S], accum
     static constexpr uint32_t kSlotOffset = kBarOffset + (2 * kTcStages + 1) * 8;
-    static constexpr uint32_t kSmemBytes = kSlotOffset + 16 + 1024;    // + slack to align the base to 1024
+    static constexpr uint32_t kBiasOffset = kSlotOffset + 16;           // BN floats
+    static constexpr uint32_t kSmemBytes = kBiasOffset + BN * 4 + 1024;  // + slack to align the base to 1024
     static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
 };
 
@@ -56,11 +57,13 @@ __global__ void __launch_bounds__(128, 1)
     uint64_t* empty = full + kTcStages;
     uint64_t* accum = empty + kTcStages;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Lay::kSlotOffset);
+    float* sbias = reinterpret_cast<float*>(smem + Lay::kBiasOffset);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long m0 = (long long)blockIdx.x * kTcBM;
     const int n0 = blockIdx.y * BN;
 
+    const int KB = a.k_blocks;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTcStages; ++s) {
             mbar_init(&full[s], 1);
@@ -68,9 +71,17 @@ __global__ void __launch_bounds__(128, 1)
         }
         mbar_init(accum, 1);
         mbar_fence_init();
-        tma_prefetch_desc(&map_a);
-        tma_prefetch_desc(&map_b);
+        // the first kTcStages K blocks need no free slot: start their loads before anything else
+        for (int kb = 0; kb < KB && kb < kTcStages; ++kb) {
+            unsigned char* st = smem + kb * Lay::kStageBytes;
+            mbar_arrive_expect_tx(&full[kb], Lay::kStageBytes);
+            tma_load_2d(st, &map_a, &full[kb], kb * kTcBK, int(m0));
+            tma_load_2d(st + Lay::kABytes, &map_b, &full[kb], kb * kTcBK, n0);
+        }
     }
+    // the tile's bias columns, staged while the loads are in flight
+    for (int i = threadIdx.x; i < BN; i += 128)
+        sbias[i] = (a.bias != nullptr && n0 + i < a.HD) ? to_acc(a.bias[n0 + i]) : 0.f;
     __syncwarp();
     if (warp == 0) {
         tmem_alloc(tmem_slot, Lay::kTmemCols);
@@ -80,11 +91,13 @@ __global__ void __launch_bounds__(128, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int KB = a.k_blocks;
+    // the sampler that follows in the project order may start its prologue now (it waits for this grid before
+    // reading value)
+    launch_dependents();
 
     if (warp == 0 && lane == 0) {
-        // TMA producer
-        for (int kb = 0; kb < KB; ++kb) {
+        // TMA producer for the K blocks beyond the first kTcStages
+        for (int kb = kTcStages; kb < KB; ++kb) {
             const int s = kb % kTcStages, round = kb / kTcStages;
             if (!mbar_wait(&empty[s], (round & 1) ^ 1, kErrSlotWait)) break;
             unsigned char* st = smem + s * Lay::kStageBytes;
@@ -115,7 +128,6 @@ __global__ void __launch_bounds__(128, 1)
     tc_fence_after();
     if (ready) {
         const long long row = m0 + warp * 32 + lane;
-        const T* bias = a.bias;
 #pragma unroll 1
         for (int j = 0; j < BN / 32; ++j) {
             const int col0 = n0 + 32 * j;
@@ -130,10 +142,7 @@ __global__ void __launch_bounds__(128, 1)
                     if (col >= a.HD) break;
                     float v[8];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        v[i] = __uint_as_float(r[8 * g + i]);
-                        if (bias != nullptr) v[i] += to_acc(bias[col + i]);
-                    }
+                    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[8 * g + i]) + sbias[32 * j + 8 * g + i];
                     store16<T>(a.value + proj_offset(row, col, a.n_tok, a.HD, a.H, a.D, a.head_major), v);
                 }
             }

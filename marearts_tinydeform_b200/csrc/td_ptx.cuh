@@ -94,6 +94,13 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// ---- programmatic dependent launch ----------------------------------------------------------------------------
+// In a kernel launched with programmatic stream serialization, wait until the preceding grid has completed and
+// its memory is visible; a no-op when the kernel was launched normally.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the next kernel in the stream, if launched with programmatic serialization, to start its prologue now.
+__device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- tcgen05: tensor memory ---------------------------------------------------------------------------------
 // Executed by one whole warp. Writes the TMEM base address to *slot.
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {

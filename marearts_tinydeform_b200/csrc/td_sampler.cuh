@@ -12,6 +12,7 @@
 #pragma once
 
 #include "td_common.cuh"
+#include "td_ptx.cuh"
 
 namespace td {
 
@@ -33,24 +34,39 @@ struct SampleArgs {
 constexpr int kSampleWarps = 8;
 
 // Vector kernel: needs D * sizeof(T) % 16 == 0, D * sizeof(T) <= 512, 16-byte aligned value/out and strides.
+// The dependent-latency chain is kept to two memory round trips: (level geometry + locations + attention weights,
+// all issued together) -> corners -> (every corner row of the lane's group issued together) -> butterfly -> store.
+// When launched with programmatic serialization right after the projection kernel, everything before
+// grid_dependency_wait() overlaps that kernel; value is only read after it.
 template <typename T>
 __global__ void __launch_bounds__(kSampleWarps * 32) sample_vec_kernel(const SampleArgs<T> a) {
     using A = typename Elem<T>::acc;
     using CT = typename Coord<T>::type;
     constexpr int V = Elem<T>::kVec;
-    __shared__ Level lv[kMaxLevels];
+    constexpr int kBatch = 8;  // corner rows in flight per lane
     __shared__ int s_tok[kSampleWarps][kMaxCorners];
     __shared__ CT s_wt[kSampleWarps][kMaxCorners];
-    load_levels(a.shapes, a.starts, a.L, lv);
-    __syncthreads();
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long row = (long long)blockIdx.x * kSampleWarps + warp;
-    if (row >= a.rows) return;  // whole warp leaves; only warp-level syncs follow
+    const bool live = row < a.rows;  // dead warps still reach grid_dependency_wait
     const int LP = a.L * a.P, S = 4 * LP;
-    for (int j = lane; j < LP; j += 32)
-        row_corners(a.loc, a.attn, lv, LP, a.P, a.n_tok, row, j, &s_tok[warp][4 * j], &s_wt[warp][4 * j]);
+    if (live) {
+        for (int j = lane; j < LP; j += 32) {
+            const int l = j / a.P;
+            Level lv;
+            long long hh = a.shapes[2 * l], ww = a.shapes[2 * l + 1];
+            lv.h = int(hh < 0 ? 0 : (hh > (1LL << 30) ? (1LL << 30) : hh));
+            lv.w = int(ww < 0 ? 0 : (ww > (1LL << 30) ? (1LL << 30) : ww));
+            lv.start = a.starts[l];
+            const long long i = row * LP + j;
+            corners4<CT>(CT(to_acc(a.loc[2 * i])), CT(to_acc(a.loc[2 * i + 1])), CT(to_acc(a.attn[i])), lv, a.n_tok,
+                         &s_tok[warp][4 * j], &s_wt[warp][4 * j]);
+        }
+    }
     __syncwarp();
+    grid_dependency_wait();
+    if (!live) return;
 
     const int h = int(row % a.H);
     const long long b = row / ((long long)a.Q * a.H);
@@ -59,15 +75,23 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_vec_kernel(const Sam
     A acc[V];
 #pragma unroll
     for (int i = 0; i < V; ++i) acc[i] = A(0);
-#pragma unroll 4
-    for (int s = cg; s < S; s += CG) {
-        const int t = s_tok[warp][s];
-        if (t >= 0) {
-            A x[V];
-            load16<T>(vb + (long long)t * a.s_tok + v * V, x);
-            const A w = A(s_wt[warp][s]);
+    for (int s0 = cg; s0 < S; s0 += kBatch * CG) {
+        uint4 raw[kBatch];
+        A w[kBatch];
 #pragma unroll
-            for (int i = 0; i < V; ++i) acc[i] = fma(w, x[i], acc[i]);
+        for (int u = 0; u < kBatch; ++u) {
+            const int s = s0 + u * CG;
+            const int t = s < S ? s_tok[warp][s] : -1;
+            w[u] = s < S ? A(s_wt[warp][s]) : A(0);
+            raw[u] = t >= 0 ? __ldg(reinterpret_cast<const uint4*>(vb + (long long)t * a.s_tok + v * V))
+                            : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            A x[V];
+            unpack16<T>(raw[u], x);
+#pragma unroll
+            for (int i = 0; i < V; ++i) acc[i] = fma(w[u], x[i], acc[i]);
         }
     }
     for (int o = G; o < 32; o <<= 1) {
@@ -85,6 +109,7 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_generic_kernel(const
     __shared__ Level lv[kMaxLevels];
     __shared__ int s_tok[kSampleWarps][kMaxCorners];
     __shared__ CT s_wt[kSampleWarps][kMaxCorners];
+    grid_dependency_wait();
     load_levels(a.shapes, a.starts, a.L, lv);
     __syncthreads();
 

@@ -99,7 +99,8 @@ int check_geometry(int64_t B, int64_t Q, int64_t N, int64_t H, int64_t L, int64_
 template <typename T>
 int launch_sampler(const T* value, long long s_img, long long s_tok, long long s_head, const int64_t* shapes,
                    const int64_t* starts, const T* loc, const T* attn, T* out, int64_t B, int64_t Q, int64_t N,
-                   int64_t H, int64_t D, int64_t L, int64_t P, cudaStream_t stream, char* err, size_t err_len) {
+                   int64_t H, int64_t D, int64_t L, int64_t P, cudaStream_t stream, char* err, size_t err_len,
+                   bool after_producer = false) {
     SampleArgs<T> a;
     a.value = value; a.loc = loc; a.attn = attn; a.out = out; a.shapes = shapes; a.starts = starts;
     a.rows = B * Q * H; a.s_img = s_img; a.s_tok = s_tok; a.s_head = s_head; a.n_tok = N;
@@ -112,11 +113,21 @@ int launch_sampler(const T* value, long long s_img, long long s_tok, long long s
                      (s_img * (long long)sizeof(T)) % 16 == 0 && (s_tok * (long long)sizeof(T)) % 16 == 0 &&
                      (s_head * (long long)sizeof(T)) % 16 == 0;
     const unsigned grid = unsigned((a.rows + kSampleWarps - 1) / kSampleWarps);
-    if (vec) {
-        sample_vec_kernel<T><<<grid, kSampleWarps * 32, 0, stream>>>(a);
-    } else {
-        sample_generic_kernel<T><<<grid, kSampleWarps * 32, 0, stream>>>(a);
-    }
+    // Right after td_project_forward's projection kernel, launch with programmatic stream serialization: the
+    // sampler's corner prologue then overlaps the projection, and it waits for it before reading value.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kSampleWarps * 32);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = after_producer ? 1 : 0;
+    cudaError_t e = vec ? cudaLaunchKernelEx(&cfg, sample_vec_kernel<T>, a)
+                        : cudaLaunchKernelEx(&cfg, sample_generic_kernel<T>, a);
+    if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "sampler launch: %s", cudaGetErrorString(e));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return check_launch(err, err_len, vec ? "sample_vec_kernel" : "sample_generic_kernel");
 }
@@ -181,12 +192,8 @@ int launch_fused(const T* memory, const T* weight, const T* bias, const int64_t*
     a.R = R; a.q_tiles = int((Q + R - 1) / R);
     a.vec = (C % Elem<T>::kVec == 0) && aligned16(memory);
     (void)sizeof(A);
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(fused_simt_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             int(smem));
-        if (e != cudaSuccess)
-            return fail(err, err_len, TD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    }
+    static std::atomic<uint64_t> smem_done{0};
+    if (int rc = allow_smem(fused_simt_kernel<T>, smem, smem_done, err, err_len)) return rc;
     const long long grid = B * H * (long long)a.q_tiles;
     fused_simt_kernel<T><<<unsigned(grid), kFusedThreads, smem, stream>>>(a);
     g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -226,11 +233,21 @@ int tensor_map_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t ro
 // Raise a kernel's dynamic shared memory limit once per device.
 template <typename K>
 int allow_smem(K kernel, size_t bytes, std::atomic<uint64_t>& done, char* err, size_t err_len) {
+    // the limit is raised to the device's opt-in maximum (less the kernel's static shared memory) once, so later
+    // calls may ask for any size up to it
+    DeviceFacts f;
+    if (int rc = device_facts(&f, err, err_len)) return rc;
+    cudaFuncAttributes attr;
+    cudaError_t e = cudaFuncGetAttributes(&attr, kernel);
+    if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "cudaFuncGetAttributes: %s", cudaGetErrorString(e));
+    const int dyn_max = f.smem_optin - int(attr.sharedSizeBytes);
+    if (bytes > size_t(dyn_max))
+        return fail(err, err_len, TD_ERR_ARG, "%zu bytes of shared memory needed, %d available", bytes, dyn_max);
     int dev = 0;
     cudaGetDevice(&dev);
     const uint64_t bit = uint64_t(1) << (dev & 63);
     if (done.load(std::memory_order_acquire) & bit) return TD_OK;
-    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn_max);
     if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     done.fetch_or(bit, std::memory_order_acq_rel);
     return TD_OK;
@@ -429,7 +446,7 @@ int td_project_forward(int dtype, const void* memory, const void* value_weight, 
             return rc;
         return launch_sampler<T>(v, H * N * D, D, N * D, spatial_shapes, level_start_index,
                                  static_cast<const T*>(sampling_locations), static_cast<const T*>(attention_weights),
-                                 static_cast<T*>(out), B, Q, N, H, D, L, P, s, err, err_len);
+                                 static_cast<T*>(out), B, Q, N, H, D, L, P, s, err, err_len, true);
     });
 }
 
