@@ -172,6 +172,18 @@ __device__ __forceinline__ void load_levels(const int64_t* __restrict__ shapes, 
     }
 }
 
+// The geometry of level l read straight from the device arrays (same clamping as load_levels), for kernels that
+// fetch it together with the sampling locations instead of staging it first.
+__device__ __forceinline__ Level level_at(const int64_t* __restrict__ shapes, const int64_t* __restrict__ starts,
+                                          int l) {
+    long long h = shapes[2 * l], w = shapes[2 * l + 1];
+    Level lv;
+    lv.h = int(h < 0 ? 0 : (h > (1LL << 30) ? (1LL << 30) : h));
+    lv.w = int(w < 0 ? 0 : (w > (1LL << 30) ? (1LL << 30) : w));
+    lv.start = starts[l];
+    return lv;
+}
+
 // The four bilinear corners of one sampling point. tok[k] = -1 marks a corner outside the map (it contributes
 // nothing, as zero padding); inside corners carry attn * bilinear weight, which may itself be 0.
 template <typename CT>

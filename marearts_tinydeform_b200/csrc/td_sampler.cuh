@@ -53,12 +53,7 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_vec_kernel(const Sam
     const int LP = a.L * a.P, S = 4 * LP;
     if (live) {
         for (int j = lane; j < LP; j += 32) {
-            const int l = j / a.P;
-            Level lv;
-            long long hh = a.shapes[2 * l], ww = a.shapes[2 * l + 1];
-            lv.h = int(hh < 0 ? 0 : (hh > (1LL << 30) ? (1LL << 30) : hh));
-            lv.w = int(ww < 0 ? 0 : (ww > (1LL << 30) ? (1LL << 30) : ww));
-            lv.start = a.starts[l];
+            const Level lv = level_at(a.shapes, a.starts, j / a.P);
             const long long i = row * LP + j;
             corners4<CT>(CT(to_acc(a.loc[2 * i])), CT(to_acc(a.loc[2 * i + 1])), CT(to_acc(a.attn[i])), lv, a.n_tok,
                          &s_tok[warp][4 * j], &s_wt[warp][4 * j]);

@@ -137,23 +137,64 @@ int tensor_map_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t ro
 template <typename K>
 int allow_smem(K kernel, size_t bytes, std::atomic<uint64_t>& done, char* err, size_t err_len);
 
+// CTAs of `kernel` one SM holds at once, from its register count, its shared memory (dynamic + static + the
+// per-block reservation) and the thread limit. At least 1.
+template <typename K>
+int resident_ctas(K kernel, int threads, size_t dyn_smem) {
+    int dev = 0, regs_sm = 65536, smem_sm = 233472, reserved = 1024, threads_sm = 2048;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    cudaDeviceGetAttribute(&threads_sm, cudaDevAttrMaxThreadsPerMultiProcessor, dev);
+    cudaFuncAttributes attr;
+    if (cudaFuncGetAttributes(&attr, kernel) != cudaSuccess) return 1;
+    const int regs_cta = ((attr.numRegs * 32 + 255) / 256 * 256) * (threads / 32);  // per-warp allocation unit
+    const size_t smem_cta = dyn_smem + attr.sharedSizeBytes + size_t(reserved);
+    int n = threads_sm / threads;
+    if (regs_cta > 0) n = n < regs_sm / regs_cta ? n : regs_sm / regs_cta;
+    const int by_smem = int(size_t(smem_sm) / smem_cta);
+    n = n < by_smem ? n : by_smem;
+    return n < 1 ? 1 : n;
+}
+
+template <typename T, int CV>
+int launch_fused_tc_cfg(const CUtensorMap& map_w, const FusedTcArgs<T>& a, int sm_count, size_t smem,
+                        cudaStream_t stream, char* err, size_t err_len) {
+    static std::atomic<uint64_t> smem_done{0};
+    auto kernel = fused_tc_kernel<T, CV>;
+    if (int rc = allow_smem(kernel, smem, smem_done, err, err_len)) return rc;
+    // one persistent CTA per SM, each with an equal share of the rows
+    const int grid = int(a.rows < sm_count ? a.rows : sm_count);
+    kernel<<<unsigned(grid), kFtcThreads, smem, stream>>>(map_w, a);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return check_launch(err, err_len, "fused_tc_kernel");
+}
+
+// Fused order on the tensor cores; *launched stays false when the shapes do not fit it (the caller then uses the
+// CUDA-core kernel).
 template <typename T>
 int launch_fused_tc(const T* memory, const T* weight, const T* bias, const int64_t* shapes, const int64_t* starts,
                     const T* loc, const T* attn, T* out, int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H,
-                    int64_t D, int64_t L, int64_t P, int RQ, size_t smem, cudaStream_t stream, char* err,
-                    size_t err_len) {
-    static std::atomic<uint64_t> smem_done{0};
+                    int64_t D, int64_t L, int64_t P, const DeviceFacts& f, cudaStream_t stream, char* err,
+                    size_t err_len, bool* launched) {
+    *launched = false;
+    if (C > 1024 || 2 * D > 512) return TD_OK;
+    const int S = int(4 * L * P);
+    const int CV = C <= 256 ? 1 : (C <= 512 ? 2 : 4);
+    const int pieces = fused_tc_pieces(S);
+    const size_t smem = FusedTcLayout(int(C), int(D), S, pieces).bytes;
+    if (smem > size_t(f.smem_optin) - 1024) return TD_OK;
     CUtensorMap map_w;
     if (int rc = tensor_map_2d(&map_w, weight, uint64_t(C), uint64_t(H * D), uint32_t(D), err, err_len)) return rc;
-    if (int rc = allow_smem(fused_tc_kernel<T>, smem, smem_done, err, err_len)) return rc;
     FusedTcArgs<T> a;
     a.memory = memory; a.bias = bias; a.loc = loc; a.attn = attn; a.out = out; a.shapes = shapes; a.starts = starts;
-    a.n_tok = N; a.B = int(B); a.Q = int(Q); a.C = int(C); a.H = int(H); a.D = int(D); a.L = int(L); a.P = int(P);
-    a.RQ = RQ; a.q_tiles = int((Q + RQ - 1) / RQ);
-    const long long grid = B * H * (long long)a.q_tiles;
-    fused_tc_kernel<T><<<unsigned(grid), kFtcThreads, smem, stream>>>(map_w, a);
-    g_launches.fetch_add(1, std::memory_order_relaxed);
-    return check_launch(err, err_len, "fused_tc_kernel");
+    a.n_tok = N; a.rows = B * H * Q; a.B = int(B); a.Q = int(Q); a.C = int(C); a.H = int(H); a.D = int(D);
+    a.L = int(L); a.P = int(P); a.pieces = pieces;
+    *launched = true;
+    if (CV == 1) return launch_fused_tc_cfg<T, 1>(map_w, a, f.sm_count, smem, stream, err, err_len);
+    if (CV == 2) return launch_fused_tc_cfg<T, 2>(map_w, a, f.sm_count, smem, stream, err, err_len);
+    return launch_fused_tc_cfg<T, 4>(map_w, a, f.sm_count, smem, stream, err, err_len);
 }
 
 template <typename T>
@@ -167,14 +208,10 @@ int launch_fused(const T* memory, const T* weight, const T* bias, const int64_t*
         // tcgen05 path: N = D a multiple of 16, whole 64-wide K blocks, 16-byte aligned rows and outputs
         if (g_policy.load(std::memory_order_relaxed) == TD_POLICY_BEST && D % 16 == 0 && D <= 256 && C % 64 == 0 &&
             aligned16(memory) && aligned16(weight) && aligned16(out)) {
-            const int S = int(4 * L * P);
-            // queries per CTA: the largest of 32, 16, 8 that still gives two CTAs per SM
-            int RQ = 32;
-            while (RQ > 8 && B * H * ((Q + RQ - 1) / RQ) < 2LL * f.sm_count) RQ >>= 1;
-            const size_t smem = FusedTcLayout(RQ, int(C), int(D), S).bytes;
-            if (smem <= size_t(f.smem_optin) - 1024)
-                return launch_fused_tc<T>(memory, weight, bias, shapes, starts, loc, attn, out, B, Q, N, C, H, D, L,
-                                          P, RQ, smem, stream, err, err_len);
+            bool launched = false;
+            const int rc = launch_fused_tc<T>(memory, weight, bias, shapes, starts, loc, attn, out, B, Q, N, C, H, D,
+                                              L, P, f, stream, err, err_len, &launched);
+            if (rc != TD_OK || launched) return rc;
         }
     }
     const int S = int(4 * L * P);
@@ -248,6 +285,9 @@ int allow_smem(K kernel, size_t bytes, std::atomic<uint64_t>& done, char* err, s
     const uint64_t bit = uint64_t(1) << (dev & 63);
     if (done.load(std::memory_order_acquire) & bit) return TD_OK;
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn_max);
+    // the whole unified L1 / shared array as shared memory, so several CTAs of a kernel fit on one SM
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     done.fetch_or(bit, std::memory_order_acq_rel);
     return TD_OK;
