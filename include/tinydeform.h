@@ -111,6 +111,28 @@ TD_API int td_project_forward(int dtype, const void* memory, const void* value_w
                        void* workspace, size_t workspace_bytes, void* stream, char* err, size_t err_len);
 
 /*
+ * Project order with no caller-provided workspace and no allocation at all. No counterpart in upstream.
+ *
+ * For callers that cannot allocate device memory on the call path: inference plugins run inside a host framework
+ * that owns all device memory (and forbids cudaMalloc in enqueue), real-time loops where cudaMalloc's implicit
+ * device synchronisation is not acceptable, and plain C hosts with no caching allocator to borrow a workspace from.
+ * The projected value lives instead in one file-scope device array of TD_NOALLOC_SCRATCH_BYTES that every GPU which
+ * loads this library holds until the process exits. Requests whose value (td_project_workspace_bytes) exceeds it
+ * are rejected with TD_ERR_WORKSPACE and a message naming both sizes; the RT-DETR 640x640 layer (B=1, N=8400,
+ * H*D=256) needs 4.3 MB in 16-bit types and 8.6 MB in float32.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress) with that device current;
+ * make that first call before any stream capture on the device. The array is shared by all calls and keeps the
+ * last call's contents; it is fully rewritten before it is read, so nothing needs clearing. Calls whose work
+ * overlaps on the GPU (other streams, other threads) race on it: serialise them.
+ */
+#define TD_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+TD_API int td_project_forward_noalloc(int dtype, const void* memory, const void* value_weight, const void* value_bias,
+                                      const int64_t* spatial_shapes, const int64_t* level_start_index,
+                                      const void* sampling_locations, const void* attention_weights, void* out,
+                                      int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H, int64_t HD, int64_t L,
+                                      int64_t P, void* stream, char* err, size_t err_len);
+
+/*
  * Kernel policy for every later call in this process: TD_POLICY_BEST (default) uses the tcgen05 tensor-core
  * kernels wherever the shapes allow; TD_POLICY_CUDA_CORES keeps every call on the CUDA-core kernels (parity tests
  * run both). No counterpart in upstream, which has only CUDA-core kernels. Returns the previous policy.

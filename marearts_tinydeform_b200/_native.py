@@ -34,6 +34,8 @@ SIGNATURES = {
     'td_project_workspace_bytes': (_sz, [_ip, _i64, _i64, _i64]),
     'td_project_forward': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                  _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp, _cp, _sz]),
+    'td_project_forward_noalloc': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                         _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _cp, _sz]),
     'td_set_kernel_policy': (_ip, [_ip]),
     'td_device_error': (_ip, [_ip, ctypes.POINTER(ctypes.c_uint), _cp, _sz]),
     'td_device_info': (_ip, [_ip, ctypes.POINTER(_ip), ctypes.POINTER(_ip), ctypes.POINTER(_ip), _cp, _sz]),

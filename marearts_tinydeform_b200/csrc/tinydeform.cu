@@ -490,6 +490,49 @@ int td_project_forward(int dtype, const void* memory, const void* value_weight, 
     });
 }
 
+}  // extern "C"
+
+// Scratch of td_project_forward_noalloc: the projected value of one call. A host-side name for device memory, so
+// host code only ever passes the address cudaGetSymbolAddress returns for the current device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[TD_NOALLOC_SCRATCH_BYTES];
+
+namespace td {
+namespace {
+std::once_flag g_scratch_once[kMaxDevices];
+void* g_scratch_ptr[kMaxDevices];
+cudaError_t g_scratch_status[kMaxDevices];
+}  // namespace
+}  // namespace td
+
+extern "C" {
+
+int td_project_forward_noalloc(int dtype, const void* memory, const void* value_weight, const void* value_bias,
+                               const int64_t* spatial_shapes, const int64_t* level_start_index,
+                               const void* sampling_locations, const void* attention_weights, void* out,
+                               int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H, int64_t HD, int64_t L,
+                               int64_t P, void* stream, char* err, size_t err_len) {
+    const size_t need = td_project_workspace_bytes(dtype, B, N, HD);
+    if (need > TD_NOALLOC_SCRATCH_BYTES)
+        return fail(err, err_len, TD_ERR_WORKSPACE,
+                    "the allocation-free project order holds at most %zu bytes of projected value, this call "
+                    "needs %zu (B * N * H * D elements plus 256 bytes of alignment)",
+                    size_t(TD_NOALLOC_SCRATCH_BYTES), need);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices) return fail(err, err_len, TD_ERR_CUDA, "device index %d out of range", dev);
+    // once per device, with that device current: the scratch array's device address
+    std::call_once(g_scratch_once[dev], [dev] {
+        g_scratch_status[dev] = cudaGetSymbolAddress(&g_scratch_ptr[dev], g_noalloc_scratch);
+    });
+    if (g_scratch_status[dev] != cudaSuccess)
+        return fail(err, err_len, TD_ERR_CUDA, "cudaGetSymbolAddress of the scratch array: %s",
+                    cudaGetErrorString(g_scratch_status[dev]));
+    return td_project_forward(dtype, memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                              sampling_locations, attention_weights, out, B, Q, N, C, H, HD, L, P,
+                              g_scratch_ptr[dev], TD_NOALLOC_SCRATCH_BYTES, stream, err, err_len);
+}
+
 int td_device_info(int device, int* sm_count, int* cc_major, int* cc_minor, char* err, size_t err_len) {
     cudaError_t e = cudaDeviceGetAttribute(sm_count, cudaDevAttrMultiProcessorCount, device);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(cc_major, cudaDevAttrComputeCapabilityMajor, device);
