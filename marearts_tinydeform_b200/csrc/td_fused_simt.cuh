@@ -11,6 +11,7 @@
 #pragma once
 
 #include "td_common.cuh"
+#include "td_ptx.cuh"
 
 namespace td {
 
@@ -65,6 +66,8 @@ __global__ void __launch_bounds__(kFusedThreads) fused_simt_kernel(const FusedAr
     off = (off + size_t(R) * S * sizeof(CT) + 15) / 16 * 16;
     A* wsum = reinterpret_cast<A*>(smem_raw + off);
 
+    grid_dependency_wait();  // launched with programmatic dependent launch: every global access comes after this
+    launch_dependents();
     // block -> (b, q-tile, h), heads fastest: the heads of one query sample around the same point, so CTAs that
     // run together read overlapping memory rows from L2.
     const int h = int(blockIdx.x % a.H);

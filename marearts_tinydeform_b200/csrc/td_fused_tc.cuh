@@ -128,6 +128,10 @@ __global__ void __launch_bounds__(kFtcThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_slot[0];
+    // Only shared memory and TMEM so far: under programmatic dependent launch this prologue overlaps the previous
+    // kernel in the stream, and every global access comes after this wait.
+    grid_dependency_wait();
+    launch_dependents();
 
     int slot_h[kFtcSegs] = {-1, -1};       // head whose weights each slot holds
     int slot_loads[kFtcSegs] = {0, 0};     // completed phases of each slot's barrier

@@ -7,6 +7,7 @@
 #pragma once
 
 #include "td_common.cuh"
+#include "td_ptx.cuh"
 
 namespace td {
 
@@ -38,6 +39,8 @@ __global__ void __launch_bounds__(kGemmThreads) proj_simt_kernel(const ProjArgs<
     using A = typename Elem<T>::acc;
     __shared__ A sa[kGemmBK][kGemmBM + 4];
     __shared__ A sb[kGemmBK][kGemmBN + 4];
+    grid_dependency_wait();  // launched with programmatic dependent launch in the project order
+    launch_dependents();
     const long long m0 = (long long)blockIdx.x * kGemmBM;
     const int n0 = blockIdx.y * kGemmBN;
     const int tid = threadIdx.x;

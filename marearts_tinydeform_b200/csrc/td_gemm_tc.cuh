@@ -71,17 +71,9 @@ __global__ void __launch_bounds__(128, 1)
         }
         mbar_init(accum, 1);
         mbar_fence_init();
-        // the first kTcStages K blocks need no free slot: start their loads before anything else
-        for (int kb = 0; kb < KB && kb < kTcStages; ++kb) {
-            unsigned char* st = smem + kb * Lay::kStageBytes;
-            mbar_arrive_expect_tx(&full[kb], Lay::kStageBytes);
-            tma_load_2d(st, &map_a, &full[kb], kb * kTcBK, int(m0));
-            tma_load_2d(st + Lay::kABytes, &map_b, &full[kb], kb * kTcBK, n0);
-        }
+        tma_prefetch_desc(&map_a);
+        tma_prefetch_desc(&map_b);
     }
-    // the tile's bias columns, staged while the loads are in flight
-    for (int i = threadIdx.x; i < BN; i += 128)
-        sbias[i] = (a.bias != nullptr && n0 + i < a.HD) ? to_acc(a.bias[n0 + i]) : 0.f;
     __syncwarp();
     if (warp == 0) {
         tmem_alloc(tmem_slot, Lay::kTmemCols);
@@ -91,10 +83,22 @@ __global__ void __launch_bounds__(128, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Everything above touches only shared memory and TMEM, so under programmatic dependent launch it overlaps the
+    // previous kernel in the stream; every global read and write comes after this wait.
+    grid_dependency_wait();
     // the sampler that follows in the project order may start its prologue now (it waits for this grid before
     // reading value)
     launch_dependents();
 
+    if (threadIdx.x == 0) {
+        // the first kTcStages K blocks need no free slot
+        for (int kb = 0; kb < KB && kb < kTcStages; ++kb) {
+            unsigned char* st = smem + kb * Lay::kStageBytes;
+            mbar_arrive_expect_tx(&full[kb], Lay::kStageBytes);
+            tma_load_2d(st, &map_a, &full[kb], kb * kTcBK, int(m0));
+            tma_load_2d(st + Lay::kABytes, &map_b, &full[kb], kb * kTcBK, n0);
+        }
+    }
     if (warp == 0 && lane == 0) {
         // TMA producer for the K blocks beyond the first kTcStages
         for (int kb = kTcStages; kb < KB; ++kb) {
@@ -122,12 +126,23 @@ __global__ void __launch_bounds__(128, 1)
         mma_commit(accum);
     }
     __syncwarp();
+    // the tile's bias columns, staged while the loads and MMAs run
+    for (int i = threadIdx.x; i < BN; i += 128)
+        sbias[i] = (a.bias != nullptr && n0 + i < a.HD) ? to_acc(a.bias[n0 + i]) : 0.f;
 
     // epilogue: thread (warp w, lane i) owns tile row 32 w + i = TMEM lane 32 w + i
     const bool ready = mbar_wait(accum, 0, kErrMmaWait);
+    __syncthreads();  // the staged bias is visible
     tc_fence_after();
     if (ready) {
         const long long row = m0 + warp * 32 + lane;
+        // where an 8-column group of this row goes: value + base + (column's head) * head_step + column's d
+        long long base = row * a.HD, head_step = a.D;
+        if (a.head_major) {
+            const long long bimg = row / a.n_tok, n = row - bimg * a.n_tok;
+            base = bimg * a.H * a.n_tok * a.D + n * a.D;
+            head_step = a.n_tok * a.D;
+        }
 #pragma unroll 1
         for (int j = 0; j < BN / 32; ++j) {
             const int col0 = n0 + 32 * j;
@@ -140,10 +155,11 @@ __global__ void __launch_bounds__(128, 1)
                 for (int g = 0; g < 4; ++g) {
                     const int col = col0 + 8 * g;
                     if (col >= a.HD) break;
+                    const int h = col / a.D, d = col - h * a.D;
                     float v[8];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[8 * g + i]) + sbias[32 * j + 8 * g + i];
-                    store16<T>(a.value + proj_offset(row, col, a.n_tok, a.HD, a.H, a.D, a.head_major), v);
+                    store16<T>(a.value + base + h * head_step + d, v);
                 }
             }
         }

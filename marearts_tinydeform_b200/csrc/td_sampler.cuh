@@ -47,6 +47,8 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_vec_kernel(const Sam
     __shared__ int s_tok[kSampleWarps][kMaxCorners];
     __shared__ CT s_wt[kSampleWarps][kMaxCorners];
 
+    // the next call's projection may be scheduled now; it waits for this grid before touching memory
+    launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long row = (long long)blockIdx.x * kSampleWarps + warp;
     const bool live = row < a.rows;  // dead warps still reach grid_dependency_wait
@@ -105,6 +107,7 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_generic_kernel(const
     __shared__ int s_tok[kSampleWarps][kMaxCorners];
     __shared__ CT s_wt[kSampleWarps][kMaxCorners];
     grid_dependency_wait();
+    launch_dependents();
     load_levels(a.shapes, a.starts, a.L, lv);
     __syncthreads();
 

@@ -96,6 +96,25 @@ int check_geometry(int64_t B, int64_t Q, int64_t N, int64_t H, int64_t L, int64_
     return TD_OK;
 }
 
+// Launch `kernel` on `stream`; with `pdl`, as a programmatic dependent launch: its CTAs may be scheduled while the
+// previous kernel in the stream is still running, and the kernel's griddepcontrol.wait (which every kernel here
+// executes before its first global memory access that could depend on earlier work) restores stream order.
+template <typename K, typename... Args>
+cudaError_t launch_kernel(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                          Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 template <typename T>
 int launch_sampler(const T* value, long long s_img, long long s_tok, long long s_head, const int64_t* shapes,
                    const int64_t* starts, const T* loc, const T* attn, T* out, int64_t B, int64_t Q, int64_t N,
@@ -115,18 +134,10 @@ int launch_sampler(const T* value, long long s_img, long long s_tok, long long s
     const unsigned grid = unsigned((a.rows + kSampleWarps - 1) / kSampleWarps);
     // Right after td_project_forward's projection kernel, launch with programmatic stream serialization: the
     // sampler's corner prologue then overlaps the projection, and it waits for it before reading value.
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kSampleWarps * 32);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = after_producer ? 1 : 0;
-    cudaError_t e = vec ? cudaLaunchKernelEx(&cfg, sample_vec_kernel<T>, a)
-                        : cudaLaunchKernelEx(&cfg, sample_generic_kernel<T>, a);
+    cudaError_t e = vec ? launch_kernel(sample_vec_kernel<T>, dim3(grid), dim3(kSampleWarps * 32), 0, stream,
+                                        after_producer, a)
+                        : launch_kernel(sample_generic_kernel<T>, dim3(grid), dim3(kSampleWarps * 32), 0, stream,
+                                        after_producer, a);
     if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "sampler launch: %s", cudaGetErrorString(e));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return check_launch(err, err_len, vec ? "sample_vec_kernel" : "sample_generic_kernel");
@@ -166,7 +177,8 @@ int launch_fused_tc_cfg(const CUtensorMap& map_w, const FusedTcArgs<T>& a, int s
     if (int rc = allow_smem(kernel, smem, smem_done, err, err_len)) return rc;
     // one persistent CTA per SM, each with an equal share of the rows
     const int grid = int(a.rows < sm_count ? a.rows : sm_count);
-    kernel<<<unsigned(grid), kFtcThreads, smem, stream>>>(map_w, a);
+    const cudaError_t e = launch_kernel(kernel, dim3(unsigned(grid)), dim3(kFtcThreads), smem, stream, true, map_w, a);
+    if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "fused_tc_kernel launch: %s", cudaGetErrorString(e));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return check_launch(err, err_len, "fused_tc_kernel");
 }
@@ -232,7 +244,9 @@ int launch_fused(const T* memory, const T* weight, const T* bias, const int64_t*
     static std::atomic<uint64_t> smem_done{0};
     if (int rc = allow_smem(fused_simt_kernel<T>, smem, smem_done, err, err_len)) return rc;
     const long long grid = B * H * (long long)a.q_tiles;
-    fused_simt_kernel<T><<<unsigned(grid), kFusedThreads, smem, stream>>>(a);
+    const cudaError_t e = launch_kernel(fused_simt_kernel<T>, dim3(unsigned(grid)), dim3(kFusedThreads), smem, stream,
+                                        true, a);
+    if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "fused_simt_kernel launch: %s", cudaGetErrorString(e));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return check_launch(err, err_len, "fused_simt_kernel");
 }
@@ -295,7 +309,8 @@ int allow_smem(K kernel, size_t bytes, std::atomic<uint64_t>& done, char* err, s
 
 template <typename T, int BN>
 int launch_proj_tc(const T* memory, const T* weight, const T* bias, T* value, int64_t M, int64_t N, int64_t C,
-                   int64_t H, int64_t HD, int head_major, cudaStream_t stream, char* err, size_t err_len) {
+                   int64_t H, int64_t HD, int head_major, cudaStream_t stream, bool pdl, char* err,
+                   size_t err_len) {
     using Lay = ProjTcLayout<BN>;
     static std::atomic<uint64_t> smem_done{0};
     CUtensorMap map_a, map_b;
@@ -306,14 +321,17 @@ int launch_proj_tc(const T* memory, const T* weight, const T* bias, T* value, in
     a.bias = bias; a.value = value; a.M = M; a.n_tok = N; a.C = int(C); a.HD = int(HD); a.H = int(H);
     a.D = int(HD / H); a.head_major = head_major; a.k_blocks = int((C + kTcBK - 1) / kTcBK);
     const dim3 grid(unsigned((M + kTcBM - 1) / kTcBM), unsigned((HD + BN - 1) / BN));
-    proj_tc_kernel<T, BN><<<grid, 128, Lay::kSmemBytes, stream>>>(map_a, map_b, a);
+    const cudaError_t e = launch_kernel(proj_tc_kernel<T, BN>, grid, dim3(128), Lay::kSmemBytes, stream, pdl, map_a,
+                                        map_b, a);
+    if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "proj_tc_kernel launch: %s", cudaGetErrorString(e));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return check_launch(err, err_len, "proj_tc_kernel");
 }
 
 template <typename T>
 int launch_proj(const T* memory, const T* weight, const T* bias, T* value, int64_t B, int64_t N, int64_t C,
-                int64_t H, int64_t HD, int head_major, cudaStream_t stream, char* err, size_t err_len) {
+                int64_t H, int64_t HD, int head_major, cudaStream_t stream, char* err, size_t err_len,
+                bool pdl = false) {
     if constexpr (std::is_same<T, __half>::value || std::is_same<T, __nv_bfloat16>::value) {
         // tcgen05 path: 16-byte aligned rows for TMA, K at least one 64-wide block, 8-column groups per head
         const int64_t D = HD / H;
@@ -325,12 +343,12 @@ int launch_proj(const T* memory, const T* weight, const T* bias, T* value, int64
             const int64_t M = B * N, m_tiles = (M + kTcBM - 1) / kTcBM;
             // one N tile when that still fills the SMs twice over; else 128 (or 64) wide tiles for more CTAs
             if (HD > 128 && HD <= 256 && m_tiles >= 2LL * f.sm_count)
-                return launch_proj_tc<T, 256>(memory, weight, bias, value, M, N, C, H, HD, head_major, stream, err,
+                return launch_proj_tc<T, 256>(memory, weight, bias, value, M, N, C, H, HD, head_major, stream, pdl, err,
                                               err_len);
             if (HD > 64)
-                return launch_proj_tc<T, 128>(memory, weight, bias, value, M, N, C, H, HD, head_major, stream, err,
+                return launch_proj_tc<T, 128>(memory, weight, bias, value, M, N, C, H, HD, head_major, stream, pdl, err,
                                               err_len);
-            return launch_proj_tc<T, 64>(memory, weight, bias, value, M, N, C, H, HD, head_major, stream, err,
+            return launch_proj_tc<T, 64>(memory, weight, bias, value, M, N, C, H, HD, head_major, stream, pdl, err,
                                          err_len);
         }
     }
@@ -339,7 +357,8 @@ int launch_proj(const T* memory, const T* weight, const T* bias, T* value, int64
     a.M = B * N; a.n_tok = N; a.C = int(C); a.HD = int(HD); a.H = int(H); a.D = int(HD / H);
     a.head_major = head_major;
     const dim3 grid(unsigned((a.M + kGemmBM - 1) / kGemmBM), unsigned((HD + kGemmBN - 1) / kGemmBN));
-    proj_simt_kernel<T><<<grid, kGemmThreads, 0, stream>>>(a);
+    const cudaError_t e = launch_kernel(proj_simt_kernel<T>, grid, dim3(kGemmThreads), 0, stream, pdl, a);
+    if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "proj_simt_kernel launch: %s", cudaGetErrorString(e));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return check_launch(err, err_len, "proj_simt_kernel");
 }
@@ -482,7 +501,7 @@ int td_project_forward(int dtype, const void* memory, const void* value_weight, 
         using T = decltype(tag);
         T* v = static_cast<T*>(value);
         if (int rc = launch_proj<T>(static_cast<const T*>(memory), static_cast<const T*>(value_weight),
-                                    static_cast<const T*>(value_bias), v, B, N, C, H, HD, 1, s, err, err_len))
+                                    static_cast<const T*>(value_bias), v, B, N, C, H, HD, 1, s, err, err_len, true))
             return rc;
         return launch_sampler<T>(v, H * N * D, D, N * D, spatial_shapes, level_start_index,
                                  static_cast<const T*>(sampling_locations), static_cast<const T*>(attention_weights),
