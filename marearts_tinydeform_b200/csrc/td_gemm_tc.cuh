@@ -1,21 +1,36 @@
-// td_gemm_tc.cuh -- value projection on tcgen05 tensor cores (float16 / bfloat16): value = memory @ W^T + b.
+// td_gemm_tc.cuh -- value projection on tcgen05 tensor cores: value = memory @ W^T + b.
 //
-// Replaces the cuBLAS F.linear of upstream's project order (marearts_tinydeform/__init__.py:77).
-// One CTA computes a 128 x BN tile of value (M = B*N tokens, N = H*D output channels, K = C):
-//   * warp 0, one thread: TMA producer -- 128 x 64 tiles of memory and BN x 64 tiles of W (128-byte swizzle,
-//     K-major) into a kStages-deep ring of shared-memory slots, each slot completed on its own mbarrier;
-//   * warp 1, one thread: MMA issuer -- four tcgen05.mma (M=128, N=BN, K=16) per 64-wide K block into a
-//     128 x BN float32 accumulator in tensor memory; a tcgen05.commit per block hands the slot back;
-//   * all four warps: epilogue -- tcgen05.ld of the thread's accumulator row (TMEM lane = tile row), + bias,
-//     narrowed to 16 bits and stored 16 bytes at a time, either as [B*N, HD] or head-major [B, H, N, D]
-//     (every 8-column group of a row lands in one head's D-row, so the stores stay 16-byte vectors).
-// Memory is read once per N tile (BN = 256 covers H*D = 256 in one tile when there are enough M tiles).
+// Replaces the cuBLAS F.linear of upstream's project order (marearts_tinydeform/__init__.py:77) for float16 and
+// bfloat16 (kind::f16) and for float32 (kind::tf32, three products per K step -- below).
+// Output tiles are 128 tokens of one image x BN channels (a tile never spans two images, so every tile is a box of
+// the [B, N, ...] tensors). Persistent and warp-specialised: each CTA walks tiles t = blockIdx.x, + gridDim.x, ...
+// (channel tiles fastest, so the CTAs that share a 128-token slice of memory run together and it is read from HBM
+// once):
+//   * warps 0-2, one thread each: TMA producers -- per tile and per 128-byte-wide K block, the 128-token slice of
+//     memory and the BN-row slice of W (K-major, 128-byte swizzle) into a ring of kStages shared-memory slots.
+//     K blocks are dealt round-robin to kProducers warps because the TMA operations of one issuing warp are served
+//     one after another (about 0.15 us each on B200, whatever their size), while those of different warps overlap.
+//     kProducers divides kStages, so every slot has one owner that fills it round after round: a parity wait on
+//     the slot's barrier can then never run two phases ahead of it;
+//   * EPI warps from warp 4 on: epilogue -- tcgen05.ld of the accumulator (TMEM lane = tile row; warp w reads
+//     lanes 32 (w % 4) .. + 31, and with 8 warps each takes half of the columns), + bias (staged in shared memory),
+//     narrowed to T and written into a staging tile laid out as the output's boxes (TMA swizzle, so the 16-byte
+//     writes of a warp hit distinct banks); the accumulator is handed back as soon as it is read, and the boxes
+//     are written with TMA tensor stores, issued by every epilogue warp in turn -- whole lines, where per-thread
+//     row stores would write half sectors. Shapes whose boxes cannot be described that way store straight from
+//     registers instead;
+//   * warp 3, one thread: MMA issuer -- four K steps per block (tcgen05.mma, M = 128, N = BN) into one of two TMEM
+//     accumulators (2 x BN float32 columns), so the epilogue of one tile runs under the MMAs of the next;
+//   * float32 only, four more warps: split -- every landed slot is rewritten as hi = x with its 13 low mantissa bits
+//     cleared (exact in TF32) and lo = x - hi in a second slot; the MMA issuer then accumulates
+//     hi*hi + hi*lo + lo*hi, which keeps about 21 bits of each product where one TF32 product keeps 11.
+// Every mbarrier wait is bounded (td_ptx.cuh): a wait that gives up records the device error word and that role
+// stops issuing work, so a broken launch ends with an error status instead of a hang.
 #pragma once
 
 #include <type_traits>
 
 #include "td_common.cuh"
-#include "td_gemm_simt.cuh"
 #include "td_ptx.cuh"
 
 namespace td {
@@ -24,55 +39,161 @@ template <typename T>
 struct ProjTcArgs {
     const T* bias;  // [HD] or null
     T* value;
-    long long M, n_tok;
+    int N;            // tokens per image
     int C, HD, H, D;
     int head_major;
-    int k_blocks;   // ceil(C / 64)
+    int k_blocks;     // ceil(C / kBK)
+    int n_tiles;      // ceil(HD / BN)
+    int m_tiles;      // ceil(N / 128): token tiles per image
+    int tiles;        // B * m_tiles * n_tiles (< 2^31)
+    // epilogue through TMA stores: boxes of `piece` columns (piece_bytes = piece * sizeof(T) in {16, 32, 64, 128})
+    // x 128 tokens, 0 = direct stores
+    int tma_store, piece, piece_bytes;
 };
 
-constexpr int kTcBM = 128, kTcBK = 64, kTcStages = 4;
+constexpr int kTcBM = 128;
+// opt-in maximum, less the alignment slack, the barriers and 12 KB left for sampler CTAs on the same SM
+constexpr int kTcSmemBudget = 232448 - 1024 - 512 - 12288;
 
-template <int BN>
+template <typename T> struct GemmKind;
+template <> struct GemmKind<__half> {
+    static constexpr int kBK = 64;  // elements of one 128-byte swizzled row
+    static constexpr bool kSplit = false;
+    static constexpr uint32_t kFormat = 0;  // A / B format field: f16
+};
+template <> struct GemmKind<__nv_bfloat16> {
+    static constexpr int kBK = 64;
+    static constexpr bool kSplit = false;
+    static constexpr uint32_t kFormat = 1;  // bf16
+};
+template <> struct GemmKind<float> {
+    static constexpr int kBK = 32;
+    static constexpr bool kSplit = true;
+    static constexpr uint32_t kFormat = 2;  // tf32
+};
+
+template <typename T, int BN, int EPI>
 struct ProjTcLayout {
-    static constexpr uint32_t kABytes = kTcBM * kTcBK * 2;  // 16 KB
-    static constexpr uint32_t kBBytes = BN * kTcBK * 2;
-    static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-    static constexpr uint32_t kTileBytes = kTcStages * kStageBytes;
-    static constexpr uint32_t kBarOffset = kTileBytes;                 // full[S], empty[S], accum
-    static constexpr uint32_t kSlotOffset = kBarOffset + (2 * kTcStages + 1) * 8;
-    static constexpr uint32_t kBiasOffset = kSlotOffset + 16;           // BN floats
-    static constexpr uint32_t kSmemBytes = kBiasOffset + BN * 4 + 1024;  // + slack to align the base to 1024
-    static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+    static constexpr bool kSplit = GemmKind<T>::kSplit;
+    static constexpr int kBK = GemmKind<T>::kBK;
+    static constexpr uint32_t kABytes = kTcBM * 128;  // 16 KB
+    static constexpr uint32_t kBBytes = BN * 128;
+    static constexpr uint32_t kStageBytes = (kABytes + kBBytes) * (kSplit ? 2 : 1);  // float32: + the lo copies
+    static constexpr uint32_t kStgBytes = kTcBM * BN * sizeof(T);  // epilogue staging tile
+    static constexpr uint32_t kBiasBytes = BN * 4;
+    static constexpr int kFit = int((kTcSmemBudget - kStgBytes - kBiasBytes) / kStageBytes);
+    // a count with a divisor among 2 / 3 / 4, so that several producer warps can share the slots
+    static constexpr int kStages = kFit >= 8 ? 8 : kFit >= 6 ? 6 : kFit >= 4 ? 4 : kFit >= 3 ? 3 : 2;
+    static constexpr uint32_t kStgOffset = kStages * kStageBytes;  // 1024-aligned: stage sizes are multiples of 1 KB
+    static constexpr uint32_t kBiasOffset = kStgOffset + kStgBytes;
+    // barriers: full[S], split[S], empty[S], tfull[2], tempty[2]
+    static constexpr uint32_t kBarOffset = kBiasOffset + kBiasBytes;
+    static constexpr uint32_t kSlotOffset = kBarOffset + (3 * kStages + 4) * 8;
+    static constexpr uint32_t kSmemBytes = kSlotOffset + 16 + 1024;  // + slack to align the base to 1024
+    static constexpr uint32_t kTmemCols = 2 * BN;
+    // warps 0 .. kProducers-1 load, warp 3 issues the MMAs, warps 4 .. 4+EPI-1 run the epilogue (a multiple of 4
+    // apart, as epilogue warp w reads TMEM lanes 32 (w % 4) ..), then the float32 split warps: whole groups of four
+    // warps, so that every SM sub-partition holds the same share of the CTA's registers
+    static constexpr int kProducers = kStages % 3 == 0 ? 3 : kStages % 2 == 0 ? 2 : 1;
+    static constexpr int kMmaWarp = 3;
+    static constexpr int kEpiWarp0 = 4;
+    static constexpr int kSplitWarp0 = kEpiWarp0 + EPI;
+    static constexpr int kThreads = 32 * (kSplitWarp0 + (kSplit ? 4 : 0));
+    static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
+    static_assert(EPI == 4 || EPI == 8, "epilogue warps");
+    static_assert(kStages >= 2, "pipeline depth");
+    static_assert(kStages % kProducers == 0, "one producer per slot");
+    static_assert(kSlotOffset + 16 <= uint32_t(kTcSmemBudget) + 512, "shared memory");
 };
 
-template <typename T, int BN>
-__global__ void __launch_bounds__(128, 1)
-    proj_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                   const ProjTcArgs<T> a) {
-    using Lay = ProjTcLayout<BN>;
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    // 1024-byte aligned base (the 128-byte swizzle pattern is anchored at 1024-byte boundaries)
-    unsigned char* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
+template <typename T>
+__device__ __forceinline__ void mma_issue(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    if constexpr (GemmKind<T>::kSplit) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+            ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(acc)
+            : "memory");
+    } else {
+        mma_f16(d, a, b, idesc, acc);
+    }
+}
+
+// hi = x with the 13 low mantissa bits cleared, lo = x - hi (exact)
+__device__ __forceinline__ void split_tf32(float4& x, float4& lo) {
+    float4 h;
+    h.x = __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
+    h.y = __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
+    h.z = __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
+    h.w = __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
+    lo = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+    x = h;
+}
+
+// 8 accumulator columns -> T, as 16-byte words (one for 16-bit types, two for float32)
+template <typename T>
+__device__ __forceinline__ void pack8(const float* f, uint4* w) {
+    if constexpr (std::is_same<T, float>::value) {
+        w[0] = make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+        w[1] = make_uint4(__float_as_uint(f[4]), __float_as_uint(f[5]), __float_as_uint(f[6]), __float_as_uint(f[7]));
+    } else {
+        uint32_t u[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if constexpr (std::is_same<T, __half>::value) {
+                const __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+                u[i] = *reinterpret_cast<const uint32_t*>(&h);
+            } else {
+                const __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+                u[i] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+        }
+        w[0] = make_uint4(u[0], u[1], u[2], u[3]);
+    }
+}
+
+// The projection tiles of this CTA, from barrier setup to TMEM release (ends with a CTA-wide barrier; every value
+// store of the CTA has completed by then). smem is the 1024-byte aligned dynamic shared memory.
+template <typename T, int BN, int EPI>
+__device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CUtensorMap& map_b,
+                                              const CUtensorMap& map_out, const ProjTcArgs<T>& a,
+                                              unsigned char* smem) {
+    using Lay = ProjTcLayout<T, BN, EPI>;
+    constexpr int S = Lay::kStages;
+    constexpr int kBK = Lay::kBK;
+    constexpr bool kSplit = Lay::kSplit;
+    constexpr int kWords = sizeof(T) == 4 ? 2 : 1;  // 16-byte words per 8 columns
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lay::kBarOffset);
-    uint64_t* empty = full + kTcStages;
-    uint64_t* accum = empty + kTcStages;
+    uint64_t* split = full + S;
+    uint64_t* empty = split + S;
+    uint64_t* tfull = empty + S;
+    uint64_t* tempty = tfull + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Lay::kSlotOffset);
+    unsigned char* stg = smem + Lay::kStgOffset;
     float* sbias = reinterpret_cast<float*>(smem + Lay::kBiasOffset);
+    // slot s: A (16 KB), B (BN x 128 B), and for float32 their lo halves after them
+    auto slot_a = [&](int s) { return smem + s * Lay::kStageBytes; };
+    auto slot_b = [&](int s) { return smem + s * Lay::kStageBytes + Lay::kABytes; };
+    auto slot_alo = [&](int s) { return smem + s * Lay::kStageBytes + Lay::kABytes + Lay::kBBytes; };
+    auto slot_blo = [&](int s) { return smem + s * Lay::kStageBytes + 2 * Lay::kABytes + Lay::kBBytes; };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long m0 = (long long)blockIdx.x * kTcBM;
-    const int n0 = blockIdx.y * BN;
-
     const int KB = a.k_blocks;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kTcStages; ++s) {
+        for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
+            mbar_init(&split[s], 4);  // one arrival per split warp
             mbar_init(&empty[s], 1);
         }
-        mbar_init(accum, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], EPI);  // one arrival per epilogue warp
+        }
         mbar_fence_init();
         tma_prefetch_desc(&map_a);
         tma_prefetch_desc(&map_b);
+        if (a.tma_store) tma_prefetch_desc(&map_out);
     }
     __syncwarp();
     if (warp == 0) {
@@ -83,6 +204,16 @@ __global__ void __launch_bounds__(128, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // tile t -> image b, first token n0, first channel c0 (32-bit: the host keeps the tile count below 2^31)
+    const int per_img = a.m_tiles * a.n_tiles;
+    auto tile_at = [&](int t, int& b, int& n0, int& c0) {
+        b = t / per_img;
+        const int r = t - b * per_img;
+        const int mt = r / a.n_tiles;
+        n0 = mt * kTcBM;
+        c0 = (r - mt * a.n_tiles) * BN;
+    };
+    const int my_tiles = a.tiles > int(blockIdx.x) ? (a.tiles - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
     // Everything above touches only shared memory and TMEM, so under programmatic dependent launch it overlaps the
     // previous kernel in the stream; every global read and write comes after this wait.
     grid_dependency_wait();
@@ -90,78 +221,195 @@ __global__ void __launch_bounds__(128, 1)
     // reading value)
     launch_dependents();
 
-    if (threadIdx.x == 0) {
-        // the first kTcStages K blocks need no free slot
-        for (int kb = 0; kb < KB && kb < kTcStages; ++kb) {
-            unsigned char* st = smem + kb * Lay::kStageBytes;
-            mbar_arrive_expect_tx(&full[kb], Lay::kStageBytes);
-            tma_load_2d(st, &map_a, &full[kb], kb * kTcBK, int(m0));
-            tma_load_2d(st + Lay::kABytes, &map_b, &full[kb], kb * kTcBK, n0);
+    if (warp < Lay::kMmaWarp) {
+        if (lane == 0 && warp < Lay::kProducers) {
+            // TMA producer `warp`: the K blocks it = warp, warp + kProducers, ... of this CTA's sequence (tile-major),
+            // which all use the slots s = warp (mod kProducers)
+            const int total = my_tiles * KB;
+            bool ok = true;
+            int it = warp;
+            for (; it < total; it += Lay::kProducers) {
+                const int tl = it / KB, kb = it - tl * KB;
+                int b, n0, c0;
+                tile_at(int(blockIdx.x) + tl * int(gridDim.x), b, n0, c0);
+                const int s = it % S;
+                if (!mbar_wait(&empty[s], uint32_t((it / S) & 1) ^ 1u, kErrSlotWait)) { ok = false; break; }
+                mbar_arrive_expect_tx(&full[s], Lay::kABytes + Lay::kBBytes);
+                tma_load_3d(slot_a(s), &map_a, &full[s], kb * kBK, n0, b);
+                tma_load_2d(slot_b(s), &map_b, &full[s], kb * kBK, c0);
+            }
+            // drain: the last use of every slot of this producer handed back, so no MMA commit is still to arrive
+            // when the CTA exits
+            for (; ok && it < total + S; it += Lay::kProducers) {
+                if (!mbar_wait(&empty[it % S], uint32_t((it / S) & 1) ^ 1u, kErrSlotWait)) ok = false;
+            }
         }
-    }
-    if (warp == 0 && lane == 0) {
-        // TMA producer for the K blocks beyond the first kTcStages
-        for (int kb = kTcStages; kb < KB; ++kb) {
-            const int s = kb % kTcStages, round = kb / kTcStages;
-            if (!mbar_wait(&empty[s], (round & 1) ^ 1, kErrSlotWait)) break;
-            unsigned char* st = smem + s * Lay::kStageBytes;
-            mbar_arrive_expect_tx(&full[s], Lay::kStageBytes);
-            tma_load_2d(st, &map_a, &full[s], kb * kTcBK, int(m0));
-            tma_load_2d(st + Lay::kABytes, &map_b, &full[s], kb * kTcBK, n0);
-        }
-    } else if (warp == 1 && lane == 0) {
-        // MMA issuer
-        constexpr uint32_t idesc = idesc_f16(std::is_same<T, __nv_bfloat16>::value, kTcBM, BN);
-        for (int kb = 0; kb < KB; ++kb) {
-            const int s = kb % kTcStages, round = kb / kTcStages;
-            if (!mbar_wait(&full[s], round & 1, kErrTmaWait)) break;
-            tc_fence_after();
-            const uint32_t sa = smem_addr(smem + s * Lay::kStageBytes);
-            const uint64_t da = sdesc_sw128(sa), db = sdesc_sw128(sa + Lay::kABytes);
+    } else if (warp == Lay::kMmaWarp) {
+        if (lane == 0) {
+            // MMA issuer. Instruction descriptor: f32 accumulator [4,6), A / B format [7,10) / [10,13), both K-major,
+            // N >> 3 at [17,23), M >> 4 at [24,29).
+            constexpr uint32_t idesc = (1u << 4) | (GemmKind<T>::kFormat << 7) | (GemmKind<T>::kFormat << 10) |
+                                       (uint32_t(BN >> 3) << 17) | (uint32_t(kTcBM >> 4) << 24);
+            int it = 0;
+            bool ok = true;
+            for (int tc = 0; ok && tc < my_tiles; ++tc) {
+                const int acc = tc & 1;
+                if (!mbar_wait(&tempty[acc], uint32_t((tc >> 1) & 1) ^ 1u, kErrSlotWait)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + uint32_t(acc * BN);
+                for (int kb = 0; kb < KB; ++kb, ++it) {
+                    const int s = it % S;
+                    if (!mbar_wait(kSplit ? &split[s] : &full[s], uint32_t((it / S) & 1), kErrTmaWait)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t da = sdesc_sw128(smem_addr(slot_a(s)));
+                    const uint64_t db = sdesc_sw128(smem_addr(slot_b(s)));
 #pragma unroll
-            for (int k = 0; k < kTcBK / 16; ++k)  // K = 16 per MMA = 32 bytes along the swizzled row
-                mma_f16(tmem, da + uint64_t(2 * k), db + uint64_t(2 * k), idesc, (kb | k) != 0);
-            mma_commit(&empty[s]);
+                    for (int k = 0; k < 4; ++k) {  // 4 K steps of 32 bytes per 128-byte row
+                        const uint64_t kofs = uint64_t(2 * k);
+                        mma_issue<T>(d, da + kofs, db + kofs, idesc, (kb | k) != 0);
+                        if constexpr (kSplit) {
+                            const uint64_t dal = sdesc_sw128(smem_addr(slot_alo(s)));
+                            const uint64_t dbl = sdesc_sw128(smem_addr(slot_blo(s)));
+                            mma_issue<T>(d, da + kofs, dbl + kofs, idesc, 1u);
+                            mma_issue<T>(d, dal + kofs, db + kofs, idesc, 1u);
+                        }
+                    }
+                    mma_commit(&empty[s]);
+                }
+                if (ok) mma_commit(&tfull[acc]);
+            }
         }
-        mma_commit(accum);
-    }
-    __syncwarp();
-    // the tile's bias columns, staged while the loads and MMAs run
-    for (int i = threadIdx.x; i < BN; i += 128)
-        sbias[i] = (a.bias != nullptr && n0 + i < a.HD) ? to_acc(a.bias[n0 + i]) : 0.f;
-
-    // epilogue: thread (warp w, lane i) owns tile row 32 w + i = TMEM lane 32 w + i
-    const bool ready = mbar_wait(accum, 0, kErrMmaWait);
-    __syncthreads();  // the staged bias is visible
-    tc_fence_after();
-    if (ready) {
-        const long long row = m0 + warp * 32 + lane;
-        // where an 8-column group of this row goes: value + base + (column's head) * head_step + column's d
-        long long base = row * a.HD, head_step = a.D;
-        if (a.head_major) {
-            const long long bimg = row / a.n_tok, n = row - bimg * a.n_tok;
-            base = bimg * a.H * a.n_tok * a.D + n * a.D;
-            head_step = a.n_tok * a.D;
-        }
+    } else if (warp >= Lay::kEpiWarp0 && warp < Lay::kSplitWarp0) {
+        // epilogue
+        constexpr int kEpiThreads = EPI * 32;
+        const int etid = threadIdx.x - 32 * Lay::kEpiWarp0;
+        const int ew = warp - Lay::kEpiWarp0;  // stores of boxes ew, ew + EPI, ... are this warp's
+        const int quarter = warp & 3;
+        constexpr int kCols = EPI == 8 ? BN / 2 : BN;  // columns this warp converts
+        const int c_lo = EPI == 8 ? (ew >> 2) * kCols : 0;
+        const int r = quarter * 32 + lane;  // tile row = TMEM lane
+        const int pb = a.piece_bytes;
+        const int pshift = 31 - __clz(a.piece);  // piece is a power of two
+        const int swz = pb / 16 - 1;             // 16-byte chunk index ^= (row * pb / 128) & swz
+        // After a wait that gave up, a warp still walks its tiles and takes part in every named barrier (so no
+        // other epilogue warp waits on it), but reads no TMEM and stores nothing.
+        bool dead = false;
+        // tc = -1 is a dry pass: the code below runs once on zeros into the staging tile, storing nothing, while the
+        // first tile's loads are in flight -- so that its instructions are already cached when the tile is ready
+        // (a first pass through cold code costs about as much as the loads).
+        for (int tc = -1; tc < my_tiles; ++tc) {
+            const bool dry = tc < 0;
+            const int acc = tc & 1;
+            int b, n0, c0;
+            tile_at(int(blockIdx.x) + (dry ? 0 : tc) * int(gridDim.x), b, n0, c0);
+            // this tile's bias; the previous tile's readers are past its second barrier
+            for (int i = etid; i < BN; i += kEpiThreads)
+                sbias[i] = (a.bias != nullptr && c0 + i < a.HD) ? to_acc(a.bias[c0 + i]) : 0.f;
+            // the staging tile is free once the previous tile's stores have read it
+            if (lane == 0 && a.tma_store) bulk_wait_read();
+            named_barrier(1, kEpiThreads);
+            bool ready = dry || (!dead && mbar_wait(&tfull[acc], uint32_t((tc >> 1) & 1), kErrMmaWait));
+            ready = __all_sync(0xffffffffu, ready);
+            dead = !ready;
+            tc_fence_after();
+            const int n = n0 + r;
+            const long long m = (long long)b * a.N + n;
 #pragma unroll 1
-        for (int j = 0; j < BN / 32; ++j) {
-            const int col0 = n0 + 32 * j;
-            if (col0 >= a.HD) break;  // uniform across the warp
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(32 * j), r);
-            tmem_ld_wait();
-            if (row < a.M) {
+            for (int j = 0; j < kCols / 32; ++j) {
+                const int cl = c_lo + 32 * j;  // tile column of this chunk
+                const bool live = ready && c0 + cl < a.HD;  // uniform across the warp
+                uint32_t v[32];
+                if (live && !dry) {
+                    tmem_ld_32x32b_x32(tmem + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN + cl), v);
+                    tmem_ld_wait();
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = 0u;
+                }
+                if (j == kCols / 32 - 1 && !dry) {
+                    // every column of this warp is in registers: hand the accumulator back
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[acc]);
+                }
+                if (!live) continue;
 #pragma unroll
                 for (int g = 0; g < 4; ++g) {
-                    const int col = col0 + 8 * g;
-                    if (col >= a.HD) break;
-                    const int h = col / a.D, d = col - h * a.D;
-                    float v[8];
+                    const int c = cl + 8 * g;  // tile column
+                    float f[8];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[8 * g + i]) + sbias[32 * j + 8 * g + i];
-                    store16<T>(a.value + base + h * head_step + d, v);
+                    for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(v[8 * g + i]) + sbias[c + i];
+                    uint4 w[kWords];
+                    pack8<T>(f, w);
+                    if (a.tma_store) {
+                        // piece p = c / piece, 16-byte chunk q within the piece's row r
+                        const int p = c >> pshift, q = ((c - (p << pshift)) * int(sizeof(T))) >> 4;
+                        unsigned char* row = stg + p * (kTcBM * pb) + r * pb;
+                        const int x = (r * pb >> 7) & swz;
+#pragma unroll
+                        for (int k = 0; k < kWords; ++k) *reinterpret_cast<uint4*>(row + (((q + k) ^ x) << 4)) = w[k];
+                    } else if (!dry && n < a.N && c0 + c < a.HD) {
+                        const int col = c0 + c, h = col / a.D;
+                        T* dst = a.head_major
+                                     ? a.value + (((long long)b * a.H + h) * a.N + n) * a.D + (col - h * a.D)
+                                     : a.value + m * a.HD + col;
+#pragma unroll
+                        for (int k = 0; k < kWords; ++k) reinterpret_cast<uint4*>(dst)[k] = w[k];
+                    }
                 }
             }
+            if (a.tma_store) {
+                fence_proxy_async_smem();  // the TMA stores (async proxy) read what these threads wrote
+                named_barrier(1, kEpiThreads);
+                if (lane == 0 && ready && !dry) {
+                    for (int p = ew; p < (BN >> pshift); p += EPI) {
+                        const int col = c0 + (p << pshift);
+                        if (col >= a.HD) break;
+                        const unsigned char* src = stg + p * (kTcBM * pb);
+                        if (a.head_major) {
+                            const int h = col / a.D;
+                            tma_store_3d(&map_out, src, col - h * a.D, n0, b * a.H + h);
+                        } else {
+                            tma_store_3d(&map_out, src, col, n0, b);
+                        }
+                    }
+                    bulk_commit();
+                }
+            }
+        }
+        if (lane == 0 && a.tma_store) bulk_wait_all();
+    } else if (kSplit && warp >= Lay::kSplitWarp0) {
+        // float32: split every landed slot into hi (in place) and lo
+        const int tid = (warp - Lay::kSplitWarp0) * 32 + lane;  // 128 threads
+        const int total = my_tiles * KB;
+        for (int it = 0; it < total; ++it) {
+            const int s = it % S;
+            const bool landed = mbar_wait(&full[s], uint32_t((it / S) & 1), kErrTmaWait);
+            if (!__all_sync(0xffffffffu, landed)) break;  // warp-uniform, for the __syncwarp below
+            float4* x = reinterpret_cast<float4*>(slot_a(s));
+            float4* xl = reinterpret_cast<float4*>(slot_alo(s));
+#pragma unroll 4
+            for (int i = tid; i < int(Lay::kABytes / 16); i += 128) {
+                float4 v = x[i], lo;
+                split_tf32(v, lo);
+                x[i] = v;
+                xl[i] = lo;
+            }
+            x = reinterpret_cast<float4*>(slot_b(s));
+            xl = reinterpret_cast<float4*>(slot_blo(s));
+#pragma unroll 4
+            for (int i = tid; i < int(Lay::kBBytes / 16); i += 128) {
+                float4 v = x[i], lo;
+                split_tf32(v, lo);
+                x[i] = v;
+                xl[i] = lo;
+            }
+            fence_proxy_async_smem();  // the MMAs (async proxy) read what these threads wrote
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&split[s]);
         }
     }
     tc_fence_before();
@@ -170,6 +418,20 @@ __global__ void __launch_bounds__(128, 1)
         tc_fence_after();
         tmem_dealloc(tmem, Lay::kTmemCols);
     }
+}
+
+__device__ __forceinline__ unsigned char* align1024(unsigned char* p) {
+    return p + ((1024 - (smem_addr(p) & 1023)) & 1023);
+}
+
+// 72 registers a thread (no spills): 12 warps, 3 per SM sub-partition (27 K registers), leave room on the SM for two
+// CTAs of the sampler that follows in the project order (launched early, under programmatic dependent launch).
+template <typename T, int BN, int EPI>
+__global__ void __maxnreg__(72)
+    proj_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                   const __grid_constant__ CUtensorMap map_out, const ProjTcArgs<T> a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    proj_tc_tiles<T, BN, EPI>(map_a, map_b, map_out, a, align1024(smem_raw));
 }
 
 }  // namespace td

@@ -33,40 +33,49 @@ struct SampleArgs {
 
 constexpr int kSampleWarps = 8;
 
-// Vector kernel: needs D * sizeof(T) % 16 == 0, D * sizeof(T) <= 512, 16-byte aligned value/out and strides.
-// The dependent-latency chain is kept to two memory round trips: (level geometry + locations + attention weights,
-// all issued together) -> corners -> (every corner row of the lane's group issued together) -> butterfly -> store.
-// When launched with programmatic serialization right after the projection kernel, everything before
-// grid_dependency_wait() overlaps that kernel; value is only read after it.
+// what a corner outside the map reads (16 bytes of zeros)
+__device__ __align__(16) const uint4 g_zero16 = {0u, 0u, 0u, 0u};
+
+// Dynamic shared memory of the vector kernel: per warp, S = 4 L P corner tokens and weights.
 template <typename T>
-__global__ void __launch_bounds__(kSampleWarps * 32) sample_vec_kernel(const SampleArgs<T> a) {
-    using A = typename Elem<T>::acc;
+__host__ __device__ inline size_t sample_vec_smem(int L, int P) {
+    return size_t(kSampleWarps) * 4 * L * P * (sizeof(int) + sizeof(typename Coord<T>::type));
+}
+
+// The corners of one (batch, query, head) row into the warp's s_tok / s_wt (lanes over the L x P points).
+template <typename T>
+__device__ __forceinline__ void sample_row_corners(const SampleArgs<T>& a, long long row, int lane, int* s_tok,
+                                                   typename Coord<T>::type* s_wt) {
     using CT = typename Coord<T>::type;
+    const int LP = a.L * a.P;
+    for (int j = lane; j < LP; j += 32) {
+        const Level lv = level_at(a.shapes, a.starts, j / a.P);
+        const long long i = row * LP + j;
+        corners4<CT>(CT(to_acc(a.loc[2 * i])), CT(to_acc(a.loc[2 * i + 1])), CT(to_acc(a.attn[i])), lv, a.n_tok,
+                     &s_tok[4 * j], &s_wt[4 * j]);
+    }
+}
+
+// out[row] = sum over the row's corners of weight * value[token] (head slice): G lanes per corner row, 16-byte
+// vectors, kBatch corner rows in flight per lane, groups summed with an xor butterfly. kCoherent reads value
+// through L2 only (ld.global.cg), for a value written earlier by the same kernel.
+template <typename T, bool kCoherent>
+__device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long long row, int lane, const int* s_tok,
+                                                  const typename Coord<T>::type* s_wt) {
+    using A = typename Elem<T>::acc;
     constexpr int V = Elem<T>::kVec;
     constexpr int kBatch = 8;  // corner rows in flight per lane
-    __shared__ int s_tok[kSampleWarps][kMaxCorners];
-    __shared__ CT s_wt[kSampleWarps][kMaxCorners];
-
-    // the next call's projection may be scheduled now; it waits for this grid before touching memory
-    launch_dependents();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long row = (long long)blockIdx.x * kSampleWarps + warp;
-    const bool live = row < a.rows;  // dead warps still reach grid_dependency_wait
-    const int LP = a.L * a.P, S = 4 * LP;
-    if (live) {
-        for (int j = lane; j < LP; j += 32) {
-            const Level lv = level_at(a.shapes, a.starts, j / a.P);
-            const long long i = row * LP + j;
-            corners4<CT>(CT(to_acc(a.loc[2 * i])), CT(to_acc(a.loc[2 * i + 1])), CT(to_acc(a.attn[i])), lv, a.n_tok,
-                         &s_tok[warp][4 * j], &s_wt[warp][4 * j]);
-        }
+    const int S = 4 * a.L * a.P;
+    int h;
+    long long b;
+    if (a.rows < (1LL << 31)) {  // 32-bit divisions where the row index allows
+        const unsigned r = unsigned(row);
+        h = int(r % unsigned(a.H));
+        b = r / (unsigned(a.Q) * unsigned(a.H));
+    } else {
+        h = int(row % a.H);
+        b = row / ((long long)a.Q * a.H);
     }
-    __syncwarp();
-    grid_dependency_wait();
-    if (!live) return;
-
-    const int h = int(row % a.H);
-    const long long b = row / ((long long)a.Q * a.H);
     const T* vb = a.value + b * a.s_img + (long long)h * a.s_head;
     const int G = a.G, CG = 32 / G, cg = lane / G, v = lane - cg * G;
     A acc[V];
@@ -75,13 +84,15 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_vec_kernel(const Sam
     for (int s0 = cg; s0 < S; s0 += kBatch * CG) {
         uint4 raw[kBatch];
         A w[kBatch];
+        // every load of the batch is issued unconditionally (no branch between them, so they are all in flight
+        // together): a corner outside the map, or past the row's last, reads a 16-byte word of zeros
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
             const int s = s0 + u * CG;
-            const int t = s < S ? s_tok[warp][s] : -1;
-            w[u] = s < S ? A(s_wt[warp][s]) : A(0);
-            raw[u] = t >= 0 ? __ldg(reinterpret_cast<const uint4*>(vb + (long long)t * a.s_tok + v * V))
-                            : make_uint4(0, 0, 0, 0);
+            const int t = s < S ? s_tok[s] : -1;
+            w[u] = t < 0 ? A(0) : A(s_wt[s]);
+            const uint4* src = t < 0 ? &g_zero16 : reinterpret_cast<const uint4*>(vb + (long long)t * a.s_tok + v * V);
+            raw[u] = kCoherent ? __ldcg(src) : __ldg(src);
         }
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
@@ -96,6 +107,33 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_vec_kernel(const Sam
         for (int i = 0; i < V; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
     }
     if (cg == 0) store16<T>(a.out + row * a.D + v * V, acc);
+}
+
+// Vector kernel: needs D * sizeof(T) % 16 == 0, D * sizeof(T) <= 512, 16-byte aligned value/out and strides.
+// The dependent-latency chain is kept to two memory round trips: (level geometry + locations + attention weights,
+// all issued together) -> corners -> (every corner row of the lane's group issued together) -> butterfly -> store.
+// When launched with programmatic serialization right after the projection kernel, everything before
+// grid_dependency_wait() overlaps that kernel; value is only read after it.
+template <typename T>
+__global__ void __launch_bounds__(kSampleWarps * 32) sample_vec_kernel(const SampleArgs<T> a) {
+    using CT = typename Coord<T>::type;
+    // per warp: S corner tokens, then S corner weights (dynamic, sample_vec_smem bytes, so that the CTAs stay small
+    // enough to become resident beside a running projection kernel)
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+
+    // the next call's projection may be scheduled now; it waits for this grid before touching memory
+    launch_dependents();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long row = (long long)blockIdx.x * kSampleWarps + warp;
+    const bool live = row < a.rows;  // dead warps still reach grid_dependency_wait
+    const int S = 4 * a.L * a.P;
+    int* s_tok = reinterpret_cast<int*>(smem_raw) + warp * S;
+    CT* s_wt = reinterpret_cast<CT*>(smem_raw + kSampleWarps * S * sizeof(int)) + warp * S;
+    if (live) sample_row_corners<T>(a, row, lane, s_tok, s_wt);
+    __syncwarp();
+    grid_dependency_wait();
+    if (!live) return;
+    sample_row_gather<T, false>(a, row, lane, s_tok, s_wt);
 }
 
 // Generic kernel: lanes over the head's D channels, scalar loads.

@@ -134,8 +134,8 @@ int launch_sampler(const T* value, long long s_img, long long s_tok, long long s
     const unsigned grid = unsigned((a.rows + kSampleWarps - 1) / kSampleWarps);
     // Right after td_project_forward's projection kernel, launch with programmatic stream serialization: the
     // sampler's corner prologue then overlaps the projection, and it waits for it before reading value.
-    cudaError_t e = vec ? launch_kernel(sample_vec_kernel<T>, dim3(grid), dim3(kSampleWarps * 32), 0, stream,
-                                        after_producer, a)
+    cudaError_t e = vec ? launch_kernel(sample_vec_kernel<T>, dim3(grid), dim3(kSampleWarps * 32),
+                                        sample_vec_smem<T>(int(L), int(P)), stream, after_producer, a)
                         : launch_kernel(sample_generic_kernel<T>, dim3(grid), dim3(kSampleWarps * 32), 0, stream,
                                         after_producer, a);
     if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "sampler launch: %s", cudaGetErrorString(e));
@@ -144,7 +144,7 @@ int launch_sampler(const T* value, long long s_img, long long s_tok, long long s
 }
 
 int tensor_map_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows, char* err,
-                  size_t err_len);
+                  size_t err_len, uint32_t elem_bytes = 2);
 template <typename K>
 int allow_smem(K kernel, size_t bytes, std::atomic<uint64_t>& done, char* err, size_t err_len);
 
@@ -265,19 +265,38 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// 2-D row-major tensor of 16-bit elements [rows, cols], 128-byte-swizzled boxes of box_rows x 64 elements.
+// 2-D row-major tensor [rows, cols] of 16-bit (or 32-bit) elements, 128-byte-swizzled boxes of box_rows rows x
+// 128 bytes (64 or 32 elements).
 int tensor_map_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows, char* err,
-                  size_t err_len) {
+                  size_t err_len, uint32_t elem_bytes) {
     auto encode = tensor_map_encoder();
     if (encode == nullptr) return fail(err, err_len, TD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     const cuuint64_t dims[2] = {cols, rows};
-    const cuuint64_t strides[1] = {cols * 2};
-    const cuuint32_t box[2] = {uint32_t(kTcBK), box_rows};
+    const cuuint64_t strides[1] = {cols * elem_bytes};
+    const cuuint32_t box[2] = {128u / elem_bytes, box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+    const CUtensorMapDataType type = elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+    const CUresult r = encode(map, type, 2, const_cast<void*>(base), dims, strides, box, estr,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(err, err_len, TD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+    return TD_OK;
+}
+
+// 3-D tensor (x innermost) of 16- or 32-bit elements with byte strides for y and z, boxes of box[0..2] elements and
+// the given shared-memory swizzle.
+int tensor_map_3d(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
+                  const uint32_t box[3], uint32_t elem_bytes, CUtensorMapSwizzle swizzle, char* err, size_t err_len) {
+    auto encode = tensor_map_encoder();
+    if (encode == nullptr) return fail(err, err_len, TD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    const cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+    const cuuint64_t st[2] = {strides[0], strides[1]};
+    const cuuint32_t bx[3] = {box[0], box[1], box[2]};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUtensorMapDataType type = elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+    const CUresult r = encode(map, type, 3, const_cast<void*>(base), d, st, bx, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(err, err_len, TD_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d)", int(r));
     return TD_OK;
 }
 
@@ -307,49 +326,156 @@ int allow_smem(K kernel, size_t bytes, std::atomic<uint64_t>& done, char* err, s
     return TD_OK;
 }
 
-template <typename T, int BN>
-int launch_proj_tc(const T* memory, const T* weight, const T* bias, T* value, int64_t M, int64_t N, int64_t C,
+// Tensor maps and arguments of the tcgen05 projection kernel.
+template <typename T, int BN, int EPI>
+int prepare_proj_tc(const T* memory, const T* weight, const T* bias, T* value, int64_t B, int64_t N, int64_t C,
+                    int64_t H, int64_t HD, int head_major, CUtensorMap* map_a, CUtensorMap* map_b,
+                    CUtensorMap* map_out, ProjTcArgs<T>* args, char* err, size_t err_len) {
+    using Lay = ProjTcLayout<T, BN, EPI>;
+    constexpr uint32_t e = sizeof(T);
+    const int64_t D = HD / H;
+    {
+        // memory as [B][N][C]: 128-token boxes never cross into the next image (rows past N read as zeros)
+        const uint64_t dims[3] = {uint64_t(C), uint64_t(N), uint64_t(B)};
+        const uint64_t strides[2] = {uint64_t(C) * e, uint64_t(N * C) * e};
+        const uint32_t box[3] = {128u / e, uint32_t(kTcBM), 1u};
+        if (int rc = tensor_map_3d(map_a, memory, dims, strides, box, e, CU_TENSOR_MAP_SWIZZLE_128B, err, err_len))
+            return rc;
+    }
+    if (int rc = tensor_map_2d(map_b, weight, uint64_t(C), uint64_t(HD), BN, err, err_len, e)) return rc;
+    // Epilogue boxes: `piece` columns x 128 tokens. Head-major value [B, H, N, D]: a piece is a head, or a 128-byte
+    // part of one; [B, N, HD]: 128-byte column groups. The row of a box must be 16, 32, 64 or 128 bytes (the TMA
+    // swizzle widths that keep the staging writes free of bank conflicts).
+    int piece = 0;
+    if (head_major) {
+        const int64_t db = D * e;
+        if (db == 16 || db == 32 || db == 64 || db == 128) piece = int(D);
+        else if (db % 128 == 0) piece = int(128 / e);
+    } else {
+        piece = int(128 / e);
+    }
+    const int piece_bytes = piece * int(e);
+    *map_out = *map_b;  // unused when the epilogue stores directly
+    if (piece) {
+        const CUtensorMapSwizzle sw = piece_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                      : piece_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                      : piece_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                          : CU_TENSOR_MAP_SWIZZLE_NONE;
+        const uint32_t box[3] = {uint32_t(piece), uint32_t(kTcBM), 1u};
+        if (head_major) {
+            const uint64_t dims[3] = {uint64_t(D), uint64_t(N), uint64_t(B * H)};
+            const uint64_t strides[2] = {uint64_t(D) * e, uint64_t(N * D) * e};
+            if (int rc = tensor_map_3d(map_out, value, dims, strides, box, e, sw, err, err_len)) return rc;
+        } else {
+            const uint64_t dims[3] = {uint64_t(HD), uint64_t(N), uint64_t(B)};
+            const uint64_t strides[2] = {uint64_t(HD) * e, uint64_t(N * HD) * e};
+            if (int rc = tensor_map_3d(map_out, value, dims, strides, box, e, sw, err, err_len)) return rc;
+        }
+    }
+    ProjTcArgs<T>& a = *args;
+    a.bias = bias; a.value = value; a.N = int(N); a.C = int(C); a.HD = int(HD); a.H = int(H); a.D = int(D);
+    a.head_major = head_major;
+    a.k_blocks = int((C + Lay::kBK - 1) / Lay::kBK);
+    a.n_tiles = int((HD + BN - 1) / BN);
+    a.m_tiles = int((N + kTcBM - 1) / kTcBM);
+    a.tiles = int(B * a.m_tiles * a.n_tiles);
+    a.tma_store = piece != 0; a.piece = piece ? piece : 8; a.piece_bytes = piece ? piece_bytes : 16;
+    return TD_OK;
+}
+
+template <typename T, int BN, int EPI>
+int launch_proj_tc(const T* memory, const T* weight, const T* bias, T* value, int64_t B, int64_t N, int64_t C,
                    int64_t H, int64_t HD, int head_major, cudaStream_t stream, bool pdl, char* err,
                    size_t err_len) {
-    using Lay = ProjTcLayout<BN>;
+    using Lay = ProjTcLayout<T, BN, EPI>;
     static std::atomic<uint64_t> smem_done{0};
-    CUtensorMap map_a, map_b;
-    if (int rc = tensor_map_2d(&map_a, memory, uint64_t(C), uint64_t(M), kTcBM, err, err_len)) return rc;
-    if (int rc = tensor_map_2d(&map_b, weight, uint64_t(C), uint64_t(HD), BN, err, err_len)) return rc;
-    if (int rc = allow_smem(proj_tc_kernel<T, BN>, Lay::kSmemBytes, smem_done, err, err_len)) return rc;
+    DeviceFacts f;
+    if (int rc = device_facts(&f, err, err_len)) return rc;
+    CUtensorMap map_a, map_b, map_out;
     ProjTcArgs<T> a;
-    a.bias = bias; a.value = value; a.M = M; a.n_tok = N; a.C = int(C); a.HD = int(HD); a.H = int(H);
-    a.D = int(HD / H); a.head_major = head_major; a.k_blocks = int((C + kTcBK - 1) / kTcBK);
-    const dim3 grid(unsigned((M + kTcBM - 1) / kTcBM), unsigned((HD + BN - 1) / BN));
-    const cudaError_t e = launch_kernel(proj_tc_kernel<T, BN>, grid, dim3(128), Lay::kSmemBytes, stream, pdl, map_a,
-                                        map_b, a);
-    if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "proj_tc_kernel launch: %s", cudaGetErrorString(e));
+    if (int rc = prepare_proj_tc<T, BN, EPI>(memory, weight, bias, value, B, N, C, H, HD, head_major, &map_a, &map_b,
+                                             &map_out, &a, err, err_len))
+        return rc;
+    if (int rc = allow_smem(proj_tc_kernel<T, BN, EPI>, Lay::kSmemBytes, smem_done, err, err_len)) return rc;
+    // persistent: at most one CTA per SM (the slot ring takes most of the shared memory)
+    const int grid = a.tiles < f.sm_count ? a.tiles : f.sm_count;
+    const cudaError_t err_launch = launch_kernel(proj_tc_kernel<T, BN, EPI>, dim3(unsigned(grid)), dim3(Lay::kThreads),
+                                                 Lay::kSmemBytes, stream, pdl, map_a, map_b, map_out, a);
+    if (err_launch != cudaSuccess)
+        return fail(err, err_len, TD_ERR_CUDA, "proj_tc_kernel launch: %s", cudaGetErrorString(err_launch));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return check_launch(err, err_len, "proj_tc_kernel");
+}
+
+#ifndef TD_PROJ_TILE
+#define TD_PROJ_TILE 0  // 0: pick the tile width from the shape; 64 / 128 / 256 force one (for tuning builds)
+#endif
+
+template <typename T>
+constexpr bool kTcType = std::is_same<T, __half>::value || std::is_same<T, __nv_bfloat16>::value ||
+                         std::is_same<T, float>::value;
+
+// tcgen05 projection: 16-byte aligned rows for TMA, K at least one 128-byte block, 8-column groups per head, and
+// every count of 128 x 64 tiles and K blocks below 2^31 (the kernel indexes them in 32 bits)
+template <typename T>
+bool proj_tc_eligible(const T* memory, const T* weight, const T* value, int64_t B, int64_t N, int64_t C, int64_t H,
+                      int64_t HD) {
+    if constexpr (!kTcType<T>) {
+        return false;
+    } else {
+        constexpr int kBK = GemmKind<T>::kBK;
+        const int64_t D = HD / H;
+        return g_policy.load(std::memory_order_relaxed) == TD_POLICY_BEST && C >= kBK &&
+               (C * int64_t(sizeof(T))) % 16 == 0 && HD % 16 == 0 && D % 8 == 0 && N < (int64_t(1) << 31) &&
+               B < (int64_t(1) << 31) / H &&
+               B * ((N + kTcBM - 1) / kTcBM) * ((HD + 63) / 64) * ((C + kBK - 1) / kBK) < (int64_t(1) << 31) &&
+               aligned16(memory) && aligned16(weight) && aligned16(value);
+    }
+}
+
+// Tile width of the tcgen05 projection: the busiest CTA runs ceil(tiles / SMs) tiles, each costing about the load
+// of its 128 memory rows (like 128 more output columns) plus BN output columns; the width that makes that smallest,
+// the widest of equals. float32 tiles are at most 128 wide (their slots hold hi and lo halves).
+template <typename T>
+int proj_tile_width(int64_t B, int64_t N, int64_t HD, int sm_count) {
+    if (TD_PROJ_TILE != 0) return TD_PROJ_TILE;
+    const int64_t m_tiles = B * ((N + kTcBM - 1) / kTcBM);
+    int bn = 64;
+    long long best = -1;
+    for (int w : {256, 128, 64}) {
+        if (std::is_same<T, float>::value && w > 128) continue;
+        const long long tiles = m_tiles * ((HD + w - 1) / w);
+        const long long cost = (tiles + sm_count - 1) / sm_count * (w + 128);
+        if (best < 0 || cost < best) { best = cost; bn = w; }
+    }
+    return bn;
+}
+
+// Calls f(std::integral_constant<int, BN>, std::integral_constant<int, EPI>) for the instantiated tile shape of bn.
+template <typename T, typename F>
+int with_tile(int bn, F&& f) {
+    if constexpr (std::is_same<T, float>::value) {
+        if (bn >= 128) return f(std::integral_constant<int, 128>{}, std::integral_constant<int, 4>{});
+        return f(std::integral_constant<int, 64>{}, std::integral_constant<int, 4>{});
+    } else {
+        if (bn == 256) return f(std::integral_constant<int, 256>{}, std::integral_constant<int, 8>{});
+        if (bn == 128) return f(std::integral_constant<int, 128>{}, std::integral_constant<int, 8>{});
+        return f(std::integral_constant<int, 64>{}, std::integral_constant<int, 4>{});
+    }
 }
 
 template <typename T>
 int launch_proj(const T* memory, const T* weight, const T* bias, T* value, int64_t B, int64_t N, int64_t C,
                 int64_t H, int64_t HD, int head_major, cudaStream_t stream, char* err, size_t err_len,
                 bool pdl = false) {
-    if constexpr (std::is_same<T, __half>::value || std::is_same<T, __nv_bfloat16>::value) {
-        // tcgen05 path: 16-byte aligned rows for TMA, K at least one 64-wide block, 8-column groups per head
-        const int64_t D = HD / H;
-        const bool tc = g_policy.load(std::memory_order_relaxed) == TD_POLICY_BEST && C >= kTcBK && C % 8 == 0 &&
-                        HD % 16 == 0 && D % 8 == 0 && aligned16(memory) && aligned16(weight) && aligned16(value);
-        if (tc) {
+    if constexpr (kTcType<T>) {
+        if (proj_tc_eligible<T>(memory, weight, value, B, N, C, H, HD)) {
             DeviceFacts f;
             if (int rc = device_facts(&f, err, err_len)) return rc;
-            const int64_t M = B * N, m_tiles = (M + kTcBM - 1) / kTcBM;
-            // one N tile when that still fills the SMs twice over; else 128 (or 64) wide tiles for more CTAs
-            if (HD > 128 && HD <= 256 && m_tiles >= 2LL * f.sm_count)
-                return launch_proj_tc<T, 256>(memory, weight, bias, value, M, N, C, H, HD, head_major, stream, pdl, err,
-                                              err_len);
-            if (HD > 64)
-                return launch_proj_tc<T, 128>(memory, weight, bias, value, M, N, C, H, HD, head_major, stream, pdl, err,
-                                              err_len);
-            return launch_proj_tc<T, 64>(memory, weight, bias, value, M, N, C, H, HD, head_major, stream, pdl, err,
-                                         err_len);
+            return with_tile<T>(proj_tile_width<T>(B, N, HD, f.sm_count), [&](auto bn, auto epi) {
+                return launch_proj_tc<T, decltype(bn)::value, decltype(epi)::value>(
+                    memory, weight, bias, value, B, N, C, H, HD, head_major, stream, pdl, err, err_len);
+            });
         }
     }
     ProjArgs<T> a;

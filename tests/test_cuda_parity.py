@@ -279,6 +279,32 @@ def test_tensor_core_shapes(policy):
                   *TOL[dtype])
 
 
+def test_value_proj_tile_widths(cuda):
+    """The persistent tcgen05 projection at every tile width it picks (64 / 128 / 256 columns; float32 on the
+    three-product TF32 path), with more tiles than SMs so every CTA walks several, ragged last row and column
+    tiles and a K that is not a multiple of the 128-byte block; plain and head-major layouts."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    g = torch.Generator().manual_seed(11)
+    M = 128 * (sms + 1) + 37  # more 128-row tiles than SMs: the widest tile is picked
+    for dtype in (torch.float32, torch.float16, torch.bfloat16):
+        for HD, H, C in ((256, 8, 256), (192, 4, 200), (128, 4, 96), (96, 2, 64), (64, 8, 72)):
+            if dtype == torch.float32 and C % 4:
+                continue
+            mem = (torch.rand(1, M, C, generator=g) * 2 - 1).to(dtype)
+            w = ((torch.rand(HD, C, generator=g) * 2 - 1) * 0.1).to(dtype)
+            b = ((torch.rand(HD, generator=g) * 2 - 1) * 0.05).to(dtype)
+            ref = mem[0].double() @ w.double().T + b.double()
+            with torch.inference_mode():
+                got = _native.value_proj(mem.cuda(), w.cuda(), b.cuda(), H)
+                hm = _native.value_proj(mem.cuda(), w.cuda(), b.cuda(), H, head_major=True)
+            atol, rtol = TOL[dtype]
+            err = (got[0].double().cpu() - ref).abs().max().item()
+            assert torch.allclose(got[0].double().cpu(), ref, atol=atol, rtol=rtol), f'{dtype} HD{HD} C{C}: {err:.3g}'
+            assert torch.equal(hm.permute(0, 2, 1, 3).reshape(got.shape), got), f'{dtype} HD{HD} C{C} head-major'
+    torch.cuda.synchronize()
+    assert _native.device_error(clear=True) == 0
+
+
 def test_device_error_word_is_clear(cuda):
     """No bounded wait in any tensor-core kernel gave up during the tests above."""
     torch.cuda.synchronize()
