@@ -31,13 +31,13 @@ MODES = ('auto', 'fused', 'project')
 # 'project' ~ batch * tokens * C * H * D plus a fixed part that matters at batch 1.
 # FUSED_LIMIT and FUSED_LIMIT_SM75 are upstream's tables (RTX 4090 / RTX 2080 Super); FUSED_LIMIT_SM100 is fitted
 # to crossovers measured with this library on B200 (bench.py --sweep over upstream's query/batch grid, c4 and the
-# c5 grid), used for compute capability 10.x. On B200 the tensor-core projection makes 'project' cheap even at
-# batch 1 (fixed cost ~9 us at the RT-DETR shape), while 'fused' pays its per-call latency once for the whole
-# batch, so in 16-bit types 'fused' only wins at batch >= 4 with few queries: b is negative (the limit grows with
-# the batch). float32 keeps a CUDA-core projection (TF32 off), so 'fused' wins up to about 0.095.
+# c5 grid: 114 cases, the pick within 10% of the faster order in all of them), used for compute capability 10.x.
+# On B200 the tensor-core projection (float32 too, as three TF32 products) makes 'project' cheap even at batch 1,
+# while 'fused' pays its per-call latency once for the whole batch, so 'fused' only wins at batch >= 4 with few
+# queries: b is negative (the limit grows with the batch).
 FUSED_LIMIT = {torch.float32: (0.073, 0.032), torch.float16: (0.023, 0.031), torch.bfloat16: (0.023, 0.031)}
 FUSED_LIMIT_SM75 = {torch.float32: (0.068, 0.0), torch.float16: (0.020, 0.0), torch.bfloat16: (0.132, 0.0)}
-FUSED_LIMIT_SM100 = {torch.float32: (0.095, 0.0), torch.float16: (0.0225, -0.019), torch.bfloat16: (0.0225, -0.019)}
+FUSED_LIMIT_SM100 = {torch.float32: (0.026, -0.05), torch.float16: (0.015, -0.024), torch.bfloat16: (0.015, -0.024)}
 
 
 @functools.lru_cache(maxsize=None)
