@@ -1,6 +1,6 @@
-// td_ptx.cuh -- thin inline-PTX wrappers for the sm_100a features the tensor-core kernels use:
-// mbarriers with bounded waits, TMA 2-D tile loads (no multicast), tcgen05 TMEM allocation, MMA, commit and loads,
-// and the shared-memory / instruction descriptors of tcgen05.mma.
+// td_ptx.cuh -- thin inline-PTX wrappers for the sm_100a features the tensor-core kernels use: mbarriers with
+// bounded waits, TMA tile loads and stores (each CTA moves its own tiles), tcgen05 TMEM allocation, MMA, commit and
+// loads, and the shared-memory / instruction descriptors of tcgen05.mma.
 //
 // Every wait here is bounded: after kSpinLimitCycles (about a second) it gives up, records the place in the
 // library's device error word and returns false, so a wrong descriptor or byte count ends the kernel with an error
