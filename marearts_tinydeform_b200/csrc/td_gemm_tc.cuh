@@ -6,12 +6,12 @@
 // the [B, N, ...] tensors). Persistent and warp-specialised: each CTA walks tiles t = blockIdx.x, + gridDim.x, ...
 // (channel tiles fastest, so the CTAs that share a 128-token slice of memory run together and it is read from HBM
 // once):
-//   * warps 0-2, one thread each: TMA producers -- per tile and per 128-byte-wide K block, the 128-token slice of
-//     memory and the BN-row slice of W (K-major, 128-byte swizzle) into a ring of kStages shared-memory slots.
-//     K blocks are dealt round-robin to kProducers warps because the TMA operations of one issuing warp are served
-//     one after another (about 0.15 us each on B200, whatever their size), while those of different warps overlap.
-//     kProducers divides kStages, so every slot has one owner that fills it round after round: a parity wait on
-//     the slot's barrier can then never run two phases ahead of it;
+//   * warp 0, two lanes per slot: TMA producers -- per tile and per 128-byte-wide K block, the 128-token slice of
+//     memory (lane 2s) and the BN-row slice of W (lane 2s + 1), K-major with 128-byte swizzle, into slot s of a ring
+//     of kStages shared-memory slots. The TMA operations of one issuing thread are served one after another (about
+//     0.15-0.3 us each on B200, whatever their size) while those of different threads overlap, so every box of a
+//     ring round has its own issuer; a lane walks its slot's rounds in order (so a parity wait on the slot's barrier
+//     never runs two phases ahead) and polls without blocking, so a slot that is not free yet holds up no other;
 //   * EPI warps from warp 4 on: epilogue -- tcgen05.ld of the accumulator (TMEM lane = tile row; warp w reads
 //     lanes 32 (w % 4) .. + 31, and with 8 warps each takes half of the columns), + bias (staged in shared memory),
 //     narrowed to T and written into a staging tile laid out as the output's boxes (TMA swizzle, so the 16-byte
@@ -82,19 +82,17 @@ struct ProjTcLayout {
     static constexpr uint32_t kStgBytes = kTcBM * BN * sizeof(T);  // epilogue staging tile
     static constexpr uint32_t kBiasBytes = BN * 4;
     static constexpr int kFit = int((kTcSmemBudget - kStgBytes - kBiasBytes) / kStageBytes);
-    // a count with a divisor among 2 / 3 / 4, so that several producer warps can share the slots
-    static constexpr int kStages = kFit >= 8 ? 8 : kFit >= 6 ? 6 : kFit >= 4 ? 4 : kFit >= 3 ? 3 : 2;
+    static constexpr int kStages = kFit < 8 ? kFit : 8;  // two producer lanes a slot: at most 16
     static constexpr uint32_t kStgOffset = kStages * kStageBytes;  // 1024-aligned: stage sizes are multiples of 1 KB
     static constexpr uint32_t kBiasOffset = kStgOffset + kStgBytes;
-    // barriers: full[S], split[S], empty[S], tfull[2], tempty[2]
+    // barriers: full[S] (two arrivals: the memory and the weight box), split[S], empty[S], tfull[2], tempty[2]
     static constexpr uint32_t kBarOffset = kBiasOffset + kBiasBytes;
     static constexpr uint32_t kSlotOffset = kBarOffset + (3 * kStages + 4) * 8;
     static constexpr uint32_t kSmemBytes = kSlotOffset + 16 + 1024;  // + slack to align the base to 1024
     static constexpr uint32_t kTmemCols = 2 * BN;
-    // warps 0 .. kProducers-1 load, warp 3 issues the MMAs, warps 4 .. 4+EPI-1 run the epilogue (a multiple of 4
-    // apart, as epilogue warp w reads TMEM lanes 32 (w % 4) ..), then the float32 split warps: whole groups of four
-    // warps, so that every SM sub-partition holds the same share of the CTA's registers
-    static constexpr int kProducers = kStages % 3 == 0 ? 3 : kStages % 2 == 0 ? 2 : 1;
+    // warp 0 loads, warp 3 issues the MMAs, warps 4 .. 4+EPI-1 run the epilogue (a multiple of 4 apart, as epilogue
+    // warp w reads TMEM lanes 32 (w % 4) ..), then the float32 split warps: whole groups of four warps, so that every
+    // SM sub-partition holds the same share of the CTA's registers
     static constexpr int kMmaWarp = 3;
     static constexpr int kEpiWarp0 = 4;
     static constexpr int kSplitWarp0 = kEpiWarp0 + EPI;
@@ -102,7 +100,6 @@ struct ProjTcLayout {
     static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
     static_assert(EPI == 4 || EPI == 8, "epilogue warps");
     static_assert(kStages >= 2, "pipeline depth");
-    static_assert(kStages % kProducers == 0, "one producer per slot");
     static_assert(kSlotOffset + 16 <= uint32_t(kTcSmemBudget) + 512, "shared memory");
 };
 
@@ -182,7 +179,7 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
     const int KB = a.k_blocks;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full[s], 2);
             mbar_init(&split[s], 4);  // one arrival per split warp
             mbar_init(&empty[s], 1);
         }
@@ -214,34 +211,49 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
         c0 = (r - mt * a.n_tiles) * BN;
     };
     const int my_tiles = a.tiles > int(blockIdx.x) ? (a.tiles - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
-    // Everything above touches only shared memory and TMEM, so under programmatic dependent launch it overlaps the
-    // previous kernel in the stream; every global read and write comes after this wait.
-    grid_dependency_wait();
-    // the sampler that follows in the project order may start its prologue now (it waits for this grid before
-    // reading value)
+    // Under programmatic dependent launch everything up to a thread's first global access overlaps the previous
+    // kernel in the stream: each role waits for it (grid_dependency_wait) right before its first global read or
+    // write, after the set-up work and the first pass through its code. The MMA and split warps touch only shared
+    // memory and TMEM, behind the producers. The sampler that follows in the project order may start its prologue
+    // now (it waits for this grid before reading value).
     launch_dependents();
 
     if (warp < Lay::kMmaWarp) {
-        if (lane == 0 && warp < Lay::kProducers) {
-            // TMA producer `warp`: the K blocks it = warp, warp + kProducers, ... of this CTA's sequence (tile-major),
-            // which all use the slots s = warp (mod kProducers)
+        if (warp == 0 && lane < 2 * S) {
+            // TMA producer lane: slot s, the memory box (even lane) or the weight box (odd lane) of the K blocks
+            // it = s, s + S, ... of this CTA's sequence (tile-major); then one more round that only waits, so that
+            // no MMA commit is still to arrive on the slot when the CTA exits
+            const int s = lane >> 1;
+            const bool box_a = (lane & 1) == 0;
             const int total = my_tiles * KB;
-            bool ok = true;
-            int it = warp;
-            for (; it < total; it += Lay::kProducers) {
-                const int tl = it / KB, kb = it - tl * KB;
-                int b, n0, c0;
-                tile_at(int(blockIdx.x) + tl * int(gridDim.x), b, n0, c0);
-                const int s = it % S;
-                if (!mbar_wait(&empty[s], uint32_t((it / S) & 1) ^ 1u, kErrSlotWait)) { ok = false; break; }
-                mbar_arrive_expect_tx(&full[s], Lay::kABytes + Lay::kBBytes);
-                tma_load_3d(slot_a(s), &map_a, &full[s], kb * kBK, n0, b);
-                tma_load_2d(slot_b(s), &map_b, &full[s], kb * kBK, c0);
-            }
-            // drain: the last use of every slot of this producer handed back, so no MMA commit is still to arrive
-            // when the CTA exits
-            for (; ok && it < total + S; it += Lay::kProducers) {
-                if (!mbar_wait(&empty[it % S], uint32_t((it / S) & 1) ^ 1u, kErrSlotWait)) ok = false;
+            long long t0 = clock64();
+            bool waited = false;
+            for (int it = s; it < total + S;) {
+                if (mbar_test(&empty[s], uint32_t((it / S) & 1) ^ 1u)) {
+                    if (it < total) {
+                        const int tl = it / KB, kb = it - tl * KB;
+                        int b, n0, c0;
+                        tile_at(int(blockIdx.x) + tl * int(gridDim.x), b, n0, c0);
+                        if (!waited) {
+                            grid_dependency_wait();
+                            waited = true;
+                        }
+                        if (box_a) {
+                            mbar_arrive_expect_tx(&full[s], Lay::kABytes);
+                            tma_load_3d(slot_a(s), &map_a, &full[s], kb * kBK, n0, b);
+                        } else {
+                            mbar_arrive_expect_tx(&full[s], Lay::kBBytes);
+                            tma_load_2d(slot_b(s), &map_b, &full[s], kb * kBK, c0);
+                        }
+                    }
+                    it += S;
+                    t0 = clock64();
+                } else if (clock64() - t0 > kSpinLimitCycles) {
+                    record_error(kErrSlotWait);
+                    break;
+                } else {
+                    __nanosleep(32);  // leave the issue slots to the epilogue warps of this sub-partition
+                }
             }
         }
     } else if (warp == Lay::kMmaWarp) {
@@ -305,9 +317,10 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
             const int acc = tc & 1;
             int b, n0, c0;
             tile_at(int(blockIdx.x) + (dry ? 0 : tc) * int(gridDim.x), b, n0, c0);
+            if (tc == 0) grid_dependency_wait();  // the dry pass reads and writes no global memory
             // this tile's bias; the previous tile's readers are past its second barrier
             for (int i = etid; i < BN; i += kEpiThreads)
-                sbias[i] = (a.bias != nullptr && c0 + i < a.HD) ? to_acc(a.bias[c0 + i]) : 0.f;
+                sbias[i] = (!dry && a.bias != nullptr && c0 + i < a.HD) ? to_acc(a.bias[c0 + i]) : 0.f;
             // the staging tile is free once the previous tile's stores have read it
             if (lane == 0 && a.tma_store) bulk_wait_read();
             named_barrier(1, kEpiThreads);
@@ -380,7 +393,8 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
                 }
             }
         }
-        if (lane == 0 && a.tma_store) bulk_wait_all();
+        // the CTA may exit once its stores have read the staging tile; the grid completes only when they are written
+        if (lane == 0 && a.tma_store) bulk_wait_read();
     } else if (kSplit && warp >= Lay::kSplitWarp0) {
         // float32: split every landed slot into hi (in place) and lo
         const int tid = (warp - Lay::kSplitWarp0) * 32 + lane;  // 128 threads
@@ -415,6 +429,7 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
+        __syncwarp();  // the producer lanes took different paths: converge for the .sync.aligned dealloc
         tc_fence_after();
         tmem_dealloc(tmem, Lay::kTmemCols);
     }
