@@ -214,9 +214,9 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
     // Under programmatic dependent launch everything up to a thread's first global access overlaps the previous
     // kernel in the stream: each role waits for it (grid_dependency_wait) right before its first global read or
     // write, after the set-up work and the first pass through its code. The MMA and split warps touch only shared
-    // memory and TMEM, behind the producers. The sampler that follows in the project order may start its prologue
-    // now (it waits for this grid before reading value).
-    launch_dependents();
+    // memory and TMEM, behind the producers. Dependents are released only after that wait (by the producer lanes):
+    // the sampler that follows in the project order reads this call's locations and weights before its own wait,
+    // so the kernels that wrote them must have completed.
 
     if (warp < Lay::kMmaWarp) {
         if (warp == 0 && lane < 2 * S) {
@@ -236,6 +236,7 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
                         tile_at(int(blockIdx.x) + tl * int(gridDim.x), b, n0, c0);
                         if (!waited) {
                             grid_dependency_wait();
+                            launch_dependents();
                             waited = true;
                         }
                         if (box_a) {
