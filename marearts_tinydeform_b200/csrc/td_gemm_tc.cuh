@@ -15,10 +15,10 @@
 //   * EPI warps from warp 4 on: epilogue -- tcgen05.ld of the accumulator (TMEM lane = tile row; warp w reads
 //     lanes 32 (w % 4) .. + 31, and with 8 warps each takes half of the columns), + bias (staged in shared memory),
 //     narrowed to T and written into a staging tile laid out as the output's boxes (TMA swizzle, so the 16-byte
-//     writes of a warp hit distinct banks); the accumulator is handed back as soon as it is read, and the boxes
-//     are written with TMA tensor stores, issued by every epilogue warp in turn -- whole lines, where per-thread
-//     row stores would write half sectors. Shapes whose boxes cannot be described that way store straight from
-//     registers instead;
+//     writes of a warp hit distinct banks); the accumulator is handed back as soon as it is read, and each warp
+//     writes its own 32-row boxes with TMA tensor stores as soon as it has staged them -- whole lines, where
+//     per-thread row stores would write half sectors. Shapes whose boxes cannot be described that way store straight
+//     from registers instead;
 //   * warp 3, one thread: MMA issuer -- four K steps per block (tcgen05.mma, M = 128, N = BN) into one of two TMEM
 //     accumulators (2 x BN float32 columns), so the epilogue of one tile runs under the MMAs of the next;
 //   * float32 only, four more warps: split -- every landed slot is rewritten as hi = x with its 13 low mantissa bits
@@ -47,7 +47,7 @@ struct ProjTcArgs {
     int m_tiles;      // ceil(N / 128): token tiles per image
     int tiles;        // B * m_tiles * n_tiles (< 2^31)
     // epilogue through TMA stores: boxes of `piece` columns (piece_bytes = piece * sizeof(T) in {16, 32, 64, 128})
-    // x 128 tokens, 0 = direct stores
+    // x 32 tokens, 0 = direct stores
     int tma_store, piece, piece_bytes;
 };
 
@@ -299,7 +299,7 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
         // epilogue
         constexpr int kEpiThreads = EPI * 32;
         const int etid = threadIdx.x - 32 * Lay::kEpiWarp0;
-        const int ew = warp - Lay::kEpiWarp0;  // stores of boxes ew, ew + EPI, ... are this warp's
+        const int ew = warp - Lay::kEpiWarp0;
         const int quarter = warp & 3;
         constexpr int kCols = EPI == 8 ? BN / 2 : BN;  // columns this warp converts
         const int c_lo = EPI == 8 ? (ew >> 2) * kCols : 0;
@@ -376,18 +376,20 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
                 }
             }
             if (a.tma_store) {
+                // this warp's boxes -- its columns [c_lo, c_lo + kCols) by its 32 rows -- as soon as it has staged
+                // them, without waiting for the other epilogue warps
                 fence_proxy_async_smem();  // the TMA stores (async proxy) read what these threads wrote
-                named_barrier(1, kEpiThreads);
+                __syncwarp();
                 if (lane == 0 && ready && !dry) {
-                    for (int p = ew; p < (BN >> pshift); p += EPI) {
+                    for (int p = c_lo >> pshift; p < (c_lo + kCols) >> pshift; ++p) {
                         const int col = c0 + (p << pshift);
                         if (col >= a.HD) break;
-                        const unsigned char* src = stg + p * (kTcBM * pb);
+                        const unsigned char* src = stg + p * (kTcBM * pb) + quarter * 32 * pb;
                         if (a.head_major) {
                             const int h = col / a.D;
-                            tma_store_3d(&map_out, src, col - h * a.D, n0, b * a.H + h);
+                            tma_store_3d(&map_out, src, col - h * a.D, n0 + quarter * 32, b * a.H + h);
                         } else {
-                            tma_store_3d(&map_out, src, col, n0, b);
+                            tma_store_3d(&map_out, src, col, n0 + quarter * 32, b);
                         }
                     }
                     bulk_commit();

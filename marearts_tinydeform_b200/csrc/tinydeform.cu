@@ -343,7 +343,7 @@ int prepare_proj_tc(const T* memory, const T* weight, const T* bias, T* value, i
             return rc;
     }
     if (int rc = tensor_map_2d(map_b, weight, uint64_t(C), uint64_t(HD), BN, err, err_len, e)) return rc;
-    // Epilogue boxes: `piece` columns x 128 tokens. Head-major value [B, H, N, D]: a piece is a head, or a 128-byte
+    // Epilogue boxes: `piece` columns x 32 tokens. Head-major value [B, H, N, D]: a piece is a head, or a 128-byte
     // part of one; [B, N, HD]: 128-byte column groups. The row of a box must be 16, 32, 64 or 128 bytes (the TMA
     // swizzle widths that keep the staging writes free of bank conflicts).
     int piece = 0;
@@ -361,7 +361,7 @@ int prepare_proj_tc(const T* memory, const T* weight, const T* bias, T* value, i
                                       : piece_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                                       : piece_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
                                                           : CU_TENSOR_MAP_SWIZZLE_NONE;
-        const uint32_t box[3] = {uint32_t(piece), uint32_t(kTcBM), 1u};
+        const uint32_t box[3] = {uint32_t(piece), 32u, 1u};  // one epilogue warp's rows
         if (head_major) {
             const uint64_t dims[3] = {uint64_t(D), uint64_t(N), uint64_t(B * H)};
             const uint64_t strides[2] = {uint64_t(D) * e, uint64_t(N * D) * e};
