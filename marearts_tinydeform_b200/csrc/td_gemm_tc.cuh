@@ -323,7 +323,7 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
             for (int i = etid; i < BN; i += kEpiThreads)
                 sbias[i] = (!dry && a.bias != nullptr && c0 + i < a.HD) ? to_acc(a.bias[c0 + i]) : 0.f;
             // the staging tile is free once the previous tile's stores have read it
-            if (lane == 0 && a.tma_store) bulk_wait_read();
+            if (a.tma_store) bulk_wait_read();
             named_barrier(1, kEpiThreads);
             bool ready = dry || (!dead && mbar_wait(&tfull[acc], uint32_t((tc >> 1) & 1), kErrMmaWait));
             ready = __all_sync(0xffffffffu, ready);
@@ -353,9 +353,14 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
 #pragma unroll
                 for (int g = 0; g < 4; ++g) {
                     const int c = cl + 8 * g;  // tile column
+                    // the 8 bias values as two 16-byte shared-memory reads (sbias is 16-byte aligned, c a multiple
+                    // of 8; every lane reads the same words: broadcast)
+                    const float4 b0 = reinterpret_cast<const float4*>(sbias + c)[0];
+                    const float4 b1 = reinterpret_cast<const float4*>(sbias + c)[1];
+                    const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
                     float f[8];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(v[8 * g + i]) + sbias[c + i];
+                    for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(v[8 * g + i]) + bb[i];
                     uint4 w[kWords];
                     pack8<T>(f, w);
                     if (a.tma_store) {
@@ -380,24 +385,23 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
                 // them, without waiting for the other epilogue warps
                 fence_proxy_async_smem();  // the TMA stores (async proxy) read what these threads wrote
                 __syncwarp();
-                if (lane == 0 && ready && !dry) {
-                    for (int p = c_lo >> pshift; p < (c_lo + kCols) >> pshift; ++p) {
-                        const int col = c0 + (p << pshift);
-                        if (col >= a.HD) break;
-                        const unsigned char* src = stg + p * (kTcBM * pb) + quarter * 32 * pb;
-                        if (a.head_major) {
-                            const int h = col / a.D;
-                            tma_store_3d(&map_out, src, col - h * a.D, n0 + quarter * 32, b * a.H + h);
-                        } else {
-                            tma_store_3d(&map_out, src, col, n0 + quarter * 32, b);
-                        }
+                // one box per lane: the TMA operations of one thread are served one after another
+                const int p = (c_lo >> pshift) + lane;
+                const int col = c0 + (p << pshift);
+                if (ready && !dry && p < ((c_lo + kCols) >> pshift) && col < a.HD) {
+                    const unsigned char* src = stg + p * (kTcBM * pb) + quarter * 32 * pb;
+                    if (a.head_major) {
+                        const int h = col / a.D;
+                        tma_store_3d(&map_out, src, col - h * a.D, n0 + quarter * 32, b * a.H + h);
+                    } else {
+                        tma_store_3d(&map_out, src, col, n0 + quarter * 32, b);
                     }
                     bulk_commit();
                 }
             }
         }
         // the CTA may exit once its stores have read the staging tile; the grid completes only when they are written
-        if (lane == 0 && a.tma_store) bulk_wait_read();
+        if (a.tma_store) bulk_wait_read();
     } else if (kSplit && warp >= Lay::kSplitWarp0) {
         // float32: split every landed slot into hi (in place) and lo
         const int tid = (warp - Lay::kSplitWarp0) * 32 + lane;  // 128 threads
