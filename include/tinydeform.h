@@ -111,6 +111,25 @@ TD_API int td_project_forward(int dtype, const void* memory, const void* value_w
                        void* workspace, size_t workspace_bytes, void* stream, char* err, size_t err_len);
 
 /*
+ * Both orders with a value padding mask. No counterpart in upstream (whose value has no mask); the semantics are
+ * Deformable-DETR's input_padding_mask: value = memory @ W^T + b, then value[b, n, :] = 0 wherever
+ * value_padding_mask[b * N + n] != 0. A padded token thus contributes nothing to the output, its bias included: its
+ * bilinear corners count as outside the map. value_padding_mask is a device array of B * N bytes (torch.bool
+ * layout), or NULL for no mask (the unmasked entry points above).
+ */
+TD_API int td_fused_forward_masked(int dtype, const void* memory, const void* value_weight, const void* value_bias,
+                            const int64_t* spatial_shapes, const int64_t* level_start_index,
+                            const void* sampling_locations, const void* attention_weights,
+                            const uint8_t* value_padding_mask, void* out, int64_t B, int64_t Q, int64_t N, int64_t C,
+                            int64_t H, int64_t HD, int64_t L, int64_t P, void* stream, char* err, size_t err_len);
+TD_API int td_project_forward_masked(int dtype, const void* memory, const void* value_weight, const void* value_bias,
+                              const int64_t* spatial_shapes, const int64_t* level_start_index,
+                              const void* sampling_locations, const void* attention_weights,
+                              const uint8_t* value_padding_mask, void* out, int64_t B, int64_t Q, int64_t N,
+                              int64_t C, int64_t H, int64_t HD, int64_t L, int64_t P, void* workspace,
+                              size_t workspace_bytes, void* stream, char* err, size_t err_len);
+
+/*
  * Project order with no caller-provided workspace and no allocation at all. No counterpart in upstream.
  *
  * For callers that cannot allocate device memory on the call path: inference plugins run inside a host framework

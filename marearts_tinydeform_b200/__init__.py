@@ -60,18 +60,22 @@ def choose_mode(memory, value_weight, sampling_locations):
 
 
 def ma_deform_attn(memory, value_weight, value_bias, spatial_shapes, level_start_index,
-                   sampling_locations, attention_weights, mode='auto'):
+                   sampling_locations, attention_weights, mode='auto', value_padding_mask=None):
     """value = memory @ value_weight.T + value_bias, then multi-scale deformable attention; [B, Q, H * D].
 
     Same arguments, shapes and result as ma_deform_attn_reference (grid_sample, bilinear, zero padding,
     align_corners=False). CUDA tensors (float32, float16, bfloat16, float64; float32 accumulation, float64 for
     float64) run the B200 kernels in the order `mode` names; CPU tensors run the reference.
+
+    value_padding_mask (an addition; the upstream operator has none): bool [B, N], True = padded token. As
+    Deformable-DETR's input_padding_mask, the projected value of a padded token is zeroed (its bias included)
+    before sampling, so it contributes nothing.
     """
     if mode not in MODES:
         raise ValueError(f'mode must be one of {MODES}, got {mode!r}')
     if not memory.is_cuda:
         return ma_deform_attn_reference(memory, value_weight, value_bias, spatial_shapes, level_start_index,
-                                        sampling_locations, attention_weights)
+                                        sampling_locations, attention_weights, value_padding_mask)
     _native.load()  # raises RuntimeError when the native library is missing: there is no fallback
     if torch.is_grad_enabled() and any(
             t is not None and t.requires_grad
@@ -82,4 +86,4 @@ def ma_deform_attn(memory, value_weight, value_bias, spatial_shapes, level_start
         mode = choose_mode(memory, value_weight, sampling_locations)
     run = _native.fused_forward if mode == 'fused' else _native.project_forward
     return run(memory, value_weight, value_bias, spatial_shapes, level_start_index, sampling_locations,
-               attention_weights)
+               attention_weights, value_padding_mask)

@@ -34,6 +34,10 @@ SIGNATURES = {
     'td_project_workspace_bytes': (_sz, [_ip, _i64, _i64, _i64]),
     'td_project_forward': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                  _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp, _cp, _sz]),
+    'td_fused_forward_masked': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                      _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _cp, _sz]),
+    'td_project_forward_masked': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                        _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp, _cp, _sz]),
     'td_project_forward_noalloc': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                          _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _cp, _sz]),
     'td_set_kernel_policy': (_ip, [_ip]),
@@ -150,12 +154,29 @@ def _dense(*ts):
     return [None if t is None else t.contiguous() for t in ts]
 
 
+def check_mask(value_padding_mask, memory):
+    """The value padding mask: bool (or uint8) [B, N] on memory's device, nonzero = padded token. Returns it as a
+    contiguous one-byte tensor (or None)."""
+    if value_padding_mask is None:
+        return None
+    m = value_padding_mask
+    if m.dtype not in (torch.bool, torch.uint8):
+        raise RuntimeError('value_padding_mask must be a bool (or uint8) tensor')
+    if m.dim() != 2 or m.size(0) != memory.size(0) or m.size(1) != memory.size(1):
+        raise RuntimeError('value_padding_mask must be [B, N] like memory')
+    if m.device != memory.device:
+        raise RuntimeError('value_padding_mask must be on the device of memory')
+    return m.contiguous()
+
+
 def fused_forward(memory, value_weight, value_bias, spatial_shapes, level_start_index,
-                  sampling_locations, attention_weights):
-    """Fused order (upstream _C.fused_forward, csrc/ma_deform_fused.cu:291-325) through td_fused_forward."""
+                  sampling_locations, attention_weights, value_padding_mask=None):
+    """Fused order (upstream _C.fused_forward, csrc/ma_deform_fused.cu:291-325) through td_fused_forward (with a
+    value padding mask: td_fused_forward_masked)."""
     lib = load()
     B, Q, H, L, P = check_geometry(memory, spatial_shapes, level_start_index, sampling_locations, attention_weights)
     HD = check_projection(memory, value_weight, value_bias, H)
+    mask = check_mask(value_padding_mask, memory)
     N, C = memory.size(1), memory.size(2)
     if C > MAX_CHANNELS:
         raise RuntimeError(f'channels must be <= {MAX_CHANNELS}')
@@ -165,17 +186,24 @@ def fused_forward(memory, value_weight, value_bias, spatial_shapes, level_start_
     if B * Q == 0:
         return out
     with torch.cuda.device(memory.device):
-        _call(lib.td_fused_forward, DTYPE_CODE[memory.dtype], _ptr(mem), _ptr(w), _ptr(b), _ptr(shp), _ptr(st),
-              _ptr(loc), _ptr(att), _ptr(out), B, Q, N, C, H, HD, L, P, _stream(memory.device))
+        if mask is None:
+            _call(lib.td_fused_forward, DTYPE_CODE[memory.dtype], _ptr(mem), _ptr(w), _ptr(b), _ptr(shp), _ptr(st),
+                  _ptr(loc), _ptr(att), _ptr(out), B, Q, N, C, H, HD, L, P, _stream(memory.device))
+        else:
+            _call(lib.td_fused_forward_masked, DTYPE_CODE[memory.dtype], _ptr(mem), _ptr(w), _ptr(b), _ptr(shp),
+                  _ptr(st), _ptr(loc), _ptr(att), _ptr(mask), _ptr(out), B, Q, N, C, H, HD, L, P,
+                  _stream(memory.device))
     return out
 
 
 def project_forward(memory, value_weight, value_bias, spatial_shapes, level_start_index,
-                    sampling_locations, attention_weights):
-    """Project order (upstream __init__.py:77-79: F.linear + _C.sample_forward) through td_project_forward."""
+                    sampling_locations, attention_weights, value_padding_mask=None):
+    """Project order (upstream __init__.py:77-79: F.linear + _C.sample_forward) through td_project_forward (with a
+    value padding mask: td_project_forward_masked)."""
     lib = load()
     B, Q, H, L, P = check_geometry(memory, spatial_shapes, level_start_index, sampling_locations, attention_weights)
     HD = check_projection(memory, value_weight, value_bias, H)
+    mask = check_mask(value_padding_mask, memory)
     N, C = memory.size(1), memory.size(2)
     mem, w, b, shp, st, loc, att = _dense(memory, value_weight, value_bias, spatial_shapes, level_start_index,
                                           sampling_locations, attention_weights)
@@ -186,8 +214,13 @@ def project_forward(memory, value_weight, value_bias, spatial_shapes, level_star
     ws_bytes = lib.td_project_workspace_bytes(code, B, N, HD)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=memory.device)
     with torch.cuda.device(memory.device):
-        _call(lib.td_project_forward, code, _ptr(mem), _ptr(w), _ptr(b), _ptr(shp), _ptr(st), _ptr(loc), _ptr(att),
-              _ptr(out), B, Q, N, C, H, HD, L, P, _ptr(ws), ws_bytes, _stream(memory.device))
+        if mask is None:
+            _call(lib.td_project_forward, code, _ptr(mem), _ptr(w), _ptr(b), _ptr(shp), _ptr(st), _ptr(loc),
+                  _ptr(att), _ptr(out), B, Q, N, C, H, HD, L, P, _ptr(ws), ws_bytes, _stream(memory.device))
+        else:
+            _call(lib.td_project_forward_masked, code, _ptr(mem), _ptr(w), _ptr(b), _ptr(shp), _ptr(st), _ptr(loc),
+                  _ptr(att), _ptr(mask), _ptr(out), B, Q, N, C, H, HD, L, P, _ptr(ws), ws_bytes,
+                  _stream(memory.device))
     return out
 
 

@@ -185,9 +185,13 @@ __device__ __forceinline__ Level level_at(const int64_t* __restrict__ shapes, co
 }
 
 // The four bilinear corners of one sampling point. tok[k] = -1 marks a corner outside the map (it contributes
-// nothing, as zero padding); inside corners carry attn * bilinear weight, which may itself be 0.
+// nothing, as zero padding); inside corners carry attn * bilinear weight, which may itself be 0. mask_b (the value
+// padding mask of the image, one byte per token, nonzero = padded; or null) turns a corner on a padded token into
+// an outside one: its value row counts as zero, as Deformable-DETR's masked_fill after the value projection makes
+// it (bias included).
 template <typename CT>
-__device__ __forceinline__ void corners4(CT lx, CT ly, CT a, const Level& lv, long long n_tok, int* tok, CT* wt) {
+__device__ __forceinline__ void corners4(CT lx, CT ly, CT a, const Level& lv, long long n_tok, int* tok, CT* wt,
+                                         const uint8_t* mask_b = nullptr) {
     const CT x = cmin(cmax(lx * CT(lv.w) - CT(0.5), CT(-2)), CT(lv.w) + CT(1));
     const CT y = cmin(cmax(ly * CT(lv.h) - CT(0.5), CT(-2)), CT(lv.h) + CT(1));
     const CT xf = cfloor(x), yf = cfloor(y);
@@ -197,7 +201,8 @@ __device__ __forceinline__ void corners4(CT lx, CT ly, CT a, const Level& lv, lo
     for (int k = 0; k < 4; ++k) {
         const int dx = k & 1, dy = k >> 1, xi = x0 + dx, yi = y0 + dy;
         const long long t = lv.start + (long long)yi * lv.w + xi;
-        const bool in = xi >= 0 && xi < lv.w && yi >= 0 && yi < lv.h && t >= 0 && t < n_tok;
+        bool in = xi >= 0 && xi < lv.w && yi >= 0 && yi < lv.h && t >= 0 && t < n_tok;
+        if (in && mask_b != nullptr) in = mask_b[t] == 0;
         tok[k] = in ? int(t) : -1;
         wt[k] = in ? a * (dx ? fx : CT(1) - fx) * (dy ? fy : CT(1) - fy) : CT(0);
     }
@@ -207,12 +212,12 @@ __device__ __forceinline__ void corners4(CT lx, CT ly, CT a, const Level& lv, lo
 template <typename T>
 __device__ __forceinline__ void row_corners(const T* __restrict__ loc, const T* __restrict__ attn, const Level* lv,
                                             int LP, int P, long long n_tok, long long bqh, int j, int* tok,
-                                            typename Coord<T>::type* wt) {
+                                            typename Coord<T>::type* wt, const uint8_t* mask_b = nullptr) {
     using CT = typename Coord<T>::type;
     const long long i = bqh * LP + j;
     const CT lx = CT(to_acc(loc[2 * i])), ly = CT(to_acc(loc[2 * i + 1]));
     const CT a = CT(to_acc(attn[i]));
-    corners4<CT>(lx, ly, a, lv[j / P], n_tok, tok, wt);
+    corners4<CT>(lx, ly, a, lv[j / P], n_tok, tok, wt, mask_b);
 }
 
 }  // namespace td

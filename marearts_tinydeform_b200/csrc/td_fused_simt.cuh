@@ -26,6 +26,7 @@ struct FusedArgs {
     const int64_t* shapes;
     const int64_t* starts;
     long long n_tok;  // N
+    const uint8_t* mask;  // value padding mask [B, N] (nonzero = padded) or null
     int B, Q, C, H, D, L, P;
     int R;            // queries per CTA (<= kFusedMaxRows)
     int q_tiles;      // ceil(Q / R)
@@ -86,7 +87,8 @@ __global__ void __launch_bounds__(kFusedThreads) fused_simt_kernel(const FusedAr
         CT* w = wt + r * S + 4 * j;
         if (r < rows) {
             const long long bqh = ((long long)b * a.Q + q0 + r) * a.H + h;
-            row_corners(a.loc, a.attn, lv, LP, a.P, a.n_tok, bqh, j, tk, w);
+            row_corners(a.loc, a.attn, lv, LP, a.P, a.n_tok, bqh, j, tk, w,
+                        a.mask != nullptr ? a.mask + (long long)b * a.n_tok : nullptr);
         } else {
 #pragma unroll
             for (int k = 0; k < 4; ++k) { tk[k] = -1; w[k] = CT(0); }

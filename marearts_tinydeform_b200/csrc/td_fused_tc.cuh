@@ -39,6 +39,7 @@ struct FusedTcArgs {
     const int64_t* shapes;
     const int64_t* starts;
     long long n_tok;
+    const uint8_t* mask;  // value padding mask [B, N] (nonzero = padded) or null
     long long rows;  // B * H * Q
     int B, Q, C, H, D, L, P;
     int pieces;      // row pieces one warp's corner range can touch in a pass
@@ -172,9 +173,11 @@ __global__ void __launch_bounds__(kFtcThreads, 1)
             const bool g = r >= n0;
             const int q = g ? r - n0 : q00 + r;
             const Level lv = level_at(a.shapes, a.starts, j / a.P);
-            const long long k = (((long long)(g ? b1 : b0) * a.Q + q) * a.H + (g ? h1 : h0)) * LP + j;
+            const int bimg = g ? b1 : b0;
+            const long long k = (((long long)bimg * a.Q + q) * a.H + (g ? h1 : h0)) * LP + j;
             corners4<float>(to_acc(a.loc[2 * k]), to_acc(a.loc[2 * k + 1]), to_acc(a.attn[k]), lv, a.n_tok,
-                            tok + r * S + 4 * j, wt + r * S + 4 * j);
+                            tok + r * S + 4 * j, wt + r * S + 4 * j,
+                            a.mask != nullptr ? a.mask + (long long)bimg * a.n_tok : nullptr);
         }
         __syncthreads();
 

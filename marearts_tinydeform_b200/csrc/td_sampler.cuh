@@ -27,6 +27,7 @@ struct SampleArgs {
     long long rows;                 // B * Q * H
     long long s_img, s_tok, s_head; // value strides in elements
     long long n_tok;                // N
+    const uint8_t* mask;            // value padding mask [B, N] (nonzero = padded) or null
     int Q, H, D, L, P;
     int G;                          // lanes per corner row = D * sizeof(T) / 16 (vector kernel only)
 };
@@ -48,11 +49,12 @@ __device__ __forceinline__ void sample_row_corners(const SampleArgs<T>& a, long 
                                                    typename Coord<T>::type* s_wt) {
     using CT = typename Coord<T>::type;
     const int LP = a.L * a.P;
+    const uint8_t* mask_b = a.mask != nullptr ? a.mask + row / ((long long)a.Q * a.H) * a.n_tok : nullptr;
     for (int j = lane; j < LP; j += 32) {
         const Level lv = level_at(a.shapes, a.starts, j / a.P);
         const long long i = row * LP + j;
         corners4<CT>(CT(to_acc(a.loc[2 * i])), CT(to_acc(a.loc[2 * i + 1])), CT(to_acc(a.attn[i])), lv, a.n_tok,
-                     &s_tok[4 * j], &s_wt[4 * j]);
+                     &s_tok[4 * j], &s_wt[4 * j], mask_b);
     }
 }
 
@@ -154,7 +156,8 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_generic_kernel(const
     if (row >= a.rows) return;
     const int LP = a.L * a.P, S = 4 * LP;
     for (int j = lane; j < LP; j += 32)
-        row_corners(a.loc, a.attn, lv, LP, a.P, a.n_tok, row, j, &s_tok[warp][4 * j], &s_wt[warp][4 * j]);
+        row_corners(a.loc, a.attn, lv, LP, a.P, a.n_tok, row, j, &s_tok[warp][4 * j], &s_wt[warp][4 * j],
+                    a.mask != nullptr ? a.mask + row / ((long long)a.Q * a.H) * a.n_tok : nullptr);
     __syncwarp();
 
     const int h = int(row % a.H);

@@ -119,10 +119,10 @@ template <typename T>
 int launch_sampler(const T* value, long long s_img, long long s_tok, long long s_head, const int64_t* shapes,
                    const int64_t* starts, const T* loc, const T* attn, T* out, int64_t B, int64_t Q, int64_t N,
                    int64_t H, int64_t D, int64_t L, int64_t P, cudaStream_t stream, char* err, size_t err_len,
-                   bool after_producer = false) {
+                   bool after_producer = false, const uint8_t* mask = nullptr) {
     SampleArgs<T> a;
     a.value = value; a.loc = loc; a.attn = attn; a.out = out; a.shapes = shapes; a.starts = starts;
-    a.rows = B * Q * H; a.s_img = s_img; a.s_tok = s_tok; a.s_head = s_head; a.n_tok = N;
+    a.rows = B * Q * H; a.s_img = s_img; a.s_tok = s_tok; a.s_head = s_head; a.n_tok = N; a.mask = mask;
     a.Q = int(Q); a.H = int(H); a.D = int(D); a.L = int(L); a.P = int(P);
     const long long row_bytes = D * (long long)sizeof(T);
     a.G = int(row_bytes / 16);
@@ -188,8 +188,8 @@ int launch_fused_tc_cfg(const CUtensorMap& map_w, const FusedTcArgs<T>& a, int s
 template <typename T>
 int launch_fused_tc(const T* memory, const T* weight, const T* bias, const int64_t* shapes, const int64_t* starts,
                     const T* loc, const T* attn, T* out, int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H,
-                    int64_t D, int64_t L, int64_t P, const DeviceFacts& f, cudaStream_t stream, char* err,
-                    size_t err_len, bool* launched) {
+                    int64_t D, int64_t L, int64_t P, const uint8_t* mask, const DeviceFacts& f, cudaStream_t stream,
+                    char* err, size_t err_len, bool* launched) {
     *launched = false;
     if (C > 1024 || 2 * D > 512) return TD_OK;
     const int S = int(4 * L * P);
@@ -201,8 +201,8 @@ int launch_fused_tc(const T* memory, const T* weight, const T* bias, const int64
     if (int rc = tensor_map_2d(&map_w, weight, uint64_t(C), uint64_t(H * D), uint32_t(D), err, err_len)) return rc;
     FusedTcArgs<T> a;
     a.memory = memory; a.bias = bias; a.loc = loc; a.attn = attn; a.out = out; a.shapes = shapes; a.starts = starts;
-    a.n_tok = N; a.rows = B * H * Q; a.B = int(B); a.Q = int(Q); a.C = int(C); a.H = int(H); a.D = int(D);
-    a.L = int(L); a.P = int(P); a.pieces = pieces;
+    a.n_tok = N; a.mask = mask; a.rows = B * H * Q; a.B = int(B); a.Q = int(Q); a.C = int(C); a.H = int(H);
+    a.D = int(D); a.L = int(L); a.P = int(P); a.pieces = pieces;
     *launched = true;
     if (CV == 1) return launch_fused_tc_cfg<T, 1>(map_w, a, f.sm_count, smem, stream, err, err_len);
     if (CV == 2) return launch_fused_tc_cfg<T, 2>(map_w, a, f.sm_count, smem, stream, err, err_len);
@@ -212,7 +212,8 @@ int launch_fused_tc(const T* memory, const T* weight, const T* bias, const int64
 template <typename T>
 int launch_fused(const T* memory, const T* weight, const T* bias, const int64_t* shapes, const int64_t* starts,
                  const T* loc, const T* attn, T* out, int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H,
-                 int64_t D, int64_t L, int64_t P, cudaStream_t stream, char* err, size_t err_len) {
+                 int64_t D, int64_t L, int64_t P, cudaStream_t stream, char* err, size_t err_len,
+                 const uint8_t* mask = nullptr) {
     using A = typename Elem<T>::acc;
     DeviceFacts f;
     if (int rc = device_facts(&f, err, err_len)) return rc;
@@ -222,7 +223,7 @@ int launch_fused(const T* memory, const T* weight, const T* bias, const int64_t*
             aligned16(memory) && aligned16(weight) && aligned16(out)) {
             bool launched = false;
             const int rc = launch_fused_tc<T>(memory, weight, bias, shapes, starts, loc, attn, out, B, Q, N, C, H, D,
-                                              L, P, f, stream, err, err_len, &launched);
+                                              L, P, mask, f, stream, err, err_len, &launched);
             if (rc != TD_OK || launched) return rc;
         }
     }
@@ -236,7 +237,7 @@ int launch_fused(const T* memory, const T* weight, const T* bias, const int64_t*
     if (smem > smem_cap) return fail(err, err_len, TD_ERR_ARG, "channels too large for shared memory");
     FusedArgs<T> a;
     a.memory = memory; a.weight = weight; a.bias = bias; a.loc = loc; a.attn = attn; a.out = out;
-    a.shapes = shapes; a.starts = starts; a.n_tok = N;
+    a.shapes = shapes; a.starts = starts; a.n_tok = N; a.mask = mask;
     a.B = int(B); a.Q = int(Q); a.C = int(C); a.H = int(H); a.D = int(D); a.L = int(L); a.P = int(P);
     a.R = R; a.q_tiles = int((Q + R - 1) / R);
     a.vec = (C % Elem<T>::kVec == 0) && aligned16(memory);
@@ -512,6 +513,16 @@ int td_fused_forward(int dtype, const void* memory, const void* value_weight, co
                      const void* sampling_locations, const void* attention_weights, void* out,
                      int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H, int64_t HD, int64_t L, int64_t P,
                      void* stream, char* err, size_t err_len) {
+    return td_fused_forward_masked(dtype, memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                                   sampling_locations, attention_weights, nullptr, out, B, Q, N, C, H, HD, L, P,
+                                   stream, err, err_len);
+}
+
+int td_fused_forward_masked(int dtype, const void* memory, const void* value_weight, const void* value_bias,
+                            const int64_t* spatial_shapes, const int64_t* level_start_index,
+                            const void* sampling_locations, const void* attention_weights,
+                            const uint8_t* value_padding_mask, void* out, int64_t B, int64_t Q, int64_t N, int64_t C,
+                            int64_t H, int64_t HD, int64_t L, int64_t P, void* stream, char* err, size_t err_len) {
     if (dtype_size(dtype) == 0) return fail(err, err_len, TD_ERR_ARG, "unsupported dtype code %d", dtype);
     if (int rc = check_geometry(B, Q, N, H, L, P, err, err_len)) return rc;
     if (C <= 0 || HD <= 0) return fail(err, err_len, TD_ERR_ARG, "channels and value_weight rows must be positive");
@@ -528,7 +539,7 @@ int td_fused_forward(int dtype, const void* memory, const void* value_weight, co
         return launch_fused<T>(static_cast<const T*>(memory), static_cast<const T*>(value_weight),
                                static_cast<const T*>(value_bias), spatial_shapes, level_start_index,
                                static_cast<const T*>(sampling_locations), static_cast<const T*>(attention_weights),
-                               static_cast<T*>(out), B, Q, N, C, H, D, L, P, s, err, err_len);
+                               static_cast<T*>(out), B, Q, N, C, H, D, L, P, s, err, err_len, value_padding_mask);
     });
 }
 
@@ -607,6 +618,17 @@ int td_project_forward(int dtype, const void* memory, const void* value_weight, 
                        const void* sampling_locations, const void* attention_weights, void* out,
                        int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H, int64_t HD, int64_t L, int64_t P,
                        void* workspace, size_t workspace_bytes, void* stream, char* err, size_t err_len) {
+    return td_project_forward_masked(dtype, memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                                     sampling_locations, attention_weights, nullptr, out, B, Q, N, C, H, HD, L, P,
+                                     workspace, workspace_bytes, stream, err, err_len);
+}
+
+int td_project_forward_masked(int dtype, const void* memory, const void* value_weight, const void* value_bias,
+                              const int64_t* spatial_shapes, const int64_t* level_start_index,
+                              const void* sampling_locations, const void* attention_weights,
+                              const uint8_t* value_padding_mask, void* out, int64_t B, int64_t Q, int64_t N,
+                              int64_t C, int64_t H, int64_t HD, int64_t L, int64_t P, void* workspace,
+                              size_t workspace_bytes, void* stream, char* err, size_t err_len) {
     if (dtype_size(dtype) == 0) return fail(err, err_len, TD_ERR_ARG, "unsupported dtype code %d", dtype);
     if (int rc = check_geometry(B, Q, N, H, L, P, err, err_len)) return rc;
     if (C <= 0 || HD <= 0) return fail(err, err_len, TD_ERR_ARG, "channels and value_weight rows must be positive");
@@ -631,7 +653,8 @@ int td_project_forward(int dtype, const void* memory, const void* value_weight, 
             return rc;
         return launch_sampler<T>(v, H * N * D, D, N * D, spatial_shapes, level_start_index,
                                  static_cast<const T*>(sampling_locations), static_cast<const T*>(attention_weights),
-                                 static_cast<T*>(out), B, Q, N, H, D, L, P, s, err, err_len, true);
+                                 static_cast<T*>(out), B, Q, N, H, D, L, P, s, err, err_len, true,
+                                 value_padding_mask);
     });
 }
 

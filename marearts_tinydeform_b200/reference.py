@@ -15,7 +15,7 @@ import torch.nn.functional as F
 
 
 def ma_deform_attn_reference(memory, value_weight, value_bias, spatial_shapes, level_start_index,
-                             sampling_locations, attention_weights):
+                             sampling_locations, attention_weights, value_padding_mask=None):
     """value = memory @ value_weight.T + value_bias, then multi-scale deformable attention.
 
     memory              [B, N, C]
@@ -25,11 +25,15 @@ def ma_deform_attn_reference(memory, value_weight, value_bias, spatial_shapes, l
     level_start_index   [L] int64       first token of each level
     sampling_locations  [B, Q, H, L, P, 2]  (x, y) normalised to [0, 1]
     attention_weights   [B, Q, H, L, P]     already normalised (softmax over L * P)
+    value_padding_mask  [B, N] bool or None: True zeroes that token's projected value (Deformable-DETR's
+                        input_padding_mask; an addition to the upstream signature, which has no mask)
     returns             [B, Q, H * D]
     """
     n_img, n_tok, _ = memory.shape
     _, n_qry, n_head, n_lvl, n_pt, _ = sampling_locations.shape
     value = F.linear(memory, value_weight, value_bias)                 # [B, N, H*D]
+    if value_padding_mask is not None:
+        value = value.masked_fill(value_padding_mask.to(torch.bool)[..., None], 0)
     head_dim = value.shape[-1] // n_head
     # grid_sample wants (x, y) in [-1, 1]; one image per (batch, head) pair, D channels each
     grid = sampling_locations.mul(2).sub(1).permute(0, 2, 1, 3, 4, 5)  # [B, H, Q, L, P, 2]

@@ -27,13 +27,15 @@ def batch_range(batch, world, rank):
 
 def shard_inputs(inputs, rank, world):
     """This rank's slice of full-batch inputs (memory, value_weight, value_bias, spatial_shapes, level_start_index,
-    sampling_locations, attention_weights); the weights and level metadata are shared, not sliced."""
+    sampling_locations, attention_weights[, value_padding_mask]); the weights and level metadata are shared, not
+    sliced; the padding mask, like memory, is sliced along the batch."""
     start, stop = batch_range(inputs[0].shape[0], world, rank)
-    return [t[start:stop] if i in BATCHED else t for i, t in enumerate(inputs)]
+    return [t[start:stop] if (i in BATCHED or i == 7) and t is not None else t for i, t in enumerate(inputs)]
 
 
 def ma_deform_attn_sharded(memory, value_weight, value_bias, spatial_shapes, level_start_index,
-                           sampling_locations, attention_weights, mode='auto', group=None, gather=False):
+                           sampling_locations, attention_weights, mode='auto', group=None, gather=False,
+                           value_padding_mask=None):
     """ma_deform_attn on this rank's images; with gather=True, the outputs of every rank concatenated in rank order.
 
     Each rank passes its own shard (possibly empty). Without gather there is no collective at all. With gather, the
@@ -41,7 +43,7 @@ def ma_deform_attn_sharded(memory, value_weight, value_bias, spatial_shapes, lev
     all_gather_into_tensor, and the padding is dropped; every rank must call it, in the same order.
     """
     out = ma_deform_attn(memory, value_weight, value_bias, spatial_shapes, level_start_index,
-                         sampling_locations, attention_weights, mode=mode)
+                         sampling_locations, attention_weights, mode=mode, value_padding_mask=value_padding_mask)
     if not gather:
         return out
     world = dist.get_world_size(group)

@@ -16,6 +16,12 @@ Two forms:
 Both are pinned against golden vectors written by upstream's own ma_deform_attn_reference
 (tests/golden/make_golden.py, checked by tests/test_oracle_golden.py).
 
+Value padding mask (an addition to upstream's operator, which has none): Deformable-DETR's input_padding_mask,
+value = value.masked_fill(mask[..., None], 0) right after the projection (models/ops/modules/ms_deform_attn.py of
+fundamentalvision/Deformable-DETR, not vendored here); a padded token then contributes nothing, its bias included.
+With bias=None this equals zeroing the padded memory rows before upstream's own reference, which is how the golden
+vectors pin it.
+
 Sampling rule: grid_sample with align_corners=False maps g = 2 * loc - 1 to pixel x = ((g + 1) * w - 1) / 2 =
 loc * w - 0.5; corner (x0 + dx, y0 + dy) of x0 = floor(x) has weight (dx ? fx : 1 - fx) * (dy ? fy : 1 - fy) and
 contributes only inside the map (zero padding). For finite locations, clamping x to [-2, w + 1] first changes
@@ -37,6 +43,13 @@ def _np(t):
         t = t.numpy()
     t = np.asarray(t)
     return t.astype(np.float64) if t.dtype.kind == 'f' else t.astype(np.int64)
+
+
+def _mask(m):
+    """value padding mask (torch / numpy, bool or 0/1) -> numpy bool [B, N]."""
+    if hasattr(m, 'detach'):
+        m = m.detach().cpu().numpy()
+    return np.asarray(m).astype(bool)
 
 
 def project(memory, weight, bias):
@@ -98,17 +111,21 @@ def sample(value, n_head, spatial_shapes, level_start_index, sampling_locations,
 
 
 def ma_deform_attn_oracle(memory, value_weight, value_bias, spatial_shapes, level_start_index,
-                          sampling_locations, attention_weights):
-    """Upstream ma_deform_attn_reference (reference.py:13-40) in float64 numpy: [B, Q, H*D]."""
+                          sampling_locations, attention_weights, value_padding_mask=None):
+    """Upstream ma_deform_attn_reference (reference.py:13-40) in float64 numpy: [B, Q, H*D]; padded tokens' value
+    rows zeroed after the projection."""
     H = sampling_locations.shape[2]
     value = project(memory, value_weight, value_bias)
+    if value_padding_mask is not None:
+        value = np.where(_mask(value_padding_mask)[..., None], 0.0, value)
     return sample(value, H, spatial_shapes, level_start_index, sampling_locations, attention_weights)
 
 
 def fused_order(memory, value_weight, value_bias, spatial_shapes, level_start_index,
-                sampling_locations, attention_weights):
+                sampling_locations, attention_weights, value_padding_mask=None):
     """The same result in the fused order (upstream csrc/ma_deform_fused.cu:6-14):
-    out[d] = W[hD + d] . (sum_s w_s memory[t_s]) + b[hD + d] * sum_s w_s.  Used as an independent property check."""
+    out[d] = W[hD + d] . (sum_s w_s memory[t_s]) + b[hD + d] * sum_s w_s, the sums over corners on unpadded tokens.
+    Used as an independent property check."""
     mem, W = _np(memory), _np(value_weight)
     b = None if value_bias is None else _np(value_bias)
     shapes, starts = _np(spatial_shapes), _np(level_start_index)
@@ -119,9 +136,13 @@ def fused_order(memory, value_weight, value_bias, spatial_shapes, level_start_in
     m = np.zeros((B, Q, H, C))
     wsum = np.zeros((B, Q, H))
     bi = np.arange(B).reshape(B, 1, 1, 1)
+    pad = None if value_padding_mask is None else _mask(value_padding_mask)
     for lvl in range(L):
         tok, wt = level_corners(loc[:, :, :, lvl], attn[:, :, :, lvl], int(shapes[lvl, 0]), int(shapes[lvl, 1]),
                                 int(starts[lvl]), N)
+        if pad is not None:  # a corner on a padded token counts as outside
+            hit = pad[bi[..., None], np.maximum(tok, 0)] & (tok >= 0)
+            tok, wt = np.where(hit, -1, tok), np.where(hit, 0.0, wt)
         for k in range(4):
             t = tok[..., k]
             rows = np.where((t >= 0)[..., None], mem[bi, np.maximum(t, 0)], 0.0)   # [B, Q, H, P, C]
@@ -135,7 +156,7 @@ def fused_order(memory, value_weight, value_bias, spatial_shapes, level_start_in
 
 
 def oracle_rows(memory, value_weight, value_bias, spatial_shapes, level_start_index, sampling_locations,
-                attention_weights, queries):
+                attention_weights, queries, value_padding_mask=None):
     """Oracle output for selected (b, q) pairs only: [len(queries), H*D] float64.
 
     Projects only the memory rows those queries touch, so full-size configs can be spot-checked in seconds.
@@ -148,6 +169,7 @@ def oracle_rows(memory, value_weight, value_bias, spatial_shapes, level_start_in
     _, Q, H, L, P, _ = loc.shape
     D = W.shape[0] // H
     out = np.zeros((len(queries), H * D))
+    pad = None if value_padding_mask is None else _mask(value_padding_mask)
     for i, (bb, qq) in enumerate(queries):
         acc = np.zeros((H, D))
         for lvl in range(L):
@@ -156,6 +178,8 @@ def oracle_rows(memory, value_weight, value_bias, spatial_shapes, level_start_in
             for h in range(H):
                 t, w = tok[h].ravel(), wt[h].ravel()
                 keep = t >= 0
+                if pad is not None:
+                    keep &= ~pad[bb, np.maximum(t, 0)]
                 if not keep.any():
                     continue
                 rows = mem[bb, t[keep]] @ W[h * D:(h + 1) * D].T                 # [k, D]
@@ -167,7 +191,7 @@ def oracle_rows(memory, value_weight, value_bias, spatial_shapes, level_start_in
 
 
 def torch_port(memory, value_weight, value_bias, spatial_shapes, level_start_index,
-               sampling_locations, attention_weights):
+               sampling_locations, attention_weights, value_padding_mask=None):
     """reference.py:13-40 on torch's CPU operators, in the inputs' dtype (the timed CPU baseline)."""
     import torch
     import torch.nn.functional as F
@@ -175,6 +199,8 @@ def torch_port(memory, value_weight, value_bias, spatial_shapes, level_start_ind
     B, N, _ = memory.shape
     _, Q, H, L, P, _ = sampling_locations.shape
     value = F.linear(memory, value_weight, value_bias)
+    if value_padding_mask is not None:
+        value = value.masked_fill(value_padding_mask.to(torch.bool)[..., None], 0)
     D = value.shape[-1] // H
     grid = (2 * sampling_locations - 1).transpose(1, 2).reshape(B * H, Q, L, P, 2)
     heads = value.view(B, N, H, D).permute(0, 2, 3, 1).reshape(B * H, D, N)

@@ -8,7 +8,11 @@ Run once, in a checkout that has upstream MareArts/marearts-tinydeform v0.1.1 im
 For every case of tests/cases.py SMALL_CASES (plus the boundary-location case) it stores the inputs in their own
 dtype and upstream's result computed in float64 on the upcast inputs, as upstream's tests do for float16 / bfloat16
 (tests/test_correctness.py:79). bfloat16 arrays are stored as their uint16 bit patterns. The fixture is small
-(well under 1 MB) and is what pins the oracle: tests/test_oracle_golden.py checks the oracle against it.
+(a few MB) and is what pins the oracle: tests/test_oracle_golden.py checks the oracle against it.
+
+Masked cases (the value padding mask is an addition; upstream has none): inputs without bias plus a bool mask
+[B, N]; the expected result is upstream's reference run on memory with the padded rows zeroed, which is what
+zeroing those tokens' projected value means when there is no bias.
 """
 
 import argparse
@@ -25,6 +29,22 @@ from cases import SMALL_CASES, boundary_case, make, upcast  # noqa: E402
 
 NAMES = ('memory', 'value_weight', 'value_bias', 'spatial_shapes', 'level_start_index', 'sampling_locations',
          'attention_weights')
+
+# name, B, Q, H, D, C, levels, P, dtype, padded fraction, images padded whole
+MASKED_CASES = [
+    ('masked-fp32', 2, 12, 8, 32, 256, [(10, 10), (5, 5), (3, 3)], 4, torch.float32, 0.3, ()),
+    ('masked-fp16', 2, 9, 8, 32, 256, [(10, 15), (5, 8), (3, 4), (2, 2)], 4, torch.float16, 0.5, ()),
+    ('masked-bf16-one-image-padded', 2, 10, 4, 16, 64, [(8, 12), (4, 6)], 8, torch.bfloat16, 0.2, (1,)),
+]
+
+
+def masked_case(i, B, Q, H, D, C, levels, P, dtype, frac, whole):
+    inputs = list(make(B, Q, H, D, C, levels, P, dtype=dtype, bias=False, seed=100 + i))
+    g = torch.Generator().manual_seed(200 + i)
+    mask = torch.rand(B, inputs[0].shape[1], generator=g) < frac
+    for b in whole:
+        mask[b] = True
+    return inputs, mask
 
 
 def to_numpy(t):
@@ -48,6 +68,19 @@ def main():
     cases.append(('boundary-locations', boundary_case(), torch.float32))
     arrays, manifest = {}, []
     with torch.no_grad():
+        for i, (name, B, Q, H, D, C, levels, P, dtype, frac, whole) in enumerate(MASKED_CASES):
+            inputs, mask = masked_case(i, B, Q, H, D, C, levels, P, dtype, frac, whole)
+            zeroed = list(upcast(inputs))
+            zeroed[0] = zeroed[0].masked_fill(mask[..., None], 0)
+            ref64 = upstream_reference(*zeroed)
+            key = name
+            for field, t in zip(NAMES, inputs):
+                if t is not None:
+                    arrays[f'{key}/{field}'] = to_numpy(t)
+            arrays[f'{key}/value_padding_mask'] = mask.numpy().astype(np.uint8)
+            arrays[f'{key}/expected_f64'] = ref64.numpy()
+            manifest.append({'key': key, 'dtype': str(dtype).replace('torch.', ''), 'bias': False,
+                             'shape': list(ref64.shape), 'masked': True})
         for name, inputs, dtype in cases:
             ref64 = upstream_reference(*upcast(inputs))
             key = name.replace(' ', '_')

@@ -25,6 +25,23 @@ def test_cpu_path_is_reference():
             assert torch.equal(ma_deform_attn(*args, mode=mode), ma_deform_attn_reference(*args))
 
 
+def test_value_padding_mask_on_the_cpu_route():
+    """The mask zeroes padded tokens' projected value (Deformable-DETR's input_padding_mask): on CPU the reference
+    applies it; with no bias that equals zeroing those memory rows; an all-False mask changes nothing."""
+    args = make(2, 9, 2, 8, 16, [(6, 7), (3, 4)], 2, bias=False, seed=4)
+    N = args[0].shape[1]
+    mask = torch.rand(2, N, generator=torch.Generator().manual_seed(1)) < 0.4
+    zeroed = list(args)
+    zeroed[0] = args[0].masked_fill(mask[..., None], 0)
+    with torch.inference_mode():
+        got = ma_deform_attn(*args, value_padding_mask=mask)
+        torch.testing.assert_close(got, ma_deform_attn_reference(*zeroed), atol=1e-6, rtol=1e-5)
+        none = torch.zeros_like(mask)
+        assert torch.equal(ma_deform_attn(*args, value_padding_mask=none), ma_deform_attn(*args))
+        full = torch.ones_like(mask)
+        assert ma_deform_attn(*args, value_padding_mask=full).abs().max().item() == 0.0
+
+
 def test_bad_mode_is_a_value_error():
     args = make(1, 4, 2, 8, 16, [(6, 7)], 2)
     with pytest.raises(ValueError):

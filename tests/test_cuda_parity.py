@@ -32,10 +32,10 @@ def oracle(args):
     return torch.from_numpy(O.ma_deform_attn_oracle(*[t if t is None else t.cpu() for t in args]))
 
 
-def check(name, args, ref, atol, rtol, modes=MODES):
+def check(name, args, ref, atol, rtol, modes=MODES, mask=None):
     with torch.inference_mode():
         for mode in modes:
-            got = ma_deform_attn(*args, mode=mode).double().cpu()
+            got = ma_deform_attn(*args, mode=mode, value_padding_mask=mask).double().cpu()
             assert got.shape == ref.shape, f'{name} [{mode}]'
             err = (got - ref).abs().max().item() if got.numel() else 0.0
             assert torch.allclose(got, ref, atol=atol, rtol=rtol), \
@@ -72,10 +72,47 @@ def test_head_rows_that_are_not_a_power_of_two_vectors(cuda):
 
 
 def test_golden_vectors_through_cuda(policy):
-    from test_oracle_golden import CASES as GOLDEN
+    from test_oracle_golden import CASES as GOLDEN, MASKS
     for key, dtype, inputs, expected, _ in GOLDEN:
         atol, rtol = TOL[dtype]
-        check(f'golden {key} {policy}', to(inputs, 'cuda'), expected.double(), atol, rtol)
+        mask = MASKS.get(key)
+        check(f'golden {key} {policy}', to(inputs, 'cuda'), expected.double(), atol, rtol,
+              mask=None if mask is None else mask.cuda())
+
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.float16, torch.bfloat16])
+def test_value_padding_mask(policy, dtype):
+    """The value padding mask in both orders and every kernel family: random masks (some images fully padded)
+    against the oracle with the mask; an all-False mask gives the unmasked result bit for bit."""
+    for i, (B, Q, H, D, C, levels, P) in enumerate((
+            (2, 33, 8, 32, 256, [(12, 13), (6, 7), (3, 4)], 4),   # tensor-core shapes
+            (3, 17, 4, 16, 64, [(9, 11), (5, 6)], 4),
+            (2, 9, 3, 10, 30, [(5, 7), (3, 4)], 4))):             # odd channels: CUDA-core kernels
+        args = make(B, Q, H, D, C, levels, P, dtype=dtype, seed=40 + i)
+        N = args[0].shape[1]
+        mask = torch.rand(B, N, generator=torch.Generator().manual_seed(i)) < 0.35
+        if i == 1:
+            mask[-1] = True  # the last image fully padded
+        ref = torch.from_numpy(O.ma_deform_attn_oracle(*upcast(args), value_padding_mask=mask))
+        dev = to(args, 'cuda')
+        check(f'mask case {i} {dtype} {policy}', dev, ref, *TOL[dtype], mask=mask.cuda())
+        with torch.inference_mode():
+            for mode in ('fused', 'project'):
+                none = torch.zeros(B, N, dtype=torch.bool, device='cuda')
+                assert torch.equal(ma_deform_attn(*dev, mode=mode, value_padding_mask=none),
+                                   ma_deform_attn(*dev, mode=mode)), f'all-False mask {mode} {dtype}'
+
+
+def test_value_padding_mask_is_checked(cuda):
+    args = to(make(2, 8, 2, 8, 16, [(6, 7), (3, 4)], 2), cuda)
+    N = args[0].shape[1]
+    for bad in (torch.zeros(2, N, device=cuda),                       # not bool
+                torch.zeros(2, N - 1, dtype=torch.bool, device=cuda),  # wrong shape
+                torch.zeros(2, N, dtype=torch.bool)):                  # wrong device
+        for mode in ('fused', 'project'):
+            with pytest.raises(RuntimeError):
+                with torch.inference_mode():
+                    ma_deform_attn(*args, mode=mode, value_padding_mask=bad)
 
 
 def test_unaligned_memory(cuda):

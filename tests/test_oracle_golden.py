@@ -15,6 +15,9 @@ NAMES = ('memory', 'value_weight', 'value_bias', 'spatial_shapes', 'level_start_
 DTYPES = {'float32': torch.float32, 'float16': torch.float16, 'bfloat16': torch.bfloat16, 'float64': torch.float64}
 
 
+MASKS = {}  # key -> value padding mask (bool [B, N]) of the masked cases
+
+
 def load_golden():
     z = np.load(GOLDEN)
     manifest = json.loads(bytes(z['manifest']).decode())
@@ -34,6 +37,8 @@ def load_golden():
                 t = torch.from_numpy(a.copy())
             inputs.append(t)
         native = torch.from_numpy(z[f'{key}/expected_native']) if f'{key}/expected_native' in z else None
+        if f'{key}/value_padding_mask' in z:
+            MASKS[key] = torch.from_numpy(z[f'{key}/value_padding_mask'].astype(bool))
         cases.append((key, dtype, inputs, torch.from_numpy(z[f'{key}/expected_f64']), native))
     return cases
 
@@ -50,8 +55,9 @@ def test_golden_fixture_is_complete():
     keys = {c[0] for c in CASES}
     assert len(CASES) >= 13
     for must in ('tiny', 'far-outside', 'no-bias', 'max-level-points', 'odd-channels', 'boundary-locations',
-                 'narrow-heads-bf16', 'float64'):
+                 'narrow-heads-bf16', 'float64', 'masked-fp32', 'masked-fp16', 'masked-bf16-one-image-padded'):
         assert must in keys
+    assert set(MASKS) == {'masked-fp32', 'masked-fp16', 'masked-bf16-one-image-padded'}
     for key, dtype, inputs, _, _ in CASES:
         assert inputs[0].dtype == dtype, key
 
@@ -59,14 +65,14 @@ def test_golden_fixture_is_complete():
 @pytest.mark.parametrize('case', CASES, ids=IDS)
 def test_numpy_oracle_matches_upstream(case):
     key, _, inputs, expected, _ = case
-    got = O.ma_deform_attn_oracle(*inputs)
+    got = O.ma_deform_attn_oracle(*inputs, value_padding_mask=MASKS.get(key))
     np.testing.assert_allclose(got, expected.numpy(), rtol=1e-12, atol=1e-12, err_msg=key)
 
 
 @pytest.mark.parametrize('case', CASES, ids=IDS)
 def test_fused_order_matches_upstream(case):
     key, _, inputs, expected, _ = case
-    got = O.fused_order(*inputs)
+    got = O.fused_order(*inputs, value_padding_mask=MASKS.get(key))
     np.testing.assert_allclose(got, expected.numpy(), rtol=1e-10, atol=1e-10, err_msg=key)
 
 
@@ -77,7 +83,7 @@ def test_row_oracle_matches_upstream(case):
     if Q == 0:
         return
     picks = [(b, q) for b in range(B) for q in range(0, Q, max(1, Q // 5))]
-    got = O.oracle_rows(*inputs, picks)
+    got = O.oracle_rows(*inputs, picks, value_padding_mask=MASKS.get(key))
     want = np.stack([expected[b, q].numpy() for b, q in picks])
     np.testing.assert_allclose(got, want, rtol=1e-10, atol=1e-10, err_msg=key)
 
@@ -85,7 +91,7 @@ def test_row_oracle_matches_upstream(case):
 @pytest.mark.parametrize('case', CASES, ids=IDS)
 def test_torch_port_matches_upstream(case):
     key, _, inputs, expected, native = case
-    got = O.torch_port(*upcast(inputs))
+    got = O.torch_port(*upcast(inputs), value_padding_mask=MASKS.get(key))
     torch.testing.assert_close(got, expected, rtol=1e-12, atol=1e-12, msg=key)
     if native is not None:  # same operators in float32: equal to upstream's float32 result up to rounding
         torch.testing.assert_close(O.torch_port(*inputs), native, rtol=1e-5, atol=1e-6, msg=key)
@@ -96,7 +102,7 @@ def test_package_reference_matches_upstream(case):
     from marearts_tinydeform_b200 import ma_deform_attn_reference
     key, _, inputs, expected, native = case
     with torch.no_grad():
-        got = ma_deform_attn_reference(*upcast(inputs))
+        got = ma_deform_attn_reference(*upcast(inputs), value_padding_mask=MASKS.get(key))
     torch.testing.assert_close(got, expected, rtol=1e-12, atol=1e-12, msg=key)
     if native is not None:
         with torch.no_grad():

@@ -49,6 +49,13 @@ def _worker(rank, world, port, batch, mode, results):
         start, stop = batch_range(batch, world, rank)
         ok_local = mine.shape[0] == stop - start and torch.allclose(mine, want[start:stop], atol=1e-6)
         ok_all = every.shape == want.shape and torch.allclose(every, want, atol=1e-6)
+        # the value padding mask is sliced with the batch
+        mask = torch.rand(batch, full[0].shape[1], generator=torch.Generator().manual_seed(5)) < 0.3
+        local_m = shard_inputs(full + [mask], rank, world)
+        with torch.inference_mode():
+            masked = ma_deform_attn_sharded(*local_m[:7], gather=True, value_padding_mask=local_m[7])
+            want_m = ma_deform_attn_reference(*full, value_padding_mask=mask)
+        ok_all = ok_all and masked.shape == want_m.shape and torch.allclose(masked, want_m, atol=1e-6)
         results[rank] = (bool(ok_local), bool(ok_all))
     finally:
         dist.destroy_process_group()
