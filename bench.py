@@ -240,10 +240,15 @@ def run_ours(args):
     N, C, H, D, L, P, Q = base[0].shape[1], cfg['C'], cfg['H'], cfg['D'], len(cfg['levels']), cfg['P'], cfg['Q']
     e = base[0].element_size()
     outs = [torch.empty(B, Q, H * D, dtype=base[0].dtype, device=dev) for _ in range(2)]
+    # optional value padding mask: a seeded random fraction of every image's tokens padded
+    mask = None
+    if args.padding_mask > 0:
+        gm = torch.Generator(device=dev).manual_seed(77)
+        mask = torch.rand(B, N, generator=gm, device=dev) < args.padding_mask
 
     def call(i):
         mem, loc, attn = pool[i % len(pool)]
-        return ma_deform_attn(mem, W, bias, shapes, starts, loc, attn, mode=args.mode)
+        return ma_deform_attn(mem, W, bias, shapes, starts, loc, attn, mode=args.mode, value_padding_mask=mask)
 
     with torch.inference_mode():
         g, launches = graph_time_us(call, args.steps, args.warmup)
@@ -279,7 +284,8 @@ def run_ours(args):
 
         # hot-L2 time (upstream's method: one input set replayed)
         gh, _ = graph_time_us(lambda i: ma_deform_attn(base[0], W, bias, shapes, starts, base[5], base[6],
-                                                       mode=args.mode), args.steps, args.warmup)
+                                                       mode=args.mode, value_padding_mask=mask),
+                              args.steps, args.warmup)
         t_hot = barrier_max(time_graph(gh, args.steps, reps=3), world)
         del gh
 
@@ -294,7 +300,7 @@ def run_ours(args):
             dev_in = [t.to(dev, non_blocking=True) for t in host]
             if bias is None:
                 dev_in.insert(2, None)
-            out = ma_deform_attn(*dev_in, mode=args.mode)
+            out = ma_deform_attn(*dev_in, mode=args.mode, value_padding_mask=mask)
             out_host.copy_(out, non_blocking=True)
 
         for _ in range(3):
@@ -321,7 +327,9 @@ def run_ours(args):
             'metric': METRIC, 'value': round(t_call, 3), 'unit': 'us', 'n_gpus': world, 'steps': args.steps,
             'warmup': args.warmup, 'ms_per_step': round(t_call / 1e3, 6), 'higher_is_better': False,
             'scaling': 'weak', 'vs_baseline': None, 'dtype': str(cfg['dtype']).replace('torch.', ''),
-            'data': 'synthetic (seeded, BASELINE config shapes)', 'config': config_dict(args.config, world, mode),
+            'data': 'synthetic (seeded, BASELINE config shapes)',
+            'config': dict(config_dict(args.config, world, mode),
+                           **({'value_padding_mask': args.padding_mask} if mask is not None else {})),
             'mode': mode, 'queries_per_s': round(B * Q * world / (t_call * 1e-6), 1),
             'hot_l2_us': round(t_hot, 3), 'kernel_us': {k: round(v, 3) for k, v in kernels.items()},
             'roofline': {'bound': 'hbm', 'kernel': top, 'achieved': round(achieved, 1), 'peak': hbm,
@@ -381,6 +389,8 @@ def main():
     ap.add_argument('--mode', default='auto', choices=('auto', 'fused', 'project'))
     ap.add_argument('--impl', default='ours', choices=('ours', 'reference'))
     ap.add_argument('--no-cpu', action='store_true')
+    ap.add_argument('--padding-mask', type=float, default=0.0,
+                    help='fraction of tokens padded by a random value padding mask (0: no mask)')
     ap.add_argument('--sweep', action='store_true')
     ap.add_argument('--dtype', nargs='+', default=['float16', 'bfloat16', 'float32'])
     args = ap.parse_args()
