@@ -246,9 +246,17 @@ def run_ours(args):
         gm = torch.Generator(device=dev).manual_seed(77)
         mask = torch.rand(B, N, generator=gm, device=dev) < args.padding_mask
 
+    # optional output_proj (the decoder's nn.Linear on the result, [C, H * D]), chained behind the attention
+    wo = bo = None
+    if args.output_proj:
+        go = torch.Generator(device=dev).manual_seed(78)
+        wo = ((torch.rand(C, H * D, generator=go, device=dev) * 2 - 1) * (6 / (C + H * D)) ** 0.5).to(W.dtype)
+        bo = torch.zeros(C, dtype=W.dtype, device=dev)
+
     def call(i):
         mem, loc, attn = pool[i % len(pool)]
-        return ma_deform_attn(mem, W, bias, shapes, starts, loc, attn, mode=args.mode, value_padding_mask=mask)
+        return ma_deform_attn(mem, W, bias, shapes, starts, loc, attn, mode=args.mode, value_padding_mask=mask,
+                              output_weight=wo, output_bias=bo)
 
     with torch.inference_mode():
         g, launches = graph_time_us(call, args.steps, args.warmup)
@@ -284,7 +292,8 @@ def run_ours(args):
 
         # hot-L2 time (upstream's method: one input set replayed)
         gh, _ = graph_time_us(lambda i: ma_deform_attn(base[0], W, bias, shapes, starts, base[5], base[6],
-                                                       mode=args.mode, value_padding_mask=mask),
+                                                       mode=args.mode, value_padding_mask=mask,
+                                                       output_weight=wo, output_bias=bo),
                               args.steps, args.warmup)
         t_hot = barrier_max(time_graph(gh, args.steps, reps=3), world)
         del gh
@@ -292,7 +301,7 @@ def run_ours(args):
         # end to end through the public API: pinned host inputs copied in, result copied out, every step
         host = [t.cpu().pin_memory() for t in (base[0], W, bias, shapes, starts, base[5], base[6]) if t is not None]
         h2d = sum(t.numel() * t.element_size() for t in host)
-        out_host = torch.empty((B, Q, H * D), dtype=base[0].dtype).pin_memory()
+        out_host = torch.empty((B, Q, C if wo is not None else H * D), dtype=base[0].dtype).pin_memory()
         d2h = out_host.numel() * out_host.element_size()
         e2e_steps = max(10, min(args.steps, 200))
 
@@ -300,7 +309,7 @@ def run_ours(args):
             dev_in = [t.to(dev, non_blocking=True) for t in host]
             if bias is None:
                 dev_in.insert(2, None)
-            out = ma_deform_attn(*dev_in, mode=args.mode, value_padding_mask=mask)
+            out = ma_deform_attn(*dev_in, mode=args.mode, value_padding_mask=mask, output_weight=wo, output_bias=bo)
             out_host.copy_(out, non_blocking=True)
 
         for _ in range(3):
@@ -329,7 +338,8 @@ def run_ours(args):
             'scaling': 'weak', 'vs_baseline': None, 'dtype': str(cfg['dtype']).replace('torch.', ''),
             'data': 'synthetic (seeded, BASELINE config shapes)',
             'config': dict(config_dict(args.config, world, mode),
-                           **({'value_padding_mask': args.padding_mask} if mask is not None else {})),
+                           **({'value_padding_mask': args.padding_mask} if mask is not None else {}),
+                           **({'output_proj': [C, H * D]} if wo is not None else {})),
             'mode': mode, 'queries_per_s': round(B * Q * world / (t_call * 1e-6), 1),
             'hot_l2_us': round(t_hot, 3), 'kernel_us': {k: round(v, 3) for k, v in kernels.items()},
             'roofline': {'bound': 'hbm', 'kernel': top, 'achieved': round(achieved, 1), 'peak': hbm,
@@ -389,6 +399,8 @@ def main():
     ap.add_argument('--mode', default='auto', choices=('auto', 'fused', 'project'))
     ap.add_argument('--impl', default='ours', choices=('ours', 'reference'))
     ap.add_argument('--no-cpu', action='store_true')
+    ap.add_argument('--output-proj', action='store_true',
+                    help='chain the decoder output_proj ([C, H*D] nn.Linear) behind the attention')
     ap.add_argument('--padding-mask', type=float, default=0.0,
                     help='fraction of tokens padded by a random value padding mask (0: no mask)')
     ap.add_argument('--sweep', action='store_true')

@@ -86,6 +86,15 @@ TD_API int td_value_proj(int dtype, const void* memory, const void* value_weight
                   void* stream, char* err, size_t err_len);
 
 /*
+ * y = x @ weight^T + bias for row-major x [M, K], weight [Nout, K], bias [Nout] or NULL, y [M, Nout]: the
+ * tensor-core projection kernel, launched with programmatic dependent launch so that its set-up overlaps the kernel
+ * before it in the stream (it waits for that kernel before reading x). For the decoder's output_proj right after
+ * ma_deform_attn (the nn.Linear callers apply to its result, upstream README.md:11); no counterpart in upstream.
+ */
+TD_API int td_linear(int dtype, const void* x, const void* weight, const void* bias, void* y, int64_t M, int64_t K,
+                     int64_t Nout, void* stream, char* err, size_t err_len);
+
+/*
  * Sampling of a projected value at explicit element strides: value element (b, token, head, d) is at
  * b * s_img + token * s_tok + head * s_head + d. td_sample_forward is the case (N*HD, HD, D); the head-major value
  * td_project_forward samples is (H*N*D, D, N*D). Generalises upstream sample_forward

@@ -60,7 +60,8 @@ def choose_mode(memory, value_weight, sampling_locations):
 
 
 def ma_deform_attn(memory, value_weight, value_bias, spatial_shapes, level_start_index,
-                   sampling_locations, attention_weights, mode='auto', value_padding_mask=None):
+                   sampling_locations, attention_weights, mode='auto', value_padding_mask=None,
+                   output_weight=None, output_bias=None):
     """value = memory @ value_weight.T + value_bias, then multi-scale deformable attention; [B, Q, H * D].
 
     Same arguments, shapes and result as ma_deform_attn_reference (grid_sample, bilinear, zero padding,
@@ -70,20 +71,29 @@ def ma_deform_attn(memory, value_weight, value_bias, spatial_shapes, level_start
     value_padding_mask (an addition; the upstream operator has none): bool [B, N], True = padded token. As
     Deformable-DETR's input_padding_mask, the projected value of a padded token is zeroed (its bias included)
     before sampling, so it contributes nothing.
+
+    output_weight / output_bias (an addition): the decoder's output_proj (an nn.Linear [C_out, H * D]) applied to the
+    result, so the call returns [B, Q, C_out]; on CUDA it runs as a tensor-core GEMM queued right behind the
+    attention kernel, overlapping its start with it.
     """
     if mode not in MODES:
         raise ValueError(f'mode must be one of {MODES}, got {mode!r}')
+    if output_bias is not None and output_weight is None:
+        raise ValueError('output_bias needs output_weight')
     if not memory.is_cuda:
-        return ma_deform_attn_reference(memory, value_weight, value_bias, spatial_shapes, level_start_index,
-                                        sampling_locations, attention_weights, value_padding_mask)
+        out = ma_deform_attn_reference(memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                                       sampling_locations, attention_weights, value_padding_mask)
+        return out if output_weight is None else torch.nn.functional.linear(out, output_weight, output_bias)
     _native.load()  # raises RuntimeError when the native library is missing: there is no fallback
     if torch.is_grad_enabled() and any(
             t is not None and t.requires_grad
-            for t in (memory, value_weight, value_bias, sampling_locations, attention_weights)):
+            for t in (memory, value_weight, value_bias, sampling_locations, attention_weights, output_weight,
+                      output_bias)):
         raise RuntimeError('ma_deform_attn is inference only: run it under torch.no_grad() / '
                            'torch.inference_mode(), or use ma_deform_attn_reference for training')
     if mode == 'auto':
         mode = choose_mode(memory, value_weight, sampling_locations)
     run = _native.fused_forward if mode == 'fused' else _native.project_forward
-    return run(memory, value_weight, value_bias, spatial_shapes, level_start_index, sampling_locations,
-               attention_weights, value_padding_mask)
+    out = run(memory, value_weight, value_bias, spatial_shapes, level_start_index, sampling_locations,
+              attention_weights, value_padding_mask)
+    return out if output_weight is None else _native.linear(out, output_weight, output_bias)

@@ -34,6 +34,7 @@ SIGNATURES = {
     'td_project_workspace_bytes': (_sz, [_ip, _i64, _i64, _i64]),
     'td_project_forward': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                  _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp, _cp, _sz]),
+    'td_linear': (_ip, [_ip, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _cp, _sz]),
     'td_fused_forward_masked': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                       _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _cp, _sz]),
     'td_project_forward_masked': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
@@ -222,6 +223,34 @@ def project_forward(memory, value_weight, value_bias, spatial_shapes, level_star
                   _ptr(att), _ptr(mask), _ptr(out), B, Q, N, C, H, HD, L, P, _ptr(ws), ws_bytes,
                   _stream(memory.device))
     return out
+
+
+def linear(x, weight, bias):
+    """y = x @ weight.T + bias over the last dimension of x, through td_linear (the tensor-core projection kernel,
+    launched to overlap the kernel before it): the decoder's output_proj after ma_deform_attn."""
+    lib = load()
+    if not x.is_cuda:
+        raise RuntimeError('inputs must be CUDA tensors')
+    if x.dtype not in DTYPE_CODE:
+        raise RuntimeError(f'unsupported dtype {x.dtype}')
+    K = x.size(-1)
+    if weight.dim() != 2 or weight.size(1) != K:
+        raise RuntimeError('output_weight must be [C_out, K] with K = the last dimension of the input')
+    if weight.device != x.device or weight.dtype != x.dtype:
+        raise RuntimeError('output_weight must have the device and dtype of the input')
+    Nout = weight.size(0)
+    if bias is not None and (bias.device != x.device or bias.dtype != x.dtype or bias.dim() != 1
+                             or bias.size(0) != Nout):
+        raise RuntimeError('output_bias must be [C_out] like output_weight, same device and dtype')
+    xs, w, b = _dense(x, weight, bias)
+    y = torch.empty(tuple(x.shape[:-1]) + (Nout,), dtype=x.dtype, device=x.device)
+    M = xs.numel() // K if K else 0
+    if M == 0:
+        return y
+    with torch.cuda.device(x.device):
+        _call(lib.td_linear, DTYPE_CODE[x.dtype], _ptr(xs), _ptr(w), _ptr(b), _ptr(y), M, K, Nout,
+              _stream(x.device))
+    return y
 
 
 def sample_forward(value, heads, spatial_shapes, level_start_index, sampling_locations, attention_weights):

@@ -584,6 +584,23 @@ int td_value_proj(int dtype, const void* memory, const void* value_weight, const
     });
 }
 
+int td_linear(int dtype, const void* x, const void* weight, const void* bias, void* y, int64_t M, int64_t K,
+              int64_t Nout, void* stream, char* err, size_t err_len) {
+    if (dtype_size(dtype) == 0) return fail(err, err_len, TD_ERR_ARG, "unsupported dtype code %d", dtype);
+    if (M < 0 || K <= 0 || Nout <= 0) return fail(err, err_len, TD_ERR_ARG, "linear needs M >= 0, K > 0, Nout > 0");
+    if (M > INT32_MAX || K > INT32_MAX || Nout > INT32_MAX) return fail(err, err_len, TD_ERR_ARG, "size too large");
+    if (M == 0) return TD_OK;
+    if (!x || !weight || !y) return fail(err, err_len, TD_ERR_ARG, "null tensor pointer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return dispatch(dtype, [&](auto tag) {
+        using T = decltype(tag);
+        // one "image" of M tokens and one "head" of Nout channels: the projection kernel in its [B, N, HD] layout,
+        // launched with programmatic dependent launch so it starts under the kernel before it
+        return launch_proj<T>(static_cast<const T*>(x), static_cast<const T*>(weight), static_cast<const T*>(bias),
+                              static_cast<T*>(y), 1, M, K, 1, Nout, 0, s, err, err_len, true);
+    });
+}
+
 int td_sample_strided(int dtype, const void* value, int64_t s_img, int64_t s_tok, int64_t s_head,
                       const int64_t* spatial_shapes, const int64_t* level_start_index,
                       const void* sampling_locations, const void* attention_weights, void* out,

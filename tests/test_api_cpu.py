@@ -42,6 +42,17 @@ def test_value_padding_mask_on_the_cpu_route():
         assert ma_deform_attn(*args, value_padding_mask=full).abs().max().item() == 0.0
 
 
+def test_output_proj_on_the_cpu_route():
+    args = make(1, 10, 2, 8, 16, [(6, 7), (3, 4)], 2)
+    wo = torch.randn(12, 16, generator=torch.Generator().manual_seed(2)) * 0.1
+    bo = torch.randn(12, generator=torch.Generator().manual_seed(3)) * 0.1
+    with torch.inference_mode():
+        got = ma_deform_attn(*args, output_weight=wo, output_bias=bo)
+        assert torch.equal(got, torch.nn.functional.linear(ma_deform_attn_reference(*args), wo, bo))
+    with pytest.raises(ValueError):
+        ma_deform_attn(*args, output_bias=bo)
+
+
 def test_bad_mode_is_a_value_error():
     args = make(1, 4, 2, 8, 16, [(6, 7)], 2)
     with pytest.raises(ValueError):

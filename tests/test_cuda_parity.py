@@ -103,6 +103,47 @@ def test_value_padding_mask(policy, dtype):
                                    ma_deform_attn(*dev, mode=mode)), f'all-False mask {mode} {dtype}'
 
 
+@pytest.mark.parametrize('dtype', [torch.float32, torch.float16, torch.bfloat16])
+def test_output_proj(policy, dtype):
+    """The decoder's output_proj chained behind the attention (output_weight / output_bias): against the oracle's
+    result projected in float64, both orders, with and without bias; odd widths take the CUDA-core GEMM."""
+    g = torch.Generator().manual_seed(9)
+    for B, Q, H, D, C, levels, P, c_out in ((2, 33, 8, 32, 256, [(12, 13), (6, 7)], 4, 256),
+                                            (1, 150, 4, 16, 64, [(9, 11), (5, 6)], 4, 96),
+                                            (2, 9, 3, 10, 30, [(5, 7), (3, 4)], 4, 20)):
+        args = make(B, Q, H, D, C, levels, P, dtype=dtype, seed=Q)
+        HD = H * D
+        wo = ((torch.rand(c_out, HD, generator=g) * 2 - 1) / HD ** 0.5).to(dtype)
+        for bo in (((torch.rand(c_out, generator=g) * 2 - 1) * 0.05).to(dtype), None):
+            attn = O.ma_deform_attn_oracle(*upcast(args))
+            want = attn @ wo.double().numpy().T + (0 if bo is None else bo.double().numpy())
+            dev = to(args, 'cuda')
+            atol, rtol = TOL[dtype]
+            with torch.inference_mode():
+                for mode in MODES:
+                    got = ma_deform_attn(*dev, mode=mode, output_weight=wo.cuda(),
+                                         output_bias=None if bo is None else bo.cuda()).double().cpu()
+                    assert got.shape == (B, Q, c_out)
+                    err = (got - torch.from_numpy(want)).abs().max().item()
+                    assert torch.allclose(got, torch.from_numpy(want), atol=atol, rtol=rtol), \
+                        f'output_proj {dtype} {mode} c_out={c_out} bias={bo is not None}: {err:.3g}'
+
+
+def test_linear_matches_torch(cuda):
+    """td_linear alone on assorted shapes (tensor-core and CUDA-core paths), against float64."""
+    g = torch.Generator().manual_seed(3)
+    for dtype in (torch.float32, torch.float16, torch.bfloat16, torch.float64):
+        for M, K, N in ((300, 256, 256), (1000, 64, 128), (7, 30, 20), (129, 96, 48)):
+            x = (torch.rand(M, K, generator=g) * 2 - 1).to(dtype)
+            w = ((torch.rand(N, K, generator=g) * 2 - 1) / K ** 0.5).to(dtype)
+            b = ((torch.rand(N, generator=g) * 2 - 1) * 0.1).to(dtype)
+            want = x.double() @ w.double().T + b.double()
+            with torch.inference_mode():
+                got = _native.linear(x.cuda(), w.cuda(), b.cuda()).double().cpu()
+            atol, rtol = TOL[dtype]
+            assert torch.allclose(got, want, atol=atol, rtol=rtol), f'{dtype} {M}x{K}x{N}'
+
+
 def test_value_padding_mask_is_checked(cuda):
     args = to(make(2, 8, 2, 8, 16, [(6, 7), (3, 4)], 2), cuda)
     N = args[0].shape[1]
