@@ -10,6 +10,11 @@ whose total size exceeds twice the 126 MB L2, so each call's memory comes from H
 With --gpus N under torchrun each rank runs its own images (batch sharding, no collective in the data path), the
 timed region is bracketed by barriers and synchronisation, and the slowest rank's time is reported.
 
+--layer times the whole deformable attention layer instead (deform_attn_layer: query -> offsets and softmaxed
+weights -> attention -> output_proj), beside the same layer with the producer in torch operators on the GPU (two
+nn.Linear, softmax, location arithmetic; then this library's ma_deform_attn) and the all-torch layer on the GPU
+(deform_attn_layer_reference: grid_sample), on the same rotating inputs.
+
 --impl reference times the CPU implementation of the same call: upstream's algorithm (nn.Linear + grid_sample, the
 oracle's torch_port on torch's CPU operators) with all host threads, on rank 0 only.
 """
@@ -28,7 +33,8 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-from marearts_tinydeform_b200 import _native, choose_mode, ma_deform_attn, workloads  # noqa: E402
+from marearts_tinydeform_b200 import (_native, choose_mode, deform_attn_layer, ma_deform_attn,  # noqa: E402
+                                      ma_deform_attn_reference, sampling_producer_reference, workloads)
 
 L2_BYTES = 126 * 2 ** 20
 METRIC = 'µs per ma_deform_attn call (device-timed) and achieved HBM GB/s vs peak'
@@ -357,6 +363,88 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_layer(args):
+    """One deformable attention layer per step (see the module docstring); prints one JSON line."""
+    torch.cuda.set_device(0)
+    dev = torch.device('cuda', 0)
+    _native.load()
+    cfg = workloads.CONFIGS[args.config]
+    B, Q, C, H, D, P, dtype = cfg['B'], cfg['Q'], cfg['C'], cfg['H'], cfg['D'], cfg['P'], cfg['dtype']
+    L = len(cfg['levels'])
+    base, pool = input_pool(args.config, B, dev, 2 * L2_BYTES)
+    W, bias, shapes, starts = base[1], base[2], base[3], base[4]
+    g = torch.Generator(device=dev).manual_seed(91)
+    LP = H * L * P
+    sw = torch.cat([torch.randn(2 * LP, C, generator=g, device=dev) * (2.0 / C ** 0.5),
+                    torch.randn(LP, C, generator=g, device=dev) / C ** 0.5]).to(dtype)
+    sb = (torch.randn(3 * LP, generator=g, device=dev) * 0.5).to(dtype)
+    wo = ((torch.rand(C, H * D, generator=g, device=dev) * 2 - 1) * (6 / (C + H * D)) ** 0.5).to(dtype)
+    bo = torch.zeros(C, dtype=dtype, device=dev)
+    sets = []
+    for mem, _, _ in pool:
+        q = torch.randn(B, Q, C, generator=g, device=dev).to(dtype)
+        ref = torch.rand(B, Q, L, args.ref_dim, generator=g, device=dev)
+        if args.ref_dim == 4:
+            ref[..., 2:] = 0.05 + 0.45 * ref[..., 2:]
+        sets.append((q, ref.to(dtype), mem))
+    mode = args.mode if args.mode != 'auto' else choose_mode(base[0], W, base[5])
+    kw = dict(output_weight=wo, output_bias=bo)
+
+    def ours(i):
+        q, ref, mem = sets[i % len(sets)]
+        return deform_attn_layer(q, ref, mem, shapes, starts, H, P, sw, sb, W, bias, mode=args.mode, **kw)
+
+    def torch_producer(i):
+        q, ref, mem = sets[i % len(sets)]
+        proj = torch.nn.functional.linear(q, sw, sb)
+        off = proj[..., :2 * LP].view(B, Q, H, L, P, 2)
+        attn = proj[..., 2 * LP:].view(B, Q, H, L * P).softmax(-1).view(B, Q, H, L, P)
+        if args.ref_dim == 2:
+            norm = torch.stack([shapes[:, 1], shapes[:, 0]], -1).to(dtype)
+            loc = ref[:, :, None, :, None, :] + off / norm[None, None, None, :, None, :]
+        else:
+            loc = ref[:, :, None, :, None, :2] + off / P * ref[:, :, None, :, None, 2:] * 0.5
+        return ma_deform_attn(mem, W, bias, shapes, starts, loc, attn, mode=args.mode, **kw)
+
+    shapes_host, starts_host = shapes.cpu(), starts.cpu()  # grid_sample callers read the level geometry on the host
+
+    def all_torch(i):
+        q, ref, mem = sets[i % len(sets)]
+        loc, attn = sampling_producer_reference(q, ref, shapes, H, P, sw, sb)
+        out = ma_deform_attn_reference(mem, W, bias, shapes_host, starts_host, loc, attn)
+        return torch.nn.functional.linear(out, wo, bo)
+
+    times = {}
+    with torch.inference_mode():
+        for name, fn in (('ours', ours), ('torch_producer', torch_producer), ('all_torch', all_torch)):
+            gr, launches = graph_time_us(fn, args.steps, args.warmup)
+            if name == 'ours':
+                ours_launches = launches
+                torch.cuda.synchronize()
+                with ClockSampler(0) as clocks:
+                    time.sleep(0.25)
+                    times[name] = time_graph(gr, args.steps, reps=max(1, args.reps))
+            else:
+                times[name] = time_graph(gr, args.steps, reps=max(1, args.reps))
+            del gr
+        gq, _ = graph_time_us(lambda i: _native.linear(sets[i % len(sets)][0], sw, sb), args.steps, args.warmup)
+        t_qproj = time_graph(gq, args.steps, reps=max(1, args.reps))
+        del gq
+        # parity of the timed configuration: ours against the all-torch layer on the first input set
+        diff = (ours(0).float() - all_torch(0).float()).abs().max().item()
+    line = {
+        'metric': 'µs per deformable attention layer (device-timed)', 'value': round(times['ours'], 3), 'unit': 'us',
+        'n_gpus': 1, 'steps': args.steps, 'warmup': args.warmup, 'higher_is_better': False,
+        'dtype': str(dtype).replace('torch.', ''), 'data': 'synthetic (seeded, BASELINE config shapes)',
+        'config': dict(config_dict(args.config, 1, mode), query_dim=C, reference_points=args.ref_dim,
+                       output_proj=[C, H * D]),
+        'torch_producer_us': round(times['torch_producer'], 3), 'all_torch_us': round(times['all_torch'], 3),
+        'query_proj_us': round(t_qproj, 3), 'max_abs_diff_vs_all_torch': diff,
+        'gpu_launches': ours_launches, 'clocks': clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_sweep(args):
     """Fused vs project over upstream's sweep grid (bench/results/rtx4090.md) and the c5 grid; prints a table."""
     torch.cuda.set_device(0)
@@ -404,6 +492,9 @@ def main():
     ap.add_argument('--padding-mask', type=float, default=0.0,
                     help='fraction of tokens padded by a random value padding mask (0: no mask)')
     ap.add_argument('--sweep', action='store_true')
+    ap.add_argument('--layer', action='store_true', help='time the whole deformable attention layer')
+    ap.add_argument('--ref-dim', type=int, default=4, choices=(2, 4),
+                    help='--layer: reference points (2) or reference boxes (4)')
     ap.add_argument('--dtype', nargs='+', default=['float16', 'bfloat16', 'float32'])
     args = ap.parse_args()
     if args.warmup < 3:
@@ -412,6 +503,8 @@ def main():
         run_reference_arm(args)
     elif args.sweep:
         run_sweep(args)
+    elif args.layer:
+        run_layer(args)
     else:
         run_ours(args)
 

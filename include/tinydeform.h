@@ -44,7 +44,7 @@ enum td_status {
     TD_OK = 0,
     TD_ERR_ARG = 1,         /* a size, pointer or dtype violates the contract; nothing was launched */
     TD_ERR_CUDA = 2,        /* a CUDA runtime call or kernel launch failed */
-    TD_ERR_WORKSPACE = 3    /* the workspace is NULL or smaller than td_project_workspace_bytes() */
+    TD_ERR_WORKSPACE = 3    /* the workspace is NULL or smaller than the call's *_workspace_bytes() */
 };
 
 /* Limits of the operator contract (upstream csrc/ma_deform_fused.cu:27-28 and :241,:264). */
@@ -93,6 +93,46 @@ TD_API int td_value_proj(int dtype, const void* memory, const void* value_weight
  */
 TD_API int td_linear(int dtype, const void* x, const void* weight, const void* bias, void* y, int64_t M, int64_t K,
                      int64_t Nout, void* stream, char* err, size_t err_len);
+
+/*
+ * The producer of sampling_locations / attention_weights in the multi-scale deformable attention layer (Deformable-
+ * DETR's MSDeformAttn, RT-DETR's decoder), from proj = query @ [W_offsets; W_attention]^T + [b_offsets; b_attention]
+ * (td_linear): proj [B * Q, 3 * H * L * P], each row the 2 * H * L * P offsets (head, level, point, x/y) then the
+ * H * L * P attention logits (head, level * point). Per (b, q, h): attention_weights = softmax over the L * P logits;
+ * sampling_locations = ref[b, q, l] + offset / (w_l, h_l) for reference_points [B, Q, L, 2] (ref_dim 2), or
+ * ref.xy + offset / P * ref.wh * 0.5 for reference boxes [B, Q, L, 4] (ref_dim 4). Writes sampling_locations
+ * [B, Q, H, L, P, 2] and attention_weights [B, Q, H, L, P]. Upstream takes both as inputs and has no producer.
+ */
+TD_API int td_sampling_producer(int dtype, const void* proj, const void* reference_points, int ref_dim,
+                                const int64_t* spatial_shapes, void* sampling_locations, void* attention_weights,
+                                int64_t B, int64_t Q, int64_t H, int64_t L, int64_t P, void* stream, char* err,
+                                size_t err_len);
+
+/*
+ * One multi-scale deformable attention layer of a DETR-style decoder (Deformable-DETR's MSDeformAttn forward, the
+ * caller of upstream's operator), in one call:
+ *   proj = query [B, Q, Cq] @ sampling_weight^T + sampling_bias       sampling_weight = [W_offsets; W_attention],
+ *                                                                     [3 * H * L * P, Cq] (td_sampling_producer)
+ *   locations, weights = the producer of td_sampling_producer on proj and reference_points [B, Q, L, ref_dim]
+ *   attn = ma_deform_attn(memory [B, N, C], value_weight [HD, C], value_bias, ...)  [B, Q, HD], with the optional
+ *          value padding mask [B, N] of td_project_forward_masked
+ *   out  = attn @ output_weight^T + output_bias  [B, Q, C_out] when output_weight is not NULL, else out = attn.
+ * order TD_ORDER_PROJECT: three launches (query projection, value projection, sampler whose corner prologue runs
+ * the producer, so locations and weights never reach memory); TD_ORDER_FUSED: query projection, producer, the
+ * fused gather-then-project kernel. Plus the output projection. Intermediates live in `workspace` of at least
+ * td_layer_workspace_bytes() bytes (same arguments; output_proj = output_weight != NULL). No counterpart in upstream,
+ * which implements only the operator.
+ */
+enum td_order { TD_ORDER_PROJECT = 0, TD_ORDER_FUSED = 1 };
+TD_API size_t td_layer_workspace_bytes(int dtype, int order, int64_t B, int64_t Q, int64_t N, int64_t H, int64_t HD,
+                                       int64_t L, int64_t P, int output_proj);
+TD_API int td_layer_forward(int dtype, int order, const void* query, int64_t Cq, const void* reference_points,
+                            int ref_dim, const void* sampling_weight, const void* sampling_bias, const void* memory,
+                            const void* value_weight, const void* value_bias, const uint8_t* value_padding_mask,
+                            const int64_t* spatial_shapes, const int64_t* level_start_index,
+                            const void* output_weight, const void* output_bias, int64_t C_out, void* out, int64_t B,
+                            int64_t Q, int64_t N, int64_t C, int64_t H, int64_t HD, int64_t L, int64_t P,
+                            void* workspace, size_t workspace_bytes, void* stream, char* err, size_t err_len);
 
 /*
  * Sampling of a projected value at explicit element strides: value element (b, token, head, d) is at

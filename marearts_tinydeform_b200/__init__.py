@@ -10,6 +10,16 @@ arguments, results and errors, computed by hand-written sm_100a kernels behind a
   mode='project'  project every memory token (our own GEMM kernel), then sample per head
   mode='auto'     choose_mode() picks one from the shapes, with crossovers measured on B200
 
+Around the operator (additions; upstream has only the operator):
+
+    deform_attn_layer(query, reference_points, memory, spatial_shapes, level_start_index, n_heads, n_points,
+                      sampling_weight, sampling_bias, value_weight, value_bias, ...)   -> [B, Q, H * D | C_out]
+    sampling_producer(query, reference_points, spatial_shapes, n_heads, n_points, sampling_weight, sampling_bias)
+        -> sampling_locations, attention_weights
+    pack_sampling_weights(offset_weight, offset_bias, attention_weight, attention_bias) -> the packed pair
+
+the whole MSDeformAttn layer (query -> offsets and softmaxed weights -> attention -> output_proj) in one library call.
+
 CPU tensors run ``ma_deform_attn_reference`` (as upstream does). CUDA tensors run only the native library; if it is
 missing, the call raises. Inference only: inputs that require grad are rejected.
 """
@@ -19,9 +29,10 @@ import functools
 import torch
 
 from . import _native
-from .reference import ma_deform_attn_reference
+from .reference import deform_attn_layer_reference, ma_deform_attn_reference, sampling_producer_reference
 
-__all__ = ['ma_deform_attn', 'ma_deform_attn_reference', 'choose_mode']
+__all__ = ['ma_deform_attn', 'ma_deform_attn_reference', 'choose_mode', 'deform_attn_layer', 'sampling_producer',
+           'pack_sampling_weights', 'deform_attn_layer_reference', 'sampling_producer_reference']
 __version__ = '0.1.1+b200'
 
 MODES = ('auto', 'fused', 'project')
@@ -50,8 +61,12 @@ def _limits(device_index):
 
 def choose_mode(memory, value_weight, sampling_locations):
     """The mode 'auto' runs: 'fused' for few queries per image, 'project' (project every token first) for many."""
-    n_img, n_tok, _ = memory.shape
     _, n_qry, n_head, n_lvl, n_pt, _ = sampling_locations.shape
+    return _pick(memory, value_weight, n_qry, n_head, n_lvl, n_pt)
+
+
+def _pick(memory, value_weight, n_qry, n_head, n_lvl, n_pt):
+    n_img, n_tok, _ = memory.shape
     head_dim = value_weight.shape[0] // n_head
     limits = _limits(memory.get_device()) if memory.is_cuda else FUSED_LIMIT
     a, b = limits.get(memory.dtype, limits[torch.float16])
@@ -97,3 +112,71 @@ def ma_deform_attn(memory, value_weight, value_bias, spatial_shapes, level_start
     out = run(memory, value_weight, value_bias, spatial_shapes, level_start_index, sampling_locations,
               attention_weights, value_padding_mask)
     return out if output_weight is None else _native.linear(out, output_weight, output_bias)
+
+
+def _check_inference(*ts):
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in ts):
+        raise RuntimeError('the CUDA kernels are inference only: run them under torch.no_grad() / '
+                           'torch.inference_mode(), or use the *_reference functions for training')
+
+
+def pack_sampling_weights(offset_weight, offset_bias, attention_weight, attention_bias):
+    """The layer's two query projections as one: sampling_offsets ([2 * H * L * P, Cq], rows (head, level, point,
+    x/y)) stacked over attention_weights ([H * L * P, Cq], rows (head, level, point)), as the nn.Linear modules of
+    Deformable-DETR's MSDeformAttn hold them. Pack once per model, not per call."""
+    weight = torch.cat([offset_weight, attention_weight], 0)
+    bias = None
+    if offset_bias is not None or attention_bias is not None:
+        zeros = offset_weight.new_zeros
+        bias = torch.cat([offset_bias if offset_bias is not None else zeros(offset_weight.shape[0]),
+                          attention_bias if attention_bias is not None else zeros(attention_weight.shape[0])])
+    return weight, bias
+
+
+def sampling_producer(query, reference_points, spatial_shapes, n_heads, n_points, sampling_weight, sampling_bias):
+    """sampling_locations [B, Q, H, L, P, 2] and attention_weights [B, Q, H, L, P] from the query [B, Q, Cq] and
+    reference points [B, Q, L, 2] (x, y) or reference boxes [B, Q, L, 4] (cx, cy, w, h), as
+    sampling_producer_reference defines them. CUDA: the projection kernel, then the producer kernel."""
+    if not query.is_cuda:
+        return sampling_producer_reference(query, reference_points, spatial_shapes, n_heads, n_points,
+                                           sampling_weight, sampling_bias)
+    _native.load()
+    _check_inference(query, reference_points, sampling_weight, sampling_bias)
+    L = spatial_shapes.shape[0]
+    if sampling_weight.dim() != 2 or sampling_weight.shape[0] != 3 * n_heads * L * n_points:
+        raise RuntimeError('sampling_weight must be [3 * H * L * P, Cq]: the offset rows, then the attention rows')
+    proj = _native.linear(query, sampling_weight, sampling_bias)
+    return _native.sampling_producer(proj, reference_points, spatial_shapes, n_heads, n_points)
+
+
+def deform_attn_layer(query, reference_points, memory, spatial_shapes, level_start_index, n_heads, n_points,
+                      sampling_weight, sampling_bias, value_weight, value_bias, output_weight=None, output_bias=None,
+                      value_padding_mask=None, mode='auto'):
+    """One multi-scale deformable attention layer (the forward of Deformable-DETR's MSDeformAttn, whose core is
+    ma_deform_attn): [B, Q, H * D], or [B, Q, C_out] with output_weight.
+
+    query [B, Q, Cq]; reference_points [B, Q, L, 2] or [B, Q, L, 4]; memory [B, N, C] (the value input);
+    sampling_weight / sampling_bias: pack_sampling_weights of the offset and attention-weight projections;
+    value_weight / value_bias: value_proj; output_weight / output_bias: output_proj (optional);
+    value_padding_mask: bool [B, N], True = padded token. Same result as deform_attn_layer_reference.
+
+    CUDA, mode 'project' (or 'auto' choosing it): three kernels in one library call (query projection, value
+    projection, and the sampler computing the softmax and locations in its prologue), plus the output projection.
+    Mode 'fused': query projection, producer kernel, fused gather-then-project kernel.
+    """
+    if mode not in MODES:
+        raise ValueError(f'mode must be one of {MODES}, got {mode!r}')
+    if output_bias is not None and output_weight is None:
+        raise ValueError('output_bias needs output_weight')
+    if not memory.is_cuda:
+        return deform_attn_layer_reference(query, reference_points, memory, spatial_shapes, level_start_index,
+                                           n_heads, n_points, sampling_weight, sampling_bias, value_weight,
+                                           value_bias, output_weight, output_bias, value_padding_mask)
+    _native.load()
+    _check_inference(query, reference_points, memory, sampling_weight, sampling_bias, value_weight, value_bias,
+                     output_weight, output_bias)
+    if mode == 'auto':
+        mode = _pick(memory, value_weight, query.shape[1], n_heads, spatial_shapes.shape[0], n_points)
+    return _native.layer_forward(query, reference_points, memory, spatial_shapes, level_start_index, n_heads,
+                                 n_points, sampling_weight, sampling_bias, value_weight, value_bias, output_weight,
+                                 output_bias, value_padding_mask, order=mode)

@@ -35,6 +35,11 @@ SIGNATURES = {
     'td_project_forward': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                  _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp, _cp, _sz]),
     'td_linear': (_ip, [_ip, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _cp, _sz]),
+    'td_sampling_producer': (_ip, [_ip, _vp, _vp, ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp,
+                                   _cp, _sz]),
+    'td_layer_workspace_bytes': (_sz, [_ip, _ip, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _ip]),
+    'td_layer_forward': (_ip, [_ip, _ip, _vp, _i64, _vp, _ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64,
+                               _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp, _cp, _sz]),
     'td_fused_forward_masked': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                       _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _cp, _sz]),
     'td_project_forward_masked': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
@@ -251,6 +256,115 @@ def linear(x, weight, bias):
         _call(lib.td_linear, DTYPE_CODE[x.dtype], _ptr(xs), _ptr(w), _ptr(b), _ptr(y), M, K, Nout,
               _stream(x.device))
     return y
+
+
+def sampling_producer(proj, reference_points, spatial_shapes, heads, points):
+    """sampling_locations [B, Q, H, L, P, 2] and attention_weights [B, Q, H, L, P] from the query projection
+    proj [B, Q, 3 * H * L * P] (offsets, then logits) and reference points [B, Q, L, 2 | 4], through
+    td_sampling_producer."""
+    lib = load()
+    if not proj.is_cuda or not reference_points.is_cuda or not spatial_shapes.is_cuda:
+        raise RuntimeError('inputs must be CUDA tensors')
+    if proj.dtype not in DTYPE_CODE or reference_points.dtype != proj.dtype:
+        raise RuntimeError('proj and reference_points must share a supported float dtype')
+    if spatial_shapes.dtype != torch.long or spatial_shapes.dim() != 2 or spatial_shapes.size(1) != 2:
+        raise RuntimeError('spatial_shapes must be int64 [L, 2]')
+    L = spatial_shapes.size(0)
+    if reference_points.dim() != 4 or reference_points.size(2) != L or reference_points.size(3) not in (2, 4):
+        raise RuntimeError('reference_points must be [B, Q, L, 2] or [B, Q, L, 4]')
+    B, Q = reference_points.shape[:2]
+    H, P = heads, points
+    if proj.shape != (B, Q, 3 * H * L * P):
+        raise RuntimeError('the query projection must be [B, Q, 3 * H * L * P]')
+    if L * P > MAX_LEVEL_POINTS:
+        raise RuntimeError(f'levels x points must be <= {MAX_LEVEL_POINTS}')
+    pr, ref, shp = _dense(proj, reference_points, spatial_shapes)
+    loc = torch.empty((B, Q, H, L, P, 2), dtype=proj.dtype, device=proj.device)
+    attn = torch.empty((B, Q, H, L, P), dtype=proj.dtype, device=proj.device)
+    if B * Q == 0:
+        return loc, attn
+    with torch.cuda.device(proj.device):
+        _call(lib.td_sampling_producer, DTYPE_CODE[proj.dtype], _ptr(pr), _ptr(ref), ref.size(3), _ptr(shp),
+              _ptr(loc), _ptr(attn), B, Q, H, L, P, _stream(proj.device))
+    return loc, attn
+
+
+ORDER_CODE = {'project': 0, 'fused': 1}
+
+
+def layer_forward(query, reference_points, memory, spatial_shapes, level_start_index, heads, points,
+                  sampling_weight, sampling_bias, value_weight, value_bias, output_weight=None, output_bias=None,
+                  value_padding_mask=None, order='project'):
+    """One deformable attention layer through td_layer_forward: query projection -> producer -> attention
+    (-> output projection). Returns [B, Q, H * D], or [B, Q, C_out] with output_weight."""
+    lib = load()
+    if order not in ORDER_CODE:
+        raise RuntimeError(f'order must be one of {tuple(ORDER_CODE)}')
+    for t in (query, reference_points, memory, spatial_shapes, level_start_index):
+        if not t.is_cuda:
+            raise RuntimeError('inputs must be CUDA tensors')
+    if memory.dim() != 3 or query.dim() != 3:
+        raise RuntimeError('memory must be [B, N, C] and query [B, Q, Cq]')
+    dt, dev = memory.dtype, memory.device
+    if dt not in DTYPE_CODE:
+        raise RuntimeError(f'unsupported dtype {dt}')
+    B, N, C = memory.shape
+    Q, Cq = query.size(1), query.size(2)
+    if query.size(0) != B:
+        raise RuntimeError('batch size mismatch')
+    if spatial_shapes.dtype != torch.long or spatial_shapes.dim() != 2 or spatial_shapes.size(1) != 2:
+        raise RuntimeError('spatial_shapes must be int64 [L, 2]')
+    L = spatial_shapes.size(0)
+    if level_start_index.dtype != torch.long or level_start_index.shape != (L,):
+        raise RuntimeError('level_start_index must be int64 [L]')
+    if reference_points.dim() != 4 or reference_points.shape[:3] != (B, Q, L) or reference_points.size(3) not in (2, 4):
+        raise RuntimeError('reference_points must be [B, Q, L, 2] or [B, Q, L, 4]')
+    H, P = heads, points
+    if H <= 0 or P <= 0 or L <= 0:
+        raise RuntimeError('heads, points and levels must be positive')
+    if L * P > MAX_LEVEL_POINTS:
+        raise RuntimeError(f'levels x points must be <= {MAX_LEVEL_POINTS}')
+    if B * Q * H > INT32_MAX:
+        raise RuntimeError('too many (batch, query, head) rows')
+    if sampling_weight.shape != (3 * H * L * P, Cq):
+        raise RuntimeError('sampling_weight must be [3 * H * L * P, Cq]: the offset rows, then the attention rows')
+    if sampling_bias is not None and sampling_bias.shape != (3 * H * L * P,):
+        raise RuntimeError('sampling_bias must be [3 * H * L * P]')
+    HD = check_projection(memory, value_weight, value_bias, H)
+    C_out = 0
+    if output_weight is not None:
+        if output_weight.dim() != 2 or output_weight.size(1) != HD:
+            raise RuntimeError('output_weight must be [C_out, H * D]')
+        C_out = output_weight.size(0)
+        if output_bias is not None and output_bias.shape != (C_out,):
+            raise RuntimeError('output_bias must be [C_out] like output_weight')
+    elif output_bias is not None:
+        raise RuntimeError('output_bias needs output_weight')
+    if order == 'fused' and C > MAX_CHANNELS:
+        raise RuntimeError(f'channels must be <= {MAX_CHANNELS}')
+    floats = (query, reference_points, sampling_weight, sampling_bias, value_weight, value_bias, output_weight,
+              output_bias)
+    for t in floats:
+        if t is not None and (t.device != dev or t.dtype != dt):
+            raise RuntimeError('all float tensors must have the dtype and device of memory')
+    for t in (spatial_shapes, level_start_index):
+        if t.device != dev:
+            raise RuntimeError('all tensors must be on the same device')
+    mask = check_mask(value_padding_mask, memory)
+    q, ref, sw, sb, mem, vw, vb, ow, ob, shp, st = _dense(query, reference_points, sampling_weight, sampling_bias,
+                                                          memory, value_weight, value_bias, output_weight,
+                                                          output_bias, spatial_shapes, level_start_index)
+    out = torch.empty((B, Q, C_out if output_weight is not None else HD), dtype=dt, device=dev)
+    if B * Q == 0:
+        return out
+    code, oc = DTYPE_CODE[dt], ORDER_CODE[order]
+    ws_bytes = lib.td_layer_workspace_bytes(code, oc, B, Q, N, H, HD, L, P, int(output_weight is not None))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _call(lib.td_layer_forward, code, oc, _ptr(q), Cq, _ptr(ref), ref.size(3), _ptr(sw), _ptr(sb), _ptr(mem),
+              _ptr(vw), _ptr(vb), _ptr(mask), _ptr(shp), _ptr(st), _ptr(ow), _ptr(ob), C_out, _ptr(out),
+              B, Q, N, C, H, HD, L, P, _ptr(ws), ws_bytes, _stream(dev))
+    return out
 
 
 def sample_forward(value, heads, spatial_shapes, level_start_index, sampling_locations, attention_weights):

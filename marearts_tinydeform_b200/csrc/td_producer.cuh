@@ -1,0 +1,125 @@
+// td_producer.cuh -- the producer of sampling_locations / attention_weights from the decoder's query projection.
+//
+// The standard multi-scale deformable attention layer (Deformable-DETR's MSDeformAttn, RT-DETR's decoder) computes,
+// per query, proj = query @ [W_off; W_att]^T + [b_off; b_att] (one projection-kernel launch) and then, per
+// (batch, query, head) row:
+//   attention_weights[l, p] = softmax over the L * P logits of the row
+//   sampling_locations[l, p] = ref[l] + offset[l, p] / (w_l, h_l)                 (2-d reference points)
+//                            = ref[l].xy + offset[l, p] / P * ref[l].wh * 0.5       (4-d reference boxes)
+// proj row layout: the 2 * H * L * P offsets (head, level, point, xy), then the H * L * P logits (head, level * point).
+// One warp per row, lanes over the row's L * P <= 64 points (two per lane); the softmax max and sum are warp
+// shuffles. produce_row is shared by the standalone producer kernel (which writes both tensors) and the sampler,
+// which runs it in its corner prologue and never writes them out.
+#pragma once
+
+#include "td_common.cuh"
+#include "td_ptx.cuh"
+
+namespace td {
+
+// The producer's inputs as the sampler carries them (proj == nullptr: the sampler reads sampling_locations and
+// attention_weights instead).
+template <typename T>
+struct ProducerIn {
+    const T* proj = nullptr;  // [B * Q, 3 * H * L * P]
+    const T* ref = nullptr;   // [B, Q, L, ref_dim]
+    int ref_dim = 2;
+};
+
+// Locations (lx, ly) and softmax weight w of the points j = lane + 32 k (k = 0, 1) of row `row` = (b * Q + q) * H + h;
+// a lane with j >= L * P gets w = 0. Every lane of the warp must call it (the softmax is a warp reduction).
+// All global loads of the row are issued before the first shuffle.
+template <typename T, typename A>
+__device__ __forceinline__ void produce_row(const ProducerIn<T>& in, const int64_t* __restrict__ shapes,
+                                            long long row, int H, int L, int P, int lane, A (&lx)[2], A (&ly)[2],
+                                            A (&w)[2]) {
+    const int LP = L * P;
+    const long long bq = row / H;
+    const int h = int(row - bq * H);
+    const T* __restrict__ base = in.proj + bq * 3LL * H * LP;
+    const T* __restrict__ off = base + (long long)h * LP * 2;
+    const T* __restrict__ logit = base + 2LL * H * LP + (long long)h * LP;
+    A x[2], ox[2], oy[2], rx[2], ry[2], sx[2], sy[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int j = lane + 32 * k;
+        const bool on = j < LP;
+        const int l = on ? j / P : 0;
+        x[k] = on ? to_acc(logit[j]) : A(-INFINITY);
+        ox[k] = on ? to_acc(off[2 * j]) : A(0);
+        oy[k] = on ? to_acc(off[2 * j + 1]) : A(0);
+        const T* __restrict__ r = in.ref + (bq * L + l) * in.ref_dim;
+        rx[k] = on ? to_acc(r[0]) : A(0);
+        ry[k] = on ? to_acc(r[1]) : A(0);
+        if (in.ref_dim == 2) {  // offset normaliser (w_l, h_l)
+            sx[k] = on ? A(shapes[2 * l + 1]) : A(1);
+            sy[k] = on ? A(shapes[2 * l]) : A(1);
+        } else {                // box width and height
+            sx[k] = on ? to_acc(r[2]) : A(0);
+            sy[k] = on ? to_acc(r[3]) : A(0);
+        }
+    }
+    A m = x[0] > x[1] ? x[0] : x[1];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const A y = __shfl_xor_sync(0xffffffffu, m, o);
+        m = y > m ? y : m;
+    }
+    A e[2], sum = A(0);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        e[k] = lane + 32 * k < LP ? exp(x[k] - m) : A(0);
+        sum += e[k];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        w[k] = e[k] / sum;
+        if (in.ref_dim == 2) {
+            lx[k] = rx[k] + ox[k] / sx[k];
+            ly[k] = ry[k] + oy[k] / sy[k];
+        } else {
+            lx[k] = rx[k] + ox[k] / A(P) * sx[k] * A(0.5);
+            ly[k] = ry[k] + oy[k] / A(P) * sy[k] * A(0.5);
+        }
+    }
+}
+
+template <typename T>
+struct ProducerArgs {
+    ProducerIn<T> in;
+    const int64_t* shapes;    // [L, 2] (height, width)
+    T* loc;                   // [B, Q, H, L, P, 2]
+    T* attn;                  // [B, Q, H, L, P]
+    long long rows;           // B * Q * H
+    int H, L, P;
+};
+
+constexpr int kProducerWarps = 8;
+
+// The standalone producer: writes sampling_locations and attention_weights. Launched with programmatic dependent
+// launch behind the projection kernel (its reads of proj come after the grid dependency wait).
+template <typename T>
+__global__ void __launch_bounds__(kProducerWarps * 32) sampling_producer_kernel(const ProducerArgs<T> a) {
+    using A = typename Elem<T>::acc;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long row = (long long)blockIdx.x * kProducerWarps + warp;
+    grid_dependency_wait();  // proj is the output of the kernel before this one
+    launch_dependents();
+    if (row >= a.rows) return;  // warp-uniform
+    A lx[2], ly[2], w[2];
+    produce_row<T, A>(a.in, a.shapes, row, a.H, a.L, a.P, lane, lx, ly, w);
+    const int LP = a.L * a.P;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int j = lane + 32 * k;
+        if (j >= LP) continue;
+        const long long i = row * LP + j;
+        a.loc[2 * i] = from_acc<T>(lx[k]);
+        a.loc[2 * i + 1] = from_acc<T>(ly[k]);
+        a.attn[i] = from_acc<T>(w[k]);
+    }
+}
+
+}  // namespace td

@@ -12,6 +12,7 @@
 #pragma once
 
 #include "td_common.cuh"
+#include "td_producer.cuh"
 #include "td_ptx.cuh"
 
 namespace td {
@@ -28,6 +29,7 @@ struct SampleArgs {
     long long s_img, s_tok, s_head; // value strides in elements
     long long n_tok;                // N
     const uint8_t* mask;            // value padding mask [B, N] (nonzero = padded) or null
+    ProducerIn<T> prod;             // prod.proj set: locations and weights come from the query projection
     int Q, H, D, L, P;
     int G;                          // lanes per corner row = D * sizeof(T) / 16 (vector kernel only)
 };
@@ -50,6 +52,19 @@ __device__ __forceinline__ void sample_row_corners(const SampleArgs<T>& a, long 
     using CT = typename Coord<T>::type;
     const int LP = a.L * a.P;
     const uint8_t* mask_b = a.mask != nullptr ? a.mask + row / ((long long)a.Q * a.H) * a.n_tok : nullptr;
+    if (a.prod.proj != nullptr) {  // the producer's softmax and locations, straight from the query projection
+        using A = typename Elem<T>::acc;
+        A lx[2], ly[2], w[2];
+        produce_row<T, A>(a.prod, a.shapes, row, a.H, a.L, a.P, lane, lx, ly, w);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int j = lane + 32 * k;
+            if (j < LP)
+                corners4<CT>(CT(lx[k]), CT(ly[k]), CT(w[k]), level_at(a.shapes, a.starts, j / a.P), a.n_tok,
+                             &s_tok[4 * j], &s_wt[4 * j], mask_b);
+        }
+        return;
+    }
     for (int j = lane; j < LP; j += 32) {
         const Level lv = level_at(a.shapes, a.starts, j / a.P);
         const long long i = row * LP + j;
@@ -111,6 +126,10 @@ __device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long l
     if (cg == 0) store16<T>(a.out + row * a.D + v * V, acc);
 }
 
+// With prod.proj set, the corners come from the query projection (produce_row): that projection is then written
+// two launches earlier (query projection -> value projection -> this kernel), and the value projection, launched
+// with programmatic serialization, lets this kernel start only after its own grid dependency wait has seen the
+// query projection complete, so the corner prologue may read it before this kernel's own wait.
 // Vector kernel: needs D * sizeof(T) % 16 == 0, D * sizeof(T) <= 512, 16-byte aligned value/out and strides.
 // The dependent-latency chain is kept to two memory round trips: (level geometry + locations + attention weights,
 // all issued together) -> corners -> (every corner row of the lane's group issued together) -> butterfly -> store.
@@ -155,9 +174,22 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_generic_kernel(const
     const long long row = (long long)blockIdx.x * kSampleWarps + warp;
     if (row >= a.rows) return;
     const int LP = a.L * a.P, S = 4 * LP;
-    for (int j = lane; j < LP; j += 32)
-        row_corners(a.loc, a.attn, lv, LP, a.P, a.n_tok, row, j, &s_tok[warp][4 * j], &s_wt[warp][4 * j],
-                    a.mask != nullptr ? a.mask + row / ((long long)a.Q * a.H) * a.n_tok : nullptr);
+    const uint8_t* mask_b = a.mask != nullptr ? a.mask + row / ((long long)a.Q * a.H) * a.n_tok : nullptr;
+    if (a.prod.proj != nullptr) {
+        A lx[2], ly[2], w[2];
+        produce_row<T, A>(a.prod, a.shapes, row, a.H, a.L, a.P, lane, lx, ly, w);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int j = lane + 32 * k;
+            if (j < LP)
+                corners4<CT>(CT(lx[k]), CT(ly[k]), CT(w[k]), lv[j / a.P], a.n_tok, &s_tok[warp][4 * j],
+                             &s_wt[warp][4 * j], mask_b);
+        }
+    } else {
+        for (int j = lane; j < LP; j += 32)
+            row_corners(a.loc, a.attn, lv, LP, a.P, a.n_tok, row, j, &s_tok[warp][4 * j], &s_wt[warp][4 * j],
+                        mask_b);
+    }
     __syncwarp();
 
     const int h = int(row % a.H);

@@ -19,6 +19,7 @@
 #include "td_fused_tc.cuh"
 #include "td_gemm_simt.cuh"
 #include "td_gemm_tc.cuh"
+#include "td_producer.cuh"
 #include "td_sampler.cuh"
 
 namespace td {
@@ -119,9 +120,9 @@ template <typename T>
 int launch_sampler(const T* value, long long s_img, long long s_tok, long long s_head, const int64_t* shapes,
                    const int64_t* starts, const T* loc, const T* attn, T* out, int64_t B, int64_t Q, int64_t N,
                    int64_t H, int64_t D, int64_t L, int64_t P, cudaStream_t stream, char* err, size_t err_len,
-                   bool after_producer = false, const uint8_t* mask = nullptr) {
+                   bool after_producer = false, const uint8_t* mask = nullptr, ProducerIn<T> prod = {}) {
     SampleArgs<T> a;
-    a.value = value; a.loc = loc; a.attn = attn; a.out = out; a.shapes = shapes; a.starts = starts;
+    a.value = value; a.loc = loc; a.attn = attn; a.out = out; a.shapes = shapes; a.starts = starts; a.prod = prod;
     a.rows = B * Q * H; a.s_img = s_img; a.s_tok = s_tok; a.s_head = s_head; a.n_tok = N; a.mask = mask;
     a.Q = int(Q); a.H = int(H); a.D = int(D); a.L = int(L); a.P = int(P);
     const long long row_bytes = D * (long long)sizeof(T);
@@ -501,6 +502,52 @@ int dispatch(int dtype, F&& f) {
     }
 }
 
+// The standalone sampling producer (td_producer.cuh), with programmatic dependent launch behind the query
+// projection.
+template <typename T>
+int launch_producer(const T* proj, const T* ref, int ref_dim, const int64_t* shapes, T* loc, T* attn, int64_t B,
+                    int64_t Q, int64_t H, int64_t L, int64_t P, cudaStream_t stream, char* err, size_t err_len) {
+    ProducerArgs<T> a;
+    a.in.proj = proj; a.in.ref = ref; a.in.ref_dim = ref_dim; a.shapes = shapes; a.loc = loc; a.attn = attn;
+    a.rows = B * Q * H; a.H = int(H); a.L = int(L); a.P = int(P);
+    const unsigned grid = unsigned((a.rows + kProducerWarps - 1) / kProducerWarps);
+    const cudaError_t e = launch_kernel(sampling_producer_kernel<T>, dim3(grid), dim3(kProducerWarps * 32), 0, stream,
+                                        true, a);
+    if (e != cudaSuccess)
+        return fail(err, err_len, TD_ERR_CUDA, "sampling_producer_kernel launch: %s", cudaGetErrorString(e));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return check_launch(err, err_len, "sampling_producer_kernel");
+}
+
+// Byte offsets of the decoder layer's intermediates in its workspace (each region 256-byte aligned, from the first
+// 256-byte boundary of the workspace): the query projection, the projected value (project order), locations and
+// weights (fused order), and the attention result when an output projection follows.
+struct LayerWorkspace {
+    size_t proj = 0, value = 0, loc = 0, attn = 0, mid = 0, bytes = 0;
+};
+
+LayerWorkspace layer_workspace(size_t e, int order, int64_t B, int64_t Q, int64_t N, int64_t H, int64_t HD,
+                               int64_t L, int64_t P, bool output_proj) {
+    LayerWorkspace w;
+    size_t at = 0;
+    auto take = [&](size_t n) {
+        const size_t off = at;
+        at += (n * e + 255) & ~size_t(255);
+        return off;
+    };
+    const size_t rows = size_t(B) * size_t(Q);
+    w.proj = take(rows * size_t(3 * H * L * P));
+    if (order == TD_ORDER_PROJECT) {
+        w.value = take(size_t(B) * size_t(N) * size_t(HD));
+    } else {
+        w.loc = take(rows * size_t(H * L * P * 2));
+        w.attn = take(rows * size_t(H * L * P));
+    }
+    if (output_proj) w.mid = take(rows * size_t(HD));
+    w.bytes = at + 256;
+    return w;
+}
+
 }  // namespace
 }  // namespace td
 
@@ -601,6 +648,29 @@ int td_linear(int dtype, const void* x, const void* weight, const void* bias, vo
     });
 }
 
+int td_sampling_producer(int dtype, const void* proj, const void* reference_points, int ref_dim,
+                         const int64_t* spatial_shapes, void* sampling_locations, void* attention_weights, int64_t B,
+                         int64_t Q, int64_t H, int64_t L, int64_t P, void* stream, char* err, size_t err_len) {
+    if (dtype_size(dtype) == 0) return fail(err, err_len, TD_ERR_ARG, "unsupported dtype code %d", dtype);
+    if (B < 0 || Q < 0 || H <= 0 || L <= 0 || P <= 0)
+        return fail(err, err_len, TD_ERR_ARG, "producer needs B, Q >= 0 and H, L, P > 0");
+    if (L * P > TD_MAX_LEVEL_POINTS)
+        return fail(err, err_len, TD_ERR_ARG, "levels x points must be <= %d", TD_MAX_LEVEL_POINTS);
+    if (ref_dim != 2 && ref_dim != 4)
+        return fail(err, err_len, TD_ERR_ARG, "reference points must have 2 (x, y) or 4 (cx, cy, w, h) coordinates");
+    if (B * Q * H > INT32_MAX) return fail(err, err_len, TD_ERR_ARG, "too many (batch, query, head) rows");
+    if (B * Q == 0) return TD_OK;
+    if (!proj || !reference_points || !spatial_shapes || !sampling_locations || !attention_weights)
+        return fail(err, err_len, TD_ERR_ARG, "null tensor pointer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return dispatch(dtype, [&](auto tag) {
+        using T = decltype(tag);
+        return launch_producer<T>(static_cast<const T*>(proj), static_cast<const T*>(reference_points), ref_dim,
+                                  spatial_shapes, static_cast<T*>(sampling_locations),
+                                  static_cast<T*>(attention_weights), B, Q, H, L, P, s, err, err_len);
+    });
+}
+
 int td_sample_strided(int dtype, const void* value, int64_t s_img, int64_t s_tok, int64_t s_head,
                       const int64_t* spatial_shapes, const int64_t* level_start_index,
                       const void* sampling_locations, const void* attention_weights, void* out,
@@ -672,6 +742,99 @@ int td_project_forward_masked(int dtype, const void* memory, const void* value_w
                                  static_cast<const T*>(sampling_locations), static_cast<const T*>(attention_weights),
                                  static_cast<T*>(out), B, Q, N, H, D, L, P, s, err, err_len, true,
                                  value_padding_mask);
+    });
+}
+
+size_t td_layer_workspace_bytes(int dtype, int order, int64_t B, int64_t Q, int64_t N, int64_t H, int64_t HD,
+                                int64_t L, int64_t P, int output_proj) {
+    const size_t e = dtype_size(dtype);
+    if (e == 0 || (order != TD_ORDER_PROJECT && order != TD_ORDER_FUSED) || B < 0 || Q < 0 || N < 0 || H < 0 ||
+        HD < 0 || L < 0 || P < 0)
+        return 0;
+    return layer_workspace(e, order, B, Q, N, H, HD, L, P, output_proj != 0).bytes;
+}
+
+int td_layer_forward(int dtype, int order, const void* query, int64_t Cq, const void* reference_points, int ref_dim,
+                     const void* sampling_weight, const void* sampling_bias, const void* memory,
+                     const void* value_weight, const void* value_bias, const uint8_t* value_padding_mask,
+                     const int64_t* spatial_shapes, const int64_t* level_start_index, const void* output_weight,
+                     const void* output_bias, int64_t C_out, void* out, int64_t B, int64_t Q, int64_t N, int64_t C,
+                     int64_t H, int64_t HD, int64_t L, int64_t P, void* workspace, size_t workspace_bytes,
+                     void* stream, char* err, size_t err_len) {
+    if (dtype_size(dtype) == 0) return fail(err, err_len, TD_ERR_ARG, "unsupported dtype code %d", dtype);
+    if (order != TD_ORDER_PROJECT && order != TD_ORDER_FUSED)
+        return fail(err, err_len, TD_ERR_ARG, "order must be TD_ORDER_PROJECT or TD_ORDER_FUSED, got %d", order);
+    if (int rc = check_geometry(B, Q, N, H, L, P, err, err_len)) return rc;
+    if (L <= 0 || P <= 0) return fail(err, err_len, TD_ERR_ARG, "the layer needs at least one level and one point");
+    if (C <= 0 || Cq <= 0 || HD <= 0)
+        return fail(err, err_len, TD_ERR_ARG, "channels and value_weight rows must be positive");
+    if (HD % H != 0) return fail(err, err_len, TD_ERR_ARG, "value_weight rows must be a multiple of the head count");
+    if (ref_dim != 2 && ref_dim != 4)
+        return fail(err, err_len, TD_ERR_ARG, "reference points must have 2 (x, y) or 4 (cx, cy, w, h) coordinates");
+    if (output_weight != nullptr && C_out <= 0)
+        return fail(err, err_len, TD_ERR_ARG, "the output projection needs C_out > 0");
+    if (output_weight == nullptr && output_bias != nullptr)
+        return fail(err, err_len, TD_ERR_ARG, "output_bias needs output_weight");
+    if (order == TD_ORDER_FUSED && C > TD_MAX_CHANNELS)
+        return fail(err, err_len, TD_ERR_ARG, "channels must be <= %d", TD_MAX_CHANNELS);
+    if (Cq > INT32_MAX || C > INT32_MAX || HD > INT32_MAX || C_out > INT32_MAX || B * Q > INT32_MAX)
+        return fail(err, err_len, TD_ERR_ARG, "size too large");
+    if (B * Q == 0) return TD_OK;
+    if (!query || !reference_points || !sampling_weight || !memory || !value_weight || !spatial_shapes ||
+        !level_start_index || !out)
+        return fail(err, err_len, TD_ERR_ARG, "null tensor pointer");
+    const size_t e = dtype_size(dtype);
+    const LayerWorkspace w = layer_workspace(e, order, B, Q, N, H, HD, L, P, output_weight != nullptr);
+    if (workspace == nullptr || workspace_bytes < w.bytes)
+        return fail(err, err_len, TD_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", w.bytes,
+                    workspace_bytes);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    unsigned char* ws = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+    const int64_t D = HD / H, LP3 = 3 * H * L * P;
+    return dispatch(dtype, [&](auto tag) {
+        using T = decltype(tag);
+        T* proj = reinterpret_cast<T*>(ws + w.proj);
+        T* target = output_weight != nullptr ? reinterpret_cast<T*>(ws + w.mid) : static_cast<T*>(out);
+        const T* ref = static_cast<const T*>(reference_points);
+        // 1. the query projection: offsets and attention logits of every (batch, query) row
+        if (int rc = launch_proj<T>(static_cast<const T*>(query), static_cast<const T*>(sampling_weight),
+                                    static_cast<const T*>(sampling_bias), proj, 1, B * Q, Cq, 1, LP3, 0, s, err,
+                                    err_len, true))
+            return rc;
+        if (order == TD_ORDER_PROJECT) {
+            // 2. the value projection (head-major), 3. the sampler, whose corner prologue runs the producer on the
+            // query projection (written two launches earlier, see sample_vec_kernel)
+            T* value = reinterpret_cast<T*>(ws + w.value);
+            if (N > 0) {
+                if (int rc = launch_proj<T>(static_cast<const T*>(memory), static_cast<const T*>(value_weight),
+                                            static_cast<const T*>(value_bias), value, B, N, C, H, HD, 1, s, err,
+                                            err_len, true))
+                    return rc;
+            }
+            ProducerIn<T> prod;
+            prod.proj = proj; prod.ref = ref; prod.ref_dim = ref_dim;
+            // with no value projection in between, the sampler follows the query projection in plain stream order
+            if (int rc = launch_sampler<T>(value, H * N * D, D, N * D, spatial_shapes, level_start_index, nullptr,
+                                           nullptr, target, B, Q, N, H, D, L, P, s, err, err_len, N > 0,
+                                           value_padding_mask, prod))
+                return rc;
+        } else {
+            // 2. locations and weights, 3. the fused gather-then-project kernel
+            T* loc = reinterpret_cast<T*>(ws + w.loc);
+            T* attn = reinterpret_cast<T*>(ws + w.attn);
+            if (int rc = launch_producer<T>(proj, ref, ref_dim, spatial_shapes, loc, attn, B, Q, H, L, P, s, err,
+                                            err_len))
+                return rc;
+            if (int rc = launch_fused<T>(static_cast<const T*>(memory), static_cast<const T*>(value_weight),
+                                         static_cast<const T*>(value_bias), spatial_shapes, level_start_index, loc,
+                                         attn, target, B, Q, N, C, H, D, L, P, s, err, err_len, value_padding_mask))
+                return rc;
+        }
+        if (output_weight == nullptr) return int(TD_OK);
+        // 4. the output projection of the attention result
+        return launch_proj<T>(target, static_cast<const T*>(output_weight), static_cast<const T*>(output_bias),
+                              static_cast<T*>(out), 1, B * Q, HD, 1, C_out, 0, s, err, err_len, true);
     });
 }
 

@@ -52,3 +52,40 @@ def ma_deform_attn_reference(memory, value_weight, value_bias, spatial_shapes, l
     weights = attention_weights.permute(0, 2, 1, 3, 4).reshape(n_img * n_head, 1, n_qry, n_lvl * n_pt)
     out = (stacked * weights).sum(-1)                                  # [B*H, D, Q]
     return out.view(n_img, n_head * head_dim, n_qry).transpose(1, 2).contiguous()
+
+
+def sampling_producer_reference(query, reference_points, spatial_shapes, n_heads, n_points, sampling_weight,
+                                sampling_bias):
+    """sampling_locations [B, Q, H, L, P, 2] and attention_weights [B, Q, H, L, P] of the multi-scale deformable
+    attention layer (Deformable-DETR's MSDeformAttn, RT-DETR's decoder). sampling_weight = [W_offsets; W_attention]
+    ([3 * H * L * P, Cq]; the offset rows ordered (head, level, point, x/y), the attention rows (head, level, point)),
+    sampling_bias likewise. The logits are normalised by a softmax over the L * P points of each head, and the
+    offsets move the reference points: ref + offset / (w_l, h_l) for reference_points [B, Q, L, 2],
+    ref.xy + offset / P * ref.wh * 0.5 for reference boxes [B, Q, L, 4]. The upstream operator takes both results as
+    inputs and has no producer."""
+    B, Q, _ = query.shape
+    L = spatial_shapes.shape[0]
+    H, P = n_heads, n_points
+    proj = F.linear(query, sampling_weight, sampling_bias)
+    offsets = proj[..., :2 * H * L * P].reshape(B, Q, H, L, P, 2)
+    logits = proj[..., 2 * H * L * P:].reshape(B, Q, H, L * P)
+    attention = logits.softmax(-1).view(B, Q, H, L, P)
+    if reference_points.shape[-1] == 2:
+        norm = torch.stack([spatial_shapes[:, 1], spatial_shapes[:, 0]], -1).to(query.dtype)   # (w, h) per level
+        loc = reference_points[:, :, None, :, None, :] + offsets / norm[None, None, None, :, None, :]
+    else:
+        loc = (reference_points[:, :, None, :, None, :2]
+               + offsets / P * reference_points[:, :, None, :, None, 2:] * 0.5)
+    return loc, attention
+
+
+def deform_attn_layer_reference(query, reference_points, memory, spatial_shapes, level_start_index, n_heads,
+                                n_points, sampling_weight, sampling_bias, value_weight, value_bias,
+                                output_weight=None, output_bias=None, value_padding_mask=None):
+    """One deformable attention layer with torch operators: the producer above, ma_deform_attn_reference, and the
+    optional output projection."""
+    loc, attention = sampling_producer_reference(query, reference_points, spatial_shapes, n_heads, n_points,
+                                                 sampling_weight, sampling_bias)
+    out = ma_deform_attn_reference(memory, value_weight, value_bias, spatial_shapes, level_start_index, loc,
+                                   attention, value_padding_mask)
+    return out if output_weight is None else F.linear(out, output_weight, output_bias)

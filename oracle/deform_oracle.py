@@ -22,6 +22,12 @@ fundamentalvision/Deformable-DETR, not vendored here); a padded token then contr
 With bias=None this equals zeroing the padded memory rows before upstream's own reference, which is how the golden
 vectors pin it.
 
+Sampling producer (``sampling_producer_oracle``; an addition: upstream takes sampling_locations and
+attention_weights as inputs, already normalised, reference.py:22-23, and has no producer): the published
+MSDeformAttn forward of Deformable-DETR (offsets and logits as linear maps of the query, softmax over L * P,
+ref + off / (w, h) or ref.xy + off / P * ref.wh * 0.5). Parity of this part is unpinned against upstream, which has
+no implementation of it; it is checked against the same steps written with torch's operators.
+
 Sampling rule: grid_sample with align_corners=False maps g = 2 * loc - 1 to pixel x = ((g + 1) * w - 1) / 2 =
 loc * w - 0.5; corner (x0 + dx, y0 + dy) of x0 = floor(x) has weight (dx ? fx : 1 - fx) * (dy ? fy : 1 - fy) and
 contributes only inside the map (zero padding). For finite locations, clamping x to [-2, w + 1] first changes
@@ -212,3 +218,51 @@ def torch_port(memory, value_weight, value_bias, spatial_shapes, level_start_ind
     a = attention_weights.transpose(1, 2).reshape(B * H, 1, Q, L * P)
     out = (torch.cat(parts, -1) * a).sum(-1)
     return out.view(B, H * D, Q).transpose(1, 2).contiguous()
+
+
+def producer_from_proj(proj, reference_points, spatial_shapes, n_heads, n_points):
+    """float64 sampling_locations and attention_weights from the query projection proj [B, Q, 3 * H * L * P]
+    (the 2 * H * L * P offsets, then the H * L * P logits) and the reference points / boxes."""
+    proj = _np(proj)
+    ref = _np(reference_points)
+    shapes = _np(spatial_shapes)
+    B, Q, _ = proj.shape
+    L = shapes.shape[0]
+    H, P = n_heads, n_points
+    off = proj[..., :2 * H * L * P].reshape(B, Q, H, L, P, 2)
+    logit = proj[..., 2 * H * L * P:].reshape(B, Q, H, L * P)
+    e = np.exp(logit - logit.max(-1, keepdims=True))
+    attn = (e / e.sum(-1, keepdims=True)).reshape(B, Q, H, L, P)
+    loc = np.empty((B, Q, H, L, P, 2))
+    for l in range(L):
+        h_l, w_l = float(shapes[l, 0]), float(shapes[l, 1])
+        r = ref[:, :, None, l, None, :]                                  # [B, Q, 1, 1, ref_dim]
+        o = off[:, :, :, l]                                              # [B, Q, H, P, 2]
+        if ref.shape[-1] == 2:
+            loc[:, :, :, l, :, 0] = r[..., 0] + o[..., 0] / w_l
+            loc[:, :, :, l, :, 1] = r[..., 1] + o[..., 1] / h_l
+        else:
+            loc[:, :, :, l, :, 0] = r[..., 0] + o[..., 0] / P * r[..., 2] * 0.5
+            loc[:, :, :, l, :, 1] = r[..., 1] + o[..., 1] / P * r[..., 3] * 0.5
+    return loc, attn
+
+
+def sampling_producer_oracle(query, reference_points, spatial_shapes, n_heads, n_points, sampling_weight,
+                             sampling_bias):
+    """float64 sampling_locations [B, Q, H, L, P, 2] and attention_weights [B, Q, H, L, P] of the MSDeformAttn
+    layer, from the query [B, Q, Cq], reference points [B, Q, L, 2] (x, y) or [B, Q, L, 4] (cx, cy, w, h) and the
+    packed sampling weight [W_offsets; W_attention] ([3 * H * L * P, Cq]) and bias."""
+    proj = project(query, sampling_weight, sampling_bias)
+    return producer_from_proj(proj, reference_points, spatial_shapes, n_heads, n_points)
+
+
+def deform_attn_layer_oracle(query, reference_points, memory, spatial_shapes, level_start_index, n_heads, n_points,
+                             sampling_weight, sampling_bias, value_weight, value_bias, output_weight=None,
+                             output_bias=None, value_padding_mask=None):
+    """float64 layer: sampling_producer_oracle, then ma_deform_attn_oracle on its float64 locations and weights,
+    then the optional output projection."""
+    loc, attn = sampling_producer_oracle(query, reference_points, spatial_shapes, n_heads, n_points,
+                                         sampling_weight, sampling_bias)
+    out = ma_deform_attn_oracle(memory, value_weight, value_bias, spatial_shapes, level_start_index, loc, attn,
+                                value_padding_mask)
+    return out if output_weight is None else project(out, output_weight, output_bias)

@@ -86,3 +86,40 @@ def to(args, device):
 def upcast(args):
     """The float64 copy the oracle is run on for float16 / bfloat16 inputs (upstream tests/test_correctness.py:79)."""
     return [t if t is None or t.dtype == torch.long else t.double() for t in args]
+
+
+# name, B, Q, Cq, H, D, C, levels, P -- decoder-layer geometries for the sampling producer and the whole layer
+LAYER_CASES = [
+    ('rtdetr-640 layer', 1, 300, 256, 8, 32, 256, [(80, 80), (40, 40), (20, 20)], 4),
+    ('deformable-detr 4 levels b2', 2, 100, 256, 8, 32, 256, [(50, 76), (25, 38), (13, 19), (7, 10)], 4),
+    ('narrow, query wider than memory', 2, 40, 128, 4, 16, 64, [(16, 24), (8, 12)], 8),
+    ('max level points', 1, 20, 64, 2, 16, 32, [(12, 12), (6, 6), (3, 3), (2, 2)], 16),
+    ('odd sizes', 2, 17, 40, 3, 10, 30, [(9, 11), (5, 6)], 3),
+]
+
+
+def make_layer(B, Q, Cq, H, D, C, levels, P, ref_dim=2, dtype=torch.float32, bias=True, seed=0):
+    """Seeded inputs of one deformable attention layer on CPU: (query, reference_points, memory, spatial_shapes,
+    level_start_index, sampling_weight, sampling_bias, value_weight, value_bias). Offsets come out ~ N(0, 2) pixels
+    (2-d) or ~ N(0, 2 P) box-halves (4-d); logits ~ N(0, 1.5); reference points ~ U(0, 1), boxes' w, h ~ U(0.05, 0.5)."""
+    g = torch.Generator().manual_seed(seed)
+    shapes = torch.tensor(levels, dtype=torch.long)
+    starts = torch.zeros(len(levels), dtype=torch.long)
+    starts[1:] = (shapes[:, 0] * shapes[:, 1]).cumsum(0)[:-1]
+    N = int((shapes[:, 0] * shapes[:, 1]).sum())
+    L = len(levels)
+    query = torch.randn(B, Q, Cq, generator=g)
+    memory = torch.randn(B, N, C, generator=g)
+    off_scale = 2.0 if ref_dim == 2 else 0.3 * P
+    w_off = torch.randn(2 * H * L * P, Cq, generator=g) * (off_scale / Cq ** 0.5)
+    w_att = torch.randn(H * L * P, Cq, generator=g) * (1.5 / Cq ** 0.5)
+    sampling_weight = torch.cat([w_off, w_att])
+    sampling_bias = torch.randn(3 * H * L * P, generator=g) * 0.5 if bias else None
+    value_weight = torch.randn(H * D, C, generator=g) / C ** 0.5
+    value_bias = torch.randn(H * D, generator=g) * 0.1 if bias else None
+    if ref_dim == 2:
+        ref = torch.rand(B, Q, L, 2, generator=g)
+    else:
+        ref = torch.cat([torch.rand(B, Q, L, 2, generator=g), 0.05 + 0.45 * torch.rand(B, Q, L, 2, generator=g)], -1)
+    return [t if t is None or t.dtype == torch.long else t.to(dtype)
+            for t in (query, ref, memory, shapes, starts, sampling_weight, sampling_bias, value_weight, value_bias)]

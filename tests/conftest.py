@@ -23,3 +23,13 @@ def cuda():
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.backends.cudnn.allow_tf32 = False
     return torch.device('cuda')
+
+
+@pytest.fixture(params=['tensor-cores', 'cuda-cores'])
+def policy(request, cuda):
+    """Run a test once with the default kernels (tcgen05 where shapes allow) and once on CUDA cores only."""
+    from marearts_tinydeform_b200 import _native
+    code = _native.POLICY_BEST if request.param == 'tensor-cores' else _native.POLICY_CUDA_CORES
+    prev = _native.set_kernel_policy(code)
+    yield request.param
+    _native.set_kernel_policy(prev)

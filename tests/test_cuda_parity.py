@@ -19,15 +19,6 @@ TOL = {torch.float32: (2e-5, 1e-4), torch.float16: (3e-3, 3e-3), torch.bfloat16:
 MODES = ('fused', 'project', 'auto')
 
 
-@pytest.fixture(params=['tensor-cores', 'cuda-cores'])
-def policy(request, cuda):
-    """Run a test once with the default kernels (tcgen05 where shapes allow) and once on CUDA cores only."""
-    code = _native.POLICY_BEST if request.param == 'tensor-cores' else _native.POLICY_CUDA_CORES
-    prev = _native.set_kernel_policy(code)
-    yield request.param
-    _native.set_kernel_policy(prev)
-
-
 def oracle(args):
     return torch.from_numpy(O.ma_deform_attn_oracle(*[t if t is None else t.cpu() for t in args]))
 
