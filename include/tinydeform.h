@@ -117,9 +117,10 @@ TD_API int td_sampling_producer(int dtype, const void* proj, const void* referen
  *   attn = ma_deform_attn(memory [B, N, C], value_weight [HD, C], value_bias, ...)  [B, Q, HD], with the optional
  *          value padding mask [B, N] of td_project_forward_masked
  *   out  = attn @ output_weight^T + output_bias  [B, Q, C_out] when output_weight is not NULL, else out = attn.
- * order TD_ORDER_PROJECT: three launches (query projection, value projection, sampler whose corner prologue runs
- * the producer, so locations and weights never reach memory); TD_ORDER_FUSED: query projection, producer, the
- * fused gather-then-project kernel. Plus the output projection. Intermediates live in `workspace` of at least
+ * order TD_ORDER_PROJECT: two launches -- the value and query projections in one tensor-core launch (when both fit
+ * it and share C; else two), then the sampler whose corner prologue runs the producer, so locations and weights
+ * never reach memory; TD_ORDER_FUSED: query projection, producer, the fused gather-then-project kernel. Plus the
+ * output projection. Intermediates live in `workspace` of at least
  * td_layer_workspace_bytes() bytes (same arguments; output_proj = output_weight != NULL). No counterpart in upstream,
  * which implements only the operator.
  */

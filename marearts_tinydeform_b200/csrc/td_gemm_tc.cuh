@@ -35,20 +35,29 @@
 
 namespace td {
 
+// One projection of a launch. A launch runs one or two (the decoder layer's value projection and query projection
+// share K and ride in one persistent grid: the second one's tiles follow the first one's).
 template <typename T>
-struct ProjTcArgs {
+struct ProjJob {
     const T* bias;  // [HD] or null
     T* value;
     int N;            // tokens per image
-    int C, HD, H, D;
+    int HD, H, D;
     int head_major;
-    int k_blocks;     // ceil(C / kBK)
     int n_tiles;      // ceil(HD / BN)
     int m_tiles;      // ceil(N / 128): token tiles per image
-    int tiles;        // B * m_tiles * n_tiles (< 2^31)
+    int tiles;        // B * m_tiles * n_tiles (< 2^31); 0 for an absent second job
     // epilogue through TMA stores: boxes of `piece` columns (piece_bytes = piece * sizeof(T) in {16, 32, 64, 128})
     // x 32 tokens, 0 = direct stores
     int tma_store, piece, piece_bytes;
+};
+
+template <typename T>
+struct ProjTcArgs {
+    ProjJob<T> job[2];
+    int C;
+    int k_blocks;     // ceil(C / kBK), the same for both jobs
+    int tiles;        // job[0].tiles + job[1].tiles (< 2^31)
 };
 
 constexpr int kTcBM = 128;
@@ -153,9 +162,10 @@ __device__ __forceinline__ void pack8(const float* f, uint4* w) {
 // The projection tiles of this CTA, from barrier setup to TMEM release (ends with a CTA-wide barrier; every value
 // store of the CTA has completed by then). smem is the 1024-byte aligned dynamic shared memory.
 template <typename T, int BN, int EPI>
-__device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CUtensorMap& map_b,
-                                              const CUtensorMap& map_out, const ProjTcArgs<T>& a,
-                                              unsigned char* smem) {
+__device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const CUtensorMap& map_b0,
+                                              const CUtensorMap& map_out0, const CUtensorMap& map_a1,
+                                              const CUtensorMap& map_b1, const CUtensorMap& map_out1,
+                                              const ProjTcArgs<T>& a, unsigned char* smem) {
     using Lay = ProjTcLayout<T, BN, EPI>;
     constexpr int S = Lay::kStages;
     constexpr int kBK = Lay::kBK;
@@ -188,9 +198,14 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
             mbar_init(&tempty[i], EPI);  // one arrival per epilogue warp
         }
         mbar_fence_init();
-        tma_prefetch_desc(&map_a);
-        tma_prefetch_desc(&map_b);
-        if (a.tma_store) tma_prefetch_desc(&map_out);
+        tma_prefetch_desc(&map_a0);
+        tma_prefetch_desc(&map_b0);
+        if (a.job[0].tma_store) tma_prefetch_desc(&map_out0);
+        if (a.job[1].tiles > 0) {
+            tma_prefetch_desc(&map_a1);
+            tma_prefetch_desc(&map_b1);
+            if (a.job[1].tma_store) tma_prefetch_desc(&map_out1);
+        }
     }
     __syncwarp();
     if (warp == 0) {
@@ -201,14 +216,18 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    // tile t -> image b, first token n0, first channel c0 (32-bit: the host keeps the tile count below 2^31)
-    const int per_img = a.m_tiles * a.n_tiles;
-    auto tile_at = [&](int t, int& b, int& n0, int& c0) {
+    // tile t -> job j, image b, first token n0, first channel c0 (32-bit: the host keeps the tile count below 2^31)
+    const int tiles0 = a.job[0].tiles;
+    auto tile_at = [&](int t, int& j, int& b, int& n0, int& c0) {
+        j = t >= tiles0;
+        if (j) t -= tiles0;
+        const int n_tiles = j ? a.job[1].n_tiles : a.job[0].n_tiles;
+        const int per_img = (j ? a.job[1].m_tiles : a.job[0].m_tiles) * n_tiles;
         b = t / per_img;
         const int r = t - b * per_img;
-        const int mt = r / a.n_tiles;
+        const int mt = r / n_tiles;
         n0 = mt * kTcBM;
-        c0 = (r - mt * a.n_tiles) * BN;
+        c0 = (r - mt * n_tiles) * BN;
     };
     const int my_tiles = a.tiles > int(blockIdx.x) ? (a.tiles - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
     // Under programmatic dependent launch everything up to a thread's first global access overlaps the previous
@@ -232,8 +251,8 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
                 if (mbar_test(&empty[s], uint32_t((it / S) & 1) ^ 1u)) {
                     if (it < total) {
                         const int tl = it / KB, kb = it - tl * KB;
-                        int b, n0, c0;
-                        tile_at(int(blockIdx.x) + tl * int(gridDim.x), b, n0, c0);
+                        int j, b, n0, c0;
+                        tile_at(int(blockIdx.x) + tl * int(gridDim.x), j, b, n0, c0);
                         if (!waited) {
                             grid_dependency_wait();
                             launch_dependents();
@@ -241,10 +260,10 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
                         }
                         if (box_a) {
                             mbar_arrive_expect_tx(&full[s], Lay::kABytes);
-                            tma_load_3d(slot_a(s), &map_a, &full[s], kb * kBK, n0, b);
+                            tma_load_3d(slot_a(s), j ? &map_a1 : &map_a0, &full[s], kb * kBK, n0, b);
                         } else {
                             mbar_arrive_expect_tx(&full[s], Lay::kBBytes);
-                            tma_load_2d(slot_b(s), &map_b, &full[s], kb * kBK, c0);
+                            tma_load_2d(slot_b(s), j ? &map_b1 : &map_b0, &full[s], kb * kBK, c0);
                         }
                     }
                     it += S;
@@ -304,9 +323,7 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
         constexpr int kCols = EPI == 8 ? BN / 2 : BN;  // columns this warp converts
         const int c_lo = EPI == 8 ? (ew >> 2) * kCols : 0;
         const int r = quarter * 32 + lane;  // tile row = TMEM lane
-        const int pb = a.piece_bytes;
-        const int pshift = 31 - __clz(a.piece);  // piece is a power of two
-        const int swz = pb / 16 - 1;             // 16-byte chunk index ^= (row * pb / 128) & swz
+        const bool any_tma_store = a.job[0].tma_store || (a.job[1].tiles > 0 && a.job[1].tma_store);
         // After a wait that gave up, a warp still walks its tiles and takes part in every named barrier (so no
         // other epilogue warp waits on it), but reads no TMEM and stores nothing.
         bool dead = false;
@@ -316,25 +333,30 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
         for (int tc = -1; tc < my_tiles; ++tc) {
             const bool dry = tc < 0;
             const int acc = tc & 1;
-            int b, n0, c0;
-            tile_at(int(blockIdx.x) + (dry ? 0 : tc) * int(gridDim.x), b, n0, c0);
+            int j, b, n0, c0;
+            tile_at(int(blockIdx.x) + (dry ? 0 : tc) * int(gridDim.x), j, b, n0, c0);
+            const ProjJob<T> J = j ? a.job[1] : a.job[0];
+            const CUtensorMap* map_out = j ? &map_out1 : &map_out0;
+            const int pb = J.piece_bytes;
+            const int pshift = 31 - __clz(J.piece);  // piece is a power of two
+            const int swz = pb / 16 - 1;             // 16-byte chunk index ^= (row * pb / 128) & swz
             if (tc == 0) grid_dependency_wait();  // the dry pass reads and writes no global memory
             // this tile's bias; the previous tile's readers are past its second barrier
             for (int i = etid; i < BN; i += kEpiThreads)
-                sbias[i] = (!dry && a.bias != nullptr && c0 + i < a.HD) ? to_acc(a.bias[c0 + i]) : 0.f;
+                sbias[i] = (!dry && J.bias != nullptr && c0 + i < J.HD) ? to_acc(J.bias[c0 + i]) : 0.f;
             // the staging tile is free once the previous tile's stores have read it
-            if (a.tma_store) bulk_wait_read();
+            if (any_tma_store) bulk_wait_read();
             named_barrier(1, kEpiThreads);
             bool ready = dry || (!dead && mbar_wait(&tfull[acc], uint32_t((tc >> 1) & 1), kErrMmaWait));
             ready = __all_sync(0xffffffffu, ready);
             dead = !ready;
             tc_fence_after();
             const int n = n0 + r;
-            const long long m = (long long)b * a.N + n;
+            const long long m = (long long)b * J.N + n;
 #pragma unroll 1
             for (int j = 0; j < kCols / 32; ++j) {
                 const int cl = c_lo + 32 * j;  // tile column of this chunk
-                const bool live = ready && c0 + cl < a.HD;  // uniform across the warp
+                const bool live = ready && c0 + cl < J.HD;  // uniform across the warp
                 uint32_t v[32];
                 if (live && !dry) {
                     tmem_ld_32x32b_x32(tmem + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN + cl), v);
@@ -363,24 +385,24 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
                     for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(v[8 * g + i]) + bb[i];
                     uint4 w[kWords];
                     pack8<T>(f, w);
-                    if (a.tma_store) {
+                    if (J.tma_store) {
                         // piece p = c / piece, 16-byte chunk q within the piece's row r
                         const int p = c >> pshift, q = ((c - (p << pshift)) * int(sizeof(T))) >> 4;
                         unsigned char* row = stg + p * (kTcBM * pb) + r * pb;
                         const int x = (r * pb >> 7) & swz;
 #pragma unroll
                         for (int k = 0; k < kWords; ++k) *reinterpret_cast<uint4*>(row + (((q + k) ^ x) << 4)) = w[k];
-                    } else if (!dry && n < a.N && c0 + c < a.HD) {
-                        const int col = c0 + c, h = col / a.D;
-                        T* dst = a.head_major
-                                     ? a.value + (((long long)b * a.H + h) * a.N + n) * a.D + (col - h * a.D)
-                                     : a.value + m * a.HD + col;
+                    } else if (!dry && n < J.N && c0 + c < J.HD) {
+                        const int col = c0 + c, h = col / J.D;
+                        T* dst = J.head_major
+                                     ? J.value + (((long long)b * J.H + h) * J.N + n) * J.D + (col - h * J.D)
+                                     : J.value + m * J.HD + col;
 #pragma unroll
                         for (int k = 0; k < kWords; ++k) reinterpret_cast<uint4*>(dst)[k] = w[k];
                     }
                 }
             }
-            if (a.tma_store) {
+            if (J.tma_store) {
                 // this warp's boxes -- its columns [c_lo, c_lo + kCols) by its 32 rows -- as soon as it has staged
                 // them, without waiting for the other epilogue warps
                 fence_proxy_async_smem();  // the TMA stores (async proxy) read what these threads wrote
@@ -388,20 +410,20 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a, const CU
                 // one box per lane: the TMA operations of one thread are served one after another
                 const int p = (c_lo >> pshift) + lane;
                 const int col = c0 + (p << pshift);
-                if (ready && !dry && p < ((c_lo + kCols) >> pshift) && col < a.HD) {
+                if (ready && !dry && p < ((c_lo + kCols) >> pshift) && col < J.HD) {
                     const unsigned char* src = stg + p * (kTcBM * pb) + quarter * 32 * pb;
-                    if (a.head_major) {
-                        const int h = col / a.D;
-                        tma_store_3d(&map_out, src, col - h * a.D, n0 + quarter * 32, b * a.H + h);
+                    if (J.head_major) {
+                        const int h = col / J.D;
+                        tma_store_3d(map_out, src, col - h * J.D, n0 + quarter * 32, b * J.H + h);
                     } else {
-                        tma_store_3d(&map_out, src, col, n0 + quarter * 32, b);
+                        tma_store_3d(map_out, src, col, n0 + quarter * 32, b);
                     }
                     bulk_commit();
                 }
             }
         }
         // the CTA may exit once its stores have read the staging tile; the grid completes only when they are written
-        if (a.tma_store) bulk_wait_read();
+        if (any_tma_store) bulk_wait_read();
     } else if (kSplit && warp >= Lay::kSplitWarp0) {
         // float32: split every landed slot into hi (in place) and lo
         const int tid = (warp - Lay::kSplitWarp0) * 32 + lane;  // 128 threads
@@ -448,12 +470,15 @@ __device__ __forceinline__ unsigned char* align1024(unsigned char* p) {
 
 // 72 registers a thread (no spills): 12 warps, 3 per SM sub-partition (27 K registers), leave room on the SM for two
 // CTAs of the sampler that follows in the project order (launched early, under programmatic dependent launch).
+// Tensor maps of job 0 (memory, weight, output) and job 1 (the same; copies of job 0's when there is no job 1).
 template <typename T, int BN, int EPI>
 __global__ void __maxnreg__(72)
-    proj_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                   const __grid_constant__ CUtensorMap map_out, const ProjTcArgs<T> a) {
+    proj_tc_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_b0,
+                   const __grid_constant__ CUtensorMap map_out0, const __grid_constant__ CUtensorMap map_a1,
+                   const __grid_constant__ CUtensorMap map_b1, const __grid_constant__ CUtensorMap map_out1,
+                   const ProjTcArgs<T> a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    proj_tc_tiles<T, BN, EPI>(map_a, map_b, map_out, a, align1024(smem_raw));
+    proj_tc_tiles<T, BN, EPI>(map_a0, map_b0, map_out0, map_a1, map_b1, map_out1, a, align1024(smem_raw));
 }
 
 }  // namespace td

@@ -24,11 +24,15 @@ struct ProducerIn {
     const T* proj = nullptr;  // [B * Q, 3 * H * L * P]
     const T* ref = nullptr;   // [B, Q, L, ref_dim]
     int ref_dim = 2;
+    // proj is written by the kernel right before this one (launched with programmatic serialization): wait for it
+    // (griddepcontrol.wait) between the loads of the reference points and those of proj
+    int wait_first = 0;
 };
 
 // Locations (lx, ly) and softmax weight w of the points j = lane + 32 k (k = 0, 1) of row `row` = (b * Q + q) * H + h;
 // a lane with j >= L * P gets w = 0. Every lane of the warp must call it (the softmax is a warp reduction).
-// All global loads of the row are issued before the first shuffle.
+// All global loads of the row are issued before the first shuffle (with wait_first, the reference points and level
+// sizes before the grid dependency wait, proj after it).
 template <typename T, typename A>
 __device__ __forceinline__ void produce_row(const ProducerIn<T>& in, const int64_t* __restrict__ shapes,
                                             long long row, int H, int L, int P, int lane, A (&lx)[2], A (&ly)[2],
@@ -45,9 +49,6 @@ __device__ __forceinline__ void produce_row(const ProducerIn<T>& in, const int64
         const int j = lane + 32 * k;
         const bool on = j < LP;
         const int l = on ? j / P : 0;
-        x[k] = on ? to_acc(logit[j]) : A(-INFINITY);
-        ox[k] = on ? to_acc(off[2 * j]) : A(0);
-        oy[k] = on ? to_acc(off[2 * j + 1]) : A(0);
         const T* __restrict__ r = in.ref + (bq * L + l) * in.ref_dim;
         rx[k] = on ? to_acc(r[0]) : A(0);
         ry[k] = on ? to_acc(r[1]) : A(0);
@@ -58,6 +59,15 @@ __device__ __forceinline__ void produce_row(const ProducerIn<T>& in, const int64
             sx[k] = on ? to_acc(r[2]) : A(0);
             sy[k] = on ? to_acc(r[3]) : A(0);
         }
+    }
+    if (in.wait_first) grid_dependency_wait();
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int j = lane + 32 * k;
+        const bool on = j < LP;
+        x[k] = on ? to_acc(logit[j]) : A(-INFINITY);
+        ox[k] = on ? to_acc(off[2 * j]) : A(0);
+        oy[k] = on ? to_acc(off[2 * j + 1]) : A(0);
     }
     A m = x[0] > x[1] ? x[0] : x[1];
 #pragma unroll

@@ -54,14 +54,21 @@ __device__ __forceinline__ void sample_row_corners(const SampleArgs<T>& a, long 
     const uint8_t* mask_b = a.mask != nullptr ? a.mask + row / ((long long)a.Q * a.H) * a.n_tok : nullptr;
     if (a.prod.proj != nullptr) {  // the producer's softmax and locations, straight from the query projection
         using A = typename Elem<T>::acc;
+        // the level geometry first: with prod.wait_first it is read before the dependency wait, with the reference
+        // points, and the corners then follow proj by one round trip
+        Level lv[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int j = lane + 32 * k;
+            lv[k] = level_at(a.shapes, a.starts, j < LP ? j / a.P : 0);
+        }
         A lx[2], ly[2], w[2];
         produce_row<T, A>(a.prod, a.shapes, row, a.H, a.L, a.P, lane, lx, ly, w);
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
             const int j = lane + 32 * k;
             if (j < LP)
-                corners4<CT>(CT(lx[k]), CT(ly[k]), CT(w[k]), level_at(a.shapes, a.starts, j / a.P), a.n_tok,
-                             &s_tok[4 * j], &s_wt[4 * j], mask_b);
+                corners4<CT>(CT(lx[k]), CT(ly[k]), CT(w[k]), lv[k], a.n_tok, &s_tok[4 * j], &s_wt[4 * j], mask_b);
         }
         return;
     }
@@ -126,10 +133,12 @@ __device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long l
     if (cg == 0) store16<T>(a.out + row * a.D + v * V, acc);
 }
 
-// With prod.proj set, the corners come from the query projection (produce_row): that projection is then written
-// two launches earlier (query projection -> value projection -> this kernel), and the value projection, launched
-// with programmatic serialization, lets this kernel start only after its own grid dependency wait has seen the
-// query projection complete, so the corner prologue may read it before this kernel's own wait.
+// With prod.proj set, the corners come from the query projection (produce_row). Either that projection ran in the
+// same launch as the value projection right before this kernel (prod.wait_first: the corner prologue waits for
+// that launch between its reads of the reference points and of proj), or two launches earlier (query projection ->
+// value projection -> this kernel): the value projection, launched with programmatic serialization, lets this
+// kernel start only after its own grid dependency wait has seen the query projection complete, so the corner
+// prologue may read proj before this kernel's own wait.
 // Vector kernel: needs D * sizeof(T) % 16 == 0, D * sizeof(T) <= 512, 16-byte aligned value/out and strides.
 // The dependent-latency chain is kept to two memory round trips: (level geometry + locations + attention weights,
 // all issued together) -> corners -> (every corner row of the lane's group issued together) -> butterfly -> store.

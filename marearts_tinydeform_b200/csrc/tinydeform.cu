@@ -328,13 +328,26 @@ int allow_smem(K kernel, size_t bytes, std::atomic<uint64_t>& done, char* err, s
     return TD_OK;
 }
 
-// Tensor maps and arguments of the tcgen05 projection kernel.
+// One projection of the tcgen05 kernel: value[B, N, HD] (or head-major [B, H, N, D]) = memory[B, N, C] @ W^T + b.
+struct ProjShape {
+    const void* memory;
+    const void* weight;
+    const void* bias;
+    void* value;
+    int64_t B, N, C, H, HD;
+    int head_major;
+};
+
+// Tensor maps and arguments of one job of the tcgen05 projection kernel.
 template <typename T, int BN, int EPI>
-int prepare_proj_tc(const T* memory, const T* weight, const T* bias, T* value, int64_t B, int64_t N, int64_t C,
-                    int64_t H, int64_t HD, int head_major, CUtensorMap* map_a, CUtensorMap* map_b,
-                    CUtensorMap* map_out, ProjTcArgs<T>* args, char* err, size_t err_len) {
-    using Lay = ProjTcLayout<T, BN, EPI>;
+int prepare_proj_tc(const ProjShape& ps, CUtensorMap* map_a, CUtensorMap* map_b, CUtensorMap* map_out,
+                    ProjJob<T>* job, char* err, size_t err_len) {
     constexpr uint32_t e = sizeof(T);
+    const T* memory = static_cast<const T*>(ps.memory);
+    const T* weight = static_cast<const T*>(ps.weight);
+    const int64_t B = ps.B, N = ps.N, C = ps.C, H = ps.H, HD = ps.HD;
+    const int head_major = ps.head_major;
+    T* value = static_cast<T*>(ps.value);
     const int64_t D = HD / H;
     {
         // memory as [B][N][C]: 128-token boxes never cross into the next image (rows past N read as zeros)
@@ -374,10 +387,9 @@ int prepare_proj_tc(const T* memory, const T* weight, const T* bias, T* value, i
             if (int rc = tensor_map_3d(map_out, value, dims, strides, box, e, sw, err, err_len)) return rc;
         }
     }
-    ProjTcArgs<T>& a = *args;
-    a.bias = bias; a.value = value; a.N = int(N); a.C = int(C); a.HD = int(HD); a.H = int(H); a.D = int(D);
-    a.head_major = head_major;
-    a.k_blocks = int((C + Lay::kBK - 1) / Lay::kBK);
+    ProjJob<T>& a = *job;
+    a.bias = static_cast<const T*>(ps.bias); a.value = value; a.N = int(N); a.HD = int(HD); a.H = int(H);
+    a.D = int(D); a.head_major = head_major;
     a.n_tiles = int((HD + BN - 1) / BN);
     a.m_tiles = int((N + kTcBM - 1) / kTcBM);
     a.tiles = int(B * a.m_tiles * a.n_tiles);
@@ -385,24 +397,35 @@ int prepare_proj_tc(const T* memory, const T* weight, const T* bias, T* value, i
     return TD_OK;
 }
 
+// One launch of the tcgen05 projection kernel for job0 and, when job1 is not null, job1 (same C): job1's tiles
+// follow job0's in the persistent grid.
 template <typename T, int BN, int EPI>
-int launch_proj_tc(const T* memory, const T* weight, const T* bias, T* value, int64_t B, int64_t N, int64_t C,
-                   int64_t H, int64_t HD, int head_major, cudaStream_t stream, bool pdl, char* err,
+int launch_proj_tc(const ProjShape& job0, const ProjShape* job1, cudaStream_t stream, bool pdl, char* err,
                    size_t err_len) {
     using Lay = ProjTcLayout<T, BN, EPI>;
     static std::atomic<uint64_t> smem_done{0};
     DeviceFacts f;
     if (int rc = device_facts(&f, err, err_len)) return rc;
-    CUtensorMap map_a, map_b, map_out;
+    CUtensorMap map_a0, map_b0, map_out0, map_a1, map_b1, map_out1;
     ProjTcArgs<T> a;
-    if (int rc = prepare_proj_tc<T, BN, EPI>(memory, weight, bias, value, B, N, C, H, HD, head_major, &map_a, &map_b,
-                                             &map_out, &a, err, err_len))
-        return rc;
+    if (int rc = prepare_proj_tc<T, BN, EPI>(job0, &map_a0, &map_b0, &map_out0, &a.job[0], err, err_len)) return rc;
+    if (job1 != nullptr) {
+        if (int rc = prepare_proj_tc<T, BN, EPI>(*job1, &map_a1, &map_b1, &map_out1, &a.job[1], err, err_len))
+            return rc;
+    } else {
+        map_a1 = map_a0; map_b1 = map_b0; map_out1 = map_out0;
+        a.job[1] = a.job[0];
+        a.job[1].tiles = 0;
+    }
+    a.C = int(job0.C);
+    a.k_blocks = int((job0.C + Lay::kBK - 1) / Lay::kBK);
+    a.tiles = a.job[0].tiles + a.job[1].tiles;
     if (int rc = allow_smem(proj_tc_kernel<T, BN, EPI>, Lay::kSmemBytes, smem_done, err, err_len)) return rc;
     // persistent: at most one CTA per SM (the slot ring takes most of the shared memory)
     const int grid = a.tiles < f.sm_count ? a.tiles : f.sm_count;
     const cudaError_t err_launch = launch_kernel(proj_tc_kernel<T, BN, EPI>, dim3(unsigned(grid)), dim3(Lay::kThreads),
-                                                 Lay::kSmemBytes, stream, pdl, map_a, map_b, map_out, a);
+                                                 Lay::kSmemBytes, stream, pdl, map_a0, map_b0, map_out0, map_a1,
+                                                 map_b1, map_out1, a);
     if (err_launch != cudaSuccess)
         return fail(err, err_len, TD_ERR_CUDA, "proj_tc_kernel launch: %s", cudaGetErrorString(err_launch));
     g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -437,16 +460,19 @@ bool proj_tc_eligible(const T* memory, const T* weight, const T* value, int64_t 
 
 // Tile width of the tcgen05 projection: the busiest CTA runs ceil(tiles / SMs) tiles, each costing about the load
 // of its 128 memory rows (like 128 more output columns) plus BN output columns; the width that makes that smallest,
-// the widest of equals. float32 tiles are at most 128 wide (their slots hold hi and lo halves).
+// the widest of equals. float32 tiles are at most 128 wide (their slots hold hi and lo halves). (B2, N2, HD2): a
+// second job in the same launch (B2 = 0: none).
 template <typename T>
-int proj_tile_width(int64_t B, int64_t N, int64_t HD, int sm_count) {
+int proj_tile_width(int64_t B, int64_t N, int64_t HD, int sm_count, int64_t B2 = 0, int64_t N2 = 0,
+                    int64_t HD2 = 0) {
     if (TD_PROJ_TILE != 0) return TD_PROJ_TILE;
     const int64_t m_tiles = B * ((N + kTcBM - 1) / kTcBM);
+    const int64_t m_tiles2 = B2 * ((N2 + kTcBM - 1) / kTcBM);
     int bn = 64;
     long long best = -1;
     for (int w : {256, 128, 64}) {
         if (std::is_same<T, float>::value && w > 128) continue;
-        const long long tiles = m_tiles * ((HD + w - 1) / w);
+        const long long tiles = m_tiles * ((HD + w - 1) / w) + m_tiles2 * ((HD2 + w - 1) / w);
         const long long cost = (tiles + sm_count - 1) / sm_count * (w + 128);
         if (best < 0 || cost < best) { best = cost; bn = w; }
     }
@@ -474,9 +500,10 @@ int launch_proj(const T* memory, const T* weight, const T* bias, T* value, int64
         if (proj_tc_eligible<T>(memory, weight, value, B, N, C, H, HD)) {
             DeviceFacts f;
             if (int rc = device_facts(&f, err, err_len)) return rc;
+            const ProjShape job{memory, weight, bias, value, B, N, C, H, HD, head_major};
             return with_tile<T>(proj_tile_width<T>(B, N, HD, f.sm_count), [&](auto bn, auto epi) {
-                return launch_proj_tc<T, decltype(bn)::value, decltype(epi)::value>(
-                    memory, weight, bias, value, B, N, C, H, HD, head_major, stream, pdl, err, err_len);
+                return launch_proj_tc<T, decltype(bn)::value, decltype(epi)::value>(job, nullptr, stream, pdl, err,
+                                                                                    err_len);
             });
         }
     }
@@ -489,6 +516,38 @@ int launch_proj(const T* memory, const T* weight, const T* bias, T* value, int64
     if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "proj_simt_kernel launch: %s", cudaGetErrorString(e));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return check_launch(err, err_len, "proj_simt_kernel");
+}
+
+// Two projections with the same K in one tcgen05 launch when both fit it (*paired = true); otherwise nothing is
+// launched (*paired = false) and the caller launches them one by one.
+template <typename T>
+int launch_proj_pair(const ProjShape& j0, const ProjShape& j1, cudaStream_t stream, bool pdl, bool* paired,
+                     char* err, size_t err_len) {
+    *paired = false;
+    if constexpr (kTcType<T>) {
+        const auto* m0 = static_cast<const T*>(j0.memory);
+        const auto* m1 = static_cast<const T*>(j1.memory);
+        if (j0.C != j1.C || j0.B * j0.N == 0 || j1.B * j1.N == 0 ||
+            !proj_tc_eligible<T>(m0, static_cast<const T*>(j0.weight), static_cast<const T*>(j0.value), j0.B, j0.N,
+                                 j0.C, j0.H, j0.HD) ||
+            !proj_tc_eligible<T>(m1, static_cast<const T*>(j1.weight), static_cast<const T*>(j1.value), j1.B, j1.N,
+                                 j1.C, j1.H, j1.HD))
+            return TD_OK;
+        const int64_t t64 = j0.B * ((j0.N + kTcBM - 1) / kTcBM) * ((j0.HD + 63) / 64) +
+                            j1.B * ((j1.N + kTcBM - 1) / kTcBM) * ((j1.HD + 63) / 64);
+        if (t64 * ((j0.C + GemmKind<T>::kBK - 1) / GemmKind<T>::kBK) >= (int64_t(1) << 31)) return TD_OK;
+        DeviceFacts f;
+        if (int rc = device_facts(&f, err, err_len)) return rc;
+        *paired = true;
+        return with_tile<T>(proj_tile_width<T>(j0.B, j0.N, j0.HD, f.sm_count, j1.B, j1.N, j1.HD),
+                            [&](auto bn, auto epi) {
+                                return launch_proj_tc<T, decltype(bn)::value, decltype(epi)::value>(
+                                    j0, &j1, stream, pdl, err, err_len);
+                            });
+    } else {
+        (void)j0; (void)j1; (void)stream; (void)pdl; (void)err; (void)err_len;
+        return TD_OK;
+    }
 }
 
 template <typename F>
@@ -797,30 +856,42 @@ int td_layer_forward(int dtype, int order, const void* query, int64_t Cq, const 
         T* proj = reinterpret_cast<T*>(ws + w.proj);
         T* target = output_weight != nullptr ? reinterpret_cast<T*>(ws + w.mid) : static_cast<T*>(out);
         const T* ref = static_cast<const T*>(reference_points);
-        // 1. the query projection: offsets and attention logits of every (batch, query) row
-        if (int rc = launch_proj<T>(static_cast<const T*>(query), static_cast<const T*>(sampling_weight),
-                                    static_cast<const T*>(sampling_bias), proj, 1, B * Q, Cq, 1, LP3, 0, s, err,
-                                    err_len, true))
-            return rc;
+        // the query projection: offsets and attention logits of every (batch, query) row
+        const ProjShape jq{query, sampling_weight, sampling_bias, proj, 1, B * Q, Cq, 1, LP3, 0};
+        auto query_proj = [&] {
+            return launch_proj<T>(static_cast<const T*>(query), static_cast<const T*>(sampling_weight),
+                                  static_cast<const T*>(sampling_bias), proj, 1, B * Q, Cq, 1, LP3, 0, s, err,
+                                  err_len, true);
+        };
         if (order == TD_ORDER_PROJECT) {
-            // 2. the value projection (head-major), 3. the sampler, whose corner prologue runs the producer on the
-            // query projection (written two launches earlier, see sample_vec_kernel)
+            // 1. the value projection (head-major) and the query projection, in one tcgen05 launch when both fit it
+            // (the query tiles take SMs the value tiles leave idle), else one after the other; 2. the sampler, whose
+            // corner prologue runs the producer on the query projection (see sample_vec_kernel)
             T* value = reinterpret_cast<T*>(ws + w.value);
+            bool paired = false;
             if (N > 0) {
-                if (int rc = launch_proj<T>(static_cast<const T*>(memory), static_cast<const T*>(value_weight),
-                                            static_cast<const T*>(value_bias), value, B, N, C, H, HD, 1, s, err,
-                                            err_len, true))
-                    return rc;
+                const ProjShape jv{memory, value_weight, value_bias, value, B, N, C, H, HD, 1};
+                if (int rc = launch_proj_pair<T>(jv, jq, s, true, &paired, err, err_len)) return rc;
+            }
+            if (!paired) {
+                if (int rc = query_proj()) return rc;
+                if (N > 0) {
+                    if (int rc = launch_proj<T>(static_cast<const T*>(memory), static_cast<const T*>(value_weight),
+                                                static_cast<const T*>(value_bias), value, B, N, C, H, HD, 1, s, err,
+                                                err_len, true))
+                        return rc;
+                }
             }
             ProducerIn<T> prod;
-            prod.proj = proj; prod.ref = ref; prod.ref_dim = ref_dim;
+            prod.proj = proj; prod.ref = ref; prod.ref_dim = ref_dim; prod.wait_first = paired ? 1 : 0;
             // with no value projection in between, the sampler follows the query projection in plain stream order
             if (int rc = launch_sampler<T>(value, H * N * D, D, N * D, spatial_shapes, level_start_index, nullptr,
                                            nullptr, target, B, Q, N, H, D, L, P, s, err, err_len, N > 0,
                                            value_padding_mask, prod))
                 return rc;
         } else {
-            // 2. locations and weights, 3. the fused gather-then-project kernel
+            // 1. the query projection, 2. locations and weights, 3. the fused gather-then-project kernel
+            if (int rc = query_proj()) return rc;
             T* loc = reinterpret_cast<T*>(ws + w.loc);
             T* attn = reinterpret_cast<T*>(ws + w.attn);
             if (int rc = launch_producer<T>(proj, ref, ref_dim, spatial_shapes, loc, attn, B, Q, H, L, P, s, err,
@@ -832,7 +903,7 @@ int td_layer_forward(int dtype, int order, const void* query, int64_t Cq, const 
                 return rc;
         }
         if (output_weight == nullptr) return int(TD_OK);
-        // 4. the output projection of the attention result
+        // then the output projection of the attention result
         return launch_proj<T>(target, static_cast<const T*>(output_weight), static_cast<const T*>(output_bias),
                               static_cast<T*>(out), 1, B * Q, HD, 1, C_out, 0, s, err, err_len, true);
     });
