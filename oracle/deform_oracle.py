@@ -127,6 +127,75 @@ def ma_deform_attn_oracle(memory, value_weight, value_bias, spatial_shapes, leve
     return sample(value, H, spatial_shapes, level_start_index, sampling_locations, attention_weights)
 
 
+def sample_backward(value, n_head, spatial_shapes, level_start_index, sampling_locations, attention_weights,
+                    grad_out):
+    """Gradients of sample() with respect to value [B, N, H*D], sampling_locations and attention_weights, given
+    grad_out [B, Q, H*D], in float64: the derivative of grid_sample's bilinear rule (x = loc * w - 0.5, corners
+    weighted (dx ? fx : 1 - fx) * (dy ? fy : 1 - fy), zero outside the map), which is what autograd computes
+    through reference.py:29-40. d x / d loc = w, so d out / d loc_x = attn * w * sum over corners of
+    (dx ? 1 : -1) * (dy ? fy : 1 - fy) * <grad_out, value[corner]>, and likewise for y."""
+    value = _np(value)
+    shapes, starts = _np(spatial_shapes), _np(level_start_index)
+    loc, attn, g = _np(sampling_locations), _np(attention_weights), _np(grad_out)
+    B, N, HD = value.shape
+    _, Q, H, L, P, _ = loc.shape
+    D = HD // H
+    v = value.reshape(B, N, H, D)
+    g = g.reshape(B, Q, H, D)
+    grad_value = np.zeros((B, N, H, D))
+    grad_loc = np.zeros(loc.shape)
+    grad_attn = np.zeros(attn.shape)
+    bi = np.broadcast_to(np.arange(B).reshape(B, 1, 1, 1), (B, Q, H, P))
+    hi = np.broadcast_to(np.arange(H).reshape(1, 1, H, 1), (B, Q, H, P))
+    for lvl in range(L):
+        h_l, w_l = int(shapes[lvl, 0]), int(shapes[lvl, 1])
+        ones = np.ones(attn[:, :, :, lvl].shape)
+        tok, wt = level_corners(loc[:, :, :, lvl], ones, h_l, w_l, int(starts[lvl]), N)   # [B, Q, H, P, 4]
+        def pixel(u, size):
+            p = u * size - 0.5
+            p = np.where(np.isnan(p), -2.0, p)
+            return np.clip(p, -2.0, size + 1.0)
+        x = pixel(loc[:, :, :, lvl, :, 0], w_l)
+        y = pixel(loc[:, :, :, lvl, :, 1], h_l)
+        fx, fy = x - np.floor(x), y - np.floor(y)
+        a = attn[:, :, :, lvl]                                                             # [B, Q, H, P]
+        for k in range(4):
+            dx, dy = k & 1, k >> 1
+            t = tok[..., k]
+            inside = t >= 0
+            rows = np.where(inside[..., None], v[bi, np.maximum(t, 0), hi], 0.0)           # [B, Q, H, P, D]
+            dot = np.einsum('bqhd,bqhpd->bqhp', g, rows)
+            grad_attn[:, :, :, lvl] += wt[..., k] * dot
+            grad_loc[:, :, :, lvl, :, 0] += a * w_l * (1.0 if dx else -1.0) * (fy if dy else 1.0 - fy) * dot
+            grad_loc[:, :, :, lvl, :, 1] += a * h_l * (1.0 if dy else -1.0) * (fx if dx else 1.0 - fx) * dot
+            contrib = (a * wt[..., k])[..., None] * g[:, :, :, None, :]                    # [B, Q, H, P, D]
+            sel = np.nonzero(inside)
+            np.add.at(grad_value, (bi[sel], t[sel], hi[sel]), contrib[sel])
+    return grad_value.reshape(B, N, HD), grad_loc, grad_attn
+
+
+def ma_deform_attn_backward_oracle(memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                                   sampling_locations, attention_weights, grad_out, value_padding_mask=None):
+    """float64 gradients of ma_deform_attn_oracle for grad_out [B, Q, H*D]: a dict with 'memory', 'value_weight',
+    'value_bias' (None without bias), 'sampling_locations', 'attention_weights' -- what torch autograd gives through
+    upstream's reference (nn.Linear, masked_fill, grid_sample)."""
+    H = sampling_locations.shape[2]
+    mem, W = _np(memory), _np(value_weight)
+    value = project(mem, W, value_bias)
+    mask = None if value_padding_mask is None else _mask(value_padding_mask)
+    if mask is not None:
+        value = np.where(mask[..., None], 0.0, value)
+    grad_value, grad_loc, grad_attn = sample_backward(value, H, spatial_shapes, level_start_index,
+                                                      sampling_locations, attention_weights, grad_out)
+    if mask is not None:
+        grad_value = np.where(mask[..., None], 0.0, grad_value)
+    B, N, HD = grad_value.shape
+    gv = grad_value.reshape(B * N, HD)
+    return {'memory': grad_value @ W, 'value_weight': gv.T @ mem.reshape(B * N, -1),
+            'value_bias': None if value_bias is None else gv.sum(0),
+            'sampling_locations': grad_loc, 'attention_weights': grad_attn}
+
+
 def fused_order(memory, value_weight, value_bias, spatial_shapes, level_start_index,
                 sampling_locations, attention_weights, value_padding_mask=None):
     """The same result in the fused order (upstream csrc/ma_deform_fused.cu:6-14):
