@@ -15,6 +15,11 @@ weights -> attention -> output_proj), beside the same layer with the producer in
 nn.Linear, softmax, location arithmetic; then this library's ma_deform_attn) and the all-torch layer on the GPU
 (deform_attn_layer_reference: grid_sample), on the same rotating inputs.
 
+--backward times training steps instead: forward + backward of ma_deform_attn (gradients of memory, value_weight,
+value_bias, sampling_locations and attention_weights), beside the same through the torch reference (nn.Linear +
+grid_sample, autograd) on the GPU, both captured in CUDA graphs on rotating inputs; plus the backward kernel alone
+with its roofline.
+
 --impl reference times the CPU implementation of the same call: upstream's algorithm (nn.Linear + grid_sample, the
 oracle's torch_port on torch's CPU operators) with all host threads, on rank 0 only.
 """
@@ -445,6 +450,80 @@ def run_layer(args):
     print(json.dumps(line), flush=True)
 
 
+def run_backward(args):
+    """Forward + backward per step (see the module docstring); prints one JSON line."""
+    torch.cuda.set_device(0)
+    dev = torch.device('cuda', 0)
+    _native.load()
+    cfg = workloads.CONFIGS[args.config]
+    B, Q, C, H, D, P = cfg['B'], cfg['Q'], cfg['C'], cfg['H'], cfg['D'], cfg['P']
+    L = len(cfg['levels'])
+    base, pool = input_pool(args.config, B, dev, 2 * L2_BYTES)
+    shapes, starts = base[3], base[4]
+    shapes_host, starts_host = shapes.cpu(), starts.cpu()
+    W = base[1].detach().clone().requires_grad_(True)
+    bias = base[2].detach().clone().requires_grad_(True)
+    sets = [tuple(t.detach().clone().requires_grad_(True) for t in s) for s in pool]
+    g = torch.Generator(device=dev).manual_seed(5)
+    gouts = [torch.randn(B, Q, H * D, generator=g, device=dev).to(W.dtype) for _ in range(4)]
+    N = base[0].shape[1]
+    e = base[0].element_size()
+    mode = args.mode if args.mode != 'auto' else choose_mode(base[0], base[1], base[5])
+
+    def step(fn, i, **kw):
+        mem, loc, attn = sets[i % len(sets)]
+        out = fn(mem, W, bias, kw.get('shapes', shapes), kw.get('starts', starts), loc, attn, **kw.get('extra', {}))
+        return torch.autograd.grad(out, (mem, W, bias, loc, attn), gouts[i % len(gouts)])
+
+    times = {}
+    gr, launches = graph_time_us(lambda i: step(ma_deform_attn, i, extra={'mode': args.mode}), args.steps,
+                                 args.warmup)
+    torch.cuda.synchronize()
+    with ClockSampler(0) as clocks:
+        time.sleep(0.25)
+        times['ours'] = time_graph(gr, args.steps, reps=max(1, args.reps))
+    del gr
+    gr, _ = graph_time_us(lambda i: step(ma_deform_attn_reference, i, shapes=shapes_host, starts=starts_host),
+                          args.steps, args.warmup)
+    times['torch'] = time_graph(gr, args.steps, reps=max(1, args.reps))
+    del gr
+    with torch.no_grad():
+        plain = [tuple(t.detach() for t in s_) for s_ in sets]
+        gf, _ = graph_time_us(lambda i: ma_deform_attn(plain[i % len(plain)][0], base[1], base[2], shapes, starts,
+                                                       *plain[i % len(plain)][1:], mode=args.mode),
+                              args.steps, args.warmup)
+        times['forward_only'] = time_graph(gf, args.steps, reps=max(1, args.reps))
+        del gf
+        # the backward kernel alone, on the values of the rotating sets in the layout the backward uses
+        vals = [torch.nn.functional.linear(p_[0], base[1], base[2]) for p_ in plain]
+        gk, _ = graph_time_us(lambda i: _native.sample_backward(vals[i % len(vals)], shapes, starts,
+                                                                *plain[i % len(plain)][1:], gouts[i % len(gouts)],
+                                                                heads=H),
+                              args.steps, args.warmup)
+        t_kernel = time_graph(gk, args.steps, reps=max(1, args.reps))
+        del gk, vals
+    # algorithmic bytes of one backward-kernel launch: value, locations, weights and grad_out read, grad_value
+    # (float32, zeroed then accumulated: written once and read once by the atomics), the small gradients written
+    S = B * Q * H * L * P
+    alg = e * (B * N * H * D + 3 * S + B * Q * H * D) + 4 * (2 * B * N * H * D) + e * 3 * S
+    hbm, peak_kind = peaks()
+    achieved = alg / (t_kernel * 1e-6) / 1e9
+    line = {
+        'metric': 'µs per forward + backward of ma_deform_attn (device-timed)', 'value': round(times['ours'], 3),
+        'unit': 'us', 'n_gpus': 1, 'steps': args.steps, 'warmup': args.warmup, 'higher_is_better': False,
+        'dtype': str(cfg['dtype']).replace('torch.', ''), 'data': 'synthetic (seeded, BASELINE config shapes)',
+        'config': dict(config_dict(args.config, 1, mode), grads=['memory', 'value_weight', 'value_bias',
+                                                                 'sampling_locations', 'attention_weights']),
+        'torch_reference_us': round(times['torch'], 3), 'forward_only_us': round(times['forward_only'], 3),
+        'backward_kernel_us': round(t_kernel, 3),
+        'roofline': {'bound': 'hbm', 'kernel': 'sample_backward', 'achieved': round(achieved, 1), 'peak': hbm,
+                     'unit': 'GB/s', 'frac': round(achieved / hbm, 4), 'peak_source': peak_kind,
+                     'algorithmic_bytes': alg},
+        'gpu_launches': launches, 'clocks': clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_sweep(args):
     """Fused vs project over upstream's sweep grid (bench/results/rtx4090.md) and the c5 grid; prints a table."""
     torch.cuda.set_device(0)
@@ -493,6 +572,7 @@ def main():
                     help='fraction of tokens padded by a random value padding mask (0: no mask)')
     ap.add_argument('--sweep', action='store_true')
     ap.add_argument('--layer', action='store_true', help='time the whole deformable attention layer')
+    ap.add_argument('--backward', action='store_true', help='time forward + backward (training)')
     ap.add_argument('--ref-dim', type=int, default=4, choices=(2, 4),
                     help='--layer: reference points (2) or reference boxes (4)')
     ap.add_argument('--dtype', nargs='+', default=['float16', 'bfloat16', 'float32'])
@@ -505,6 +585,8 @@ def main():
         run_sweep(args)
     elif args.layer:
         run_layer(args)
+    elif args.backward:
+        run_backward(args)
     else:
         run_ours(args)
 

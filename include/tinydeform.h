@@ -109,6 +109,26 @@ TD_API int td_sampling_producer(int dtype, const void* proj, const void* referen
                                 size_t err_len);
 
 /*
+ * Backward of the sampling half (upstream's CUDA operator is inference only; this is the derivative of its
+ * reference, reference.py:29-40, as autograd computes it through grid_sample): given grad_out [B, Q, H * D] for
+ * out = sample(value, sampling_locations, attention_weights), writes
+ *   grad_value [B, N, H * D] -- float32, float64 for TD_F64 -- zeroed here, then accumulated with atomics (the sum
+ *                                order, and so the last bits, vary from run to run),
+ *   grad_sampling_locations [B, Q, H, L, P, 2] and grad_attention_weights [B, Q, H, L, P] in dtype.
+ * value is addressed through element strides as in td_sample_strided (the head-major [B, H, N, D] layout the
+ * projection writes: s_img = H * N * D, s_tok = D, s_head = N * D); value_padding_mask [B, N] or NULL (a padded
+ * token's value counts as zero and receives no gradient). The gradients of memory, value_weight and value_bias
+ * follow from grad_value by two plain GEMMs and a column sum (the caller's).
+ */
+TD_API int td_sample_backward(int dtype, const void* value, int64_t s_img, int64_t s_tok, int64_t s_head,
+                              const int64_t* spatial_shapes, const int64_t* level_start_index,
+                              const void* sampling_locations, const void* attention_weights,
+                              const uint8_t* value_padding_mask, const void* grad_out, void* grad_value,
+                              void* grad_sampling_locations, void* grad_attention_weights, int64_t B, int64_t Q,
+                              int64_t N, int64_t H, int64_t D, int64_t L, int64_t P, void* stream, char* err,
+                              size_t err_len);
+
+/*
  * One multi-scale deformable attention layer of a DETR-style decoder (Deformable-DETR's MSDeformAttn forward, the
  * caller of upstream's operator), in one call:
  *   proj = query [B, Q, Cq] @ sampling_weight^T + sampling_bias       sampling_weight = [W_offsets; W_attention],

@@ -21,7 +21,8 @@ Around the operator (additions; upstream has only the operator):
 the whole MSDeformAttn layer (query -> offsets and softmaxed weights -> attention -> output_proj) in one library call.
 
 CPU tensors run ``ma_deform_attn_reference`` (as upstream does). CUDA tensors run only the native library; if it is
-missing, the call raises. Inference only: inputs that require grad are rejected.
+missing, the call raises. Unlike upstream (inference only), CUDA inputs that require grad are differentiated: the
+forward runs the same kernels and the backward runs this library's backward kernel (``autograd.py``).
 """
 
 import functools
@@ -29,6 +30,7 @@ import functools
 import torch
 
 from . import _native
+from .autograd import ma_deform_attn_train
 from .reference import deform_attn_layer_reference, ma_deform_attn_reference, sampling_producer_reference
 
 __all__ = ['ma_deform_attn', 'ma_deform_attn_reference', 'choose_mode', 'deform_attn_layer', 'sampling_producer',
@@ -100,24 +102,25 @@ def ma_deform_attn(memory, value_weight, value_bias, spatial_shapes, level_start
                                        sampling_locations, attention_weights, value_padding_mask)
         return out if output_weight is None else torch.nn.functional.linear(out, output_weight, output_bias)
     _native.load()  # raises RuntimeError when the native library is missing: there is no fallback
-    if torch.is_grad_enabled() and any(
-            t is not None and t.requires_grad
-            for t in (memory, value_weight, value_bias, sampling_locations, attention_weights, output_weight,
-                      output_bias)):
-        raise RuntimeError('ma_deform_attn is inference only: run it under torch.no_grad() / '
-                           'torch.inference_mode(), or use ma_deform_attn_reference for training')
     if mode == 'auto':
         mode = choose_mode(memory, value_weight, sampling_locations)
+    if _wants_grad(memory, value_weight, value_bias, sampling_locations, attention_weights, output_weight,
+                   output_bias):
+        # training: the same forward kernels behind an autograd Function whose backward runs td_sample_backward;
+        # output_proj through torch's nn.Linear (cuBLAS), differentiable as it is
+        _native.check_geometry(memory, spatial_shapes, level_start_index, sampling_locations, attention_weights)
+        _native.check_projection(memory, value_weight, value_bias, sampling_locations.shape[2])
+        out = ma_deform_attn_train(memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                                   sampling_locations, attention_weights, mode, value_padding_mask)
+        return out if output_weight is None else torch.nn.functional.linear(out, output_weight, output_bias)
     run = _native.fused_forward if mode == 'fused' else _native.project_forward
     out = run(memory, value_weight, value_bias, spatial_shapes, level_start_index, sampling_locations,
               attention_weights, value_padding_mask)
     return out if output_weight is None else _native.linear(out, output_weight, output_bias)
 
 
-def _check_inference(*ts):
-    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in ts):
-        raise RuntimeError('the CUDA kernels are inference only: run them under torch.no_grad() / '
-                           'torch.inference_mode(), or use the *_reference functions for training')
+def _wants_grad(*ts):
+    return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in ts)
 
 
 def pack_sampling_weights(offset_weight, offset_bias, attention_weight, attention_bias):
@@ -141,7 +144,10 @@ def sampling_producer(query, reference_points, spatial_shapes, n_heads, n_points
         return sampling_producer_reference(query, reference_points, spatial_shapes, n_heads, n_points,
                                            sampling_weight, sampling_bias)
     _native.load()
-    _check_inference(query, reference_points, sampling_weight, sampling_bias)
+    if _wants_grad(query, reference_points, sampling_weight, sampling_bias):
+        # training: torch's operators (two GEMMs, softmax, arithmetic), differentiable as they are
+        return sampling_producer_reference(query, reference_points, spatial_shapes, n_heads, n_points,
+                                           sampling_weight, sampling_bias)
     L = spatial_shapes.shape[0]
     if sampling_weight.dim() != 2 or sampling_weight.shape[0] != 3 * n_heads * L * n_points:
         raise RuntimeError('sampling_weight must be [3 * H * L * P, Cq]: the offset rows, then the attention rows')
@@ -173,10 +179,16 @@ def deform_attn_layer(query, reference_points, memory, spatial_shapes, level_sta
                                            n_heads, n_points, sampling_weight, sampling_bias, value_weight,
                                            value_bias, output_weight, output_bias, value_padding_mask)
     _native.load()
-    _check_inference(query, reference_points, memory, sampling_weight, sampling_bias, value_weight, value_bias,
-                     output_weight, output_bias)
     if mode == 'auto':
         mode = _pick(memory, value_weight, query.shape[1], n_heads, spatial_shapes.shape[0], n_points)
+    if _wants_grad(query, reference_points, memory, sampling_weight, sampling_bias, value_weight, value_bias,
+                   output_weight, output_bias):
+        # training: the producer in torch's operators, the attention through the differentiable CUDA operator
+        loc, attn = sampling_producer_reference(query, reference_points, spatial_shapes, n_heads, n_points,
+                                                sampling_weight, sampling_bias)
+        return ma_deform_attn(memory, value_weight, value_bias, spatial_shapes, level_start_index, loc, attn,
+                              mode=mode, value_padding_mask=value_padding_mask, output_weight=output_weight,
+                              output_bias=output_bias)
     return _native.layer_forward(query, reference_points, memory, spatial_shapes, level_start_index, n_heads,
                                  n_points, sampling_weight, sampling_bias, value_weight, value_bias, output_weight,
                                  output_bias, value_padding_mask, order=mode)

@@ -37,6 +37,8 @@ SIGNATURES = {
     'td_linear': (_ip, [_ip, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _cp, _sz]),
     'td_sampling_producer': (_ip, [_ip, _vp, _vp, ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp,
                                    _cp, _sz]),
+    'td_sample_backward': (_ip, [_ip, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                 _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _cp, _sz]),
     'td_layer_workspace_bytes': (_sz, [_ip, _ip, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _ip]),
     'td_layer_forward': (_ip, [_ip, _ip, _vp, _i64, _vp, _ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64,
                                _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp, _cp, _sz]),
@@ -382,6 +384,46 @@ def sample_forward(value, heads, spatial_shapes, level_start_index, sampling_loc
         _call(lib.td_sample_forward, DTYPE_CODE[value.dtype], _ptr(v), heads, _ptr(shp), _ptr(st), _ptr(loc),
               _ptr(att), _ptr(out), B, Q, N, HD, H, L, P, _stream(value.device))
     return out
+
+
+def sample_backward(value, spatial_shapes, level_start_index, sampling_locations, attention_weights,
+                    grad_out, value_padding_mask=None, heads=None):
+    """Gradients of the sampling half through td_sample_backward, for value in the nn.Linear layout [B, N, H * D]
+    (heads given) or head-major [B, H, N, D] (heads=None), and grad_out [B, Q, H * D]: (grad_value [B, N, H * D]
+    in float32 -- float64 for float64 --, grad_sampling_locations, grad_attention_weights in the input dtype)."""
+    lib = load()
+    if heads is None:
+        B, H, N, D = value.shape
+        strides = (H * N * D, D, N * D)
+    else:
+        B, N, HD = value.shape
+        H = heads
+        if HD % H != 0:
+            raise RuntimeError('value must be [B, N, H * D]')
+        D = HD // H
+        strides = (N * HD, HD, D)
+    check_geometry(value.reshape(B, -1, D), spatial_shapes, level_start_index, sampling_locations,
+                   attention_weights)
+    Q = sampling_locations.size(1)
+    L, P = sampling_locations.shape[3:5]
+    if grad_out.shape != (B, Q, H * D) or grad_out.dtype != value.dtype or grad_out.device != value.device:
+        raise RuntimeError('grad_out must be [B, Q, H * D] with the dtype and device of value')
+    mask = value_padding_mask
+    if mask is not None:
+        if mask.dtype not in (torch.bool, torch.uint8) or mask.shape != (B, N) or mask.device != value.device:
+            raise RuntimeError('value_padding_mask must be a bool (or uint8) [B, N] tensor on the device of value')
+        mask = mask.contiguous()
+    v, shp, st, loc, att, g = _dense(value, spatial_shapes, level_start_index, sampling_locations,
+                                     attention_weights, grad_out)
+    acc = torch.float64 if value.dtype == torch.float64 else torch.float32
+    grad_value = torch.empty((B, N, H * D), dtype=acc, device=v.device)
+    grad_loc = torch.empty_like(loc)
+    grad_attn = torch.empty_like(att)
+    with torch.cuda.device(v.device):
+        _call(lib.td_sample_backward, DTYPE_CODE[v.dtype], _ptr(v), *strides, _ptr(shp), _ptr(st),
+              _ptr(loc), _ptr(att), _ptr(mask), _ptr(g), _ptr(grad_value), _ptr(grad_loc), _ptr(grad_attn),
+              B, Q, N, H, D, L, P, _stream(v.device))
+    return grad_value, grad_loc, grad_attn
 
 
 def sample_head_major(value_hm, spatial_shapes, level_start_index, sampling_locations, attention_weights):

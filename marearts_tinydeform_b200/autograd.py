@@ -1,0 +1,69 @@
+"""Training support: ma_deform_attn on CUDA tensors that require grad.
+
+Upstream's CUDA operator is inference only (marearts_tinydeform/__init__.py:67-71 rejects inputs that require
+grad); this build differentiates it. Forward: the same B200 kernels as inference, in the order `mode` picks,
+saving only the inputs. Backward (activation recompute): the value projection is run again (nn.Linear layout,
+by torch's GEMM: the backward runs on autograd's worker thread, also under CUDA-graph capture, where a library
+GEMM needs no tensor-map set-up), then td_sample_backward gives grad_value (float32 accumulation),
+grad_sampling_locations and grad_attention_weights in one pass, and the three parameter gradients follow by plain
+GEMMs and a column sum:
+
+    grad_memory       = grad_value @ value_weight
+    grad_value_weight = grad_value^T @ memory          (summed over every token of every image)
+    grad_value_bias   = sum of grad_value over tokens
+
+These two GEMMs are library GEMMs (torch.matmul, cuBLAS) in the inputs' dtype -- grad_value is rounded once from
+its float32 accumulator, as autograd's own half-precision backward keeps its gradients in half precision, and the
+tensor cores then run them -- except for float32 / float64 inputs, which keep float32 / float64; the bias gradient
+is summed from the float32 accumulator. The value padding mask blocks the gradient of padded tokens exactly as
+masked_fill does in the reference.
+"""
+
+import torch
+
+from . import _native
+
+
+class MaDeformAttnFunction(torch.autograd.Function):
+    """out = ma_deform_attn(memory, value_weight, value_bias, spatial_shapes, level_start_index,
+    sampling_locations, attention_weights) on CUDA, differentiable in the five float inputs."""
+
+    @staticmethod
+    def forward(ctx, memory, value_weight, value_bias, spatial_shapes, level_start_index, sampling_locations,
+                attention_weights, mode, value_padding_mask):
+        run = _native.fused_forward if mode == 'fused' else _native.project_forward
+        out = run(memory, value_weight, value_bias, spatial_shapes, level_start_index, sampling_locations,
+                  attention_weights, value_padding_mask)
+        ctx.save_for_backward(memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                              sampling_locations, attention_weights, value_padding_mask)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        memory, weight, bias, shapes, starts, loc, attn, mask = ctx.saved_tensors
+        need = ctx.needs_input_grad
+        H = loc.shape[2]
+        B, N, C = memory.shape
+        HD = weight.shape[0]
+        value = torch.nn.functional.linear(memory, weight, bias)  # [B, N, H * D]
+        grad_value, grad_loc, grad_attn = _native.sample_backward(
+            value, shapes, starts, loc, attn, grad_out.to(memory.dtype).contiguous(), mask, heads=H)
+        acc = grad_value.view(B * N, HD)
+        gv = acc.to(memory.dtype) if memory.dtype in (torch.float16, torch.bfloat16) else acc
+        grad_memory = grad_weight = grad_bias = None
+        if need[0]:
+            grad_memory = (gv @ weight.to(gv.dtype)).view(B, N, C).to(memory.dtype)
+        if need[1]:
+            grad_weight = (gv.t() @ memory.reshape(B * N, C).to(gv.dtype)).to(weight.dtype)
+        if bias is not None and need[2]:
+            grad_bias = acc.sum(0).to(bias.dtype)
+        return (grad_memory, grad_weight, grad_bias, None, None, grad_loc if need[5] else None,
+                grad_attn if need[6] else None, None, None)
+
+
+def ma_deform_attn_train(memory, value_weight, value_bias, spatial_shapes, level_start_index, sampling_locations,
+                         attention_weights, mode, value_padding_mask=None):
+    """The differentiable CUDA call (mode 'fused' or 'project' for the forward)."""
+    mask = _native.check_mask(value_padding_mask, memory)
+    return MaDeformAttnFunction.apply(memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                                      sampling_locations, attention_weights, mode, mask)

@@ -20,6 +20,7 @@
 #include "td_gemm_simt.cuh"
 #include "td_gemm_tc.cuh"
 #include "td_producer.cuh"
+#include "td_backward.cuh"
 #include "td_sampler.cuh"
 
 namespace td {
@@ -578,6 +579,42 @@ int launch_producer(const T* proj, const T* ref, int ref_dim, const int64_t* sha
     return check_launch(err, err_len, "sampling_producer_kernel");
 }
 
+// Backward of the sampling half (td_backward.cuh): zeroes grad_value, then one warp per (b, q, h) row.
+template <typename T>
+int launch_sample_backward(const T* value, long long s_img, long long s_tok, long long s_head, const int64_t* shapes,
+                           const int64_t* starts, const T* loc, const T* attn, const uint8_t* mask, const T* grad_out,
+                           typename Coord<T>::type* grad_value, T* grad_loc, T* grad_attn, int64_t B, int64_t Q,
+                           int64_t N, int64_t H, int64_t D, int64_t L, int64_t P, cudaStream_t stream, char* err,
+                           size_t err_len) {
+    using CT = typename Coord<T>::type;
+    cudaError_t e = cudaMemsetAsync(grad_value, 0, size_t(B) * size_t(N) * size_t(H * D) * sizeof(CT), stream);
+    if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    if (B * Q == 0) return TD_OK;
+    BackArgs<T> a;
+    a.value = value; a.s_img = s_img; a.s_tok = s_tok; a.s_head = s_head; a.loc = loc; a.attn = attn;
+    a.grad_out = grad_out; a.grad_value = grad_value; a.grad_loc = grad_loc; a.grad_attn = grad_attn;
+    a.shapes = shapes; a.starts = starts; a.mask = mask; a.rows = B * Q * H; a.n_tok = N;
+    a.Q = int(Q); a.H = int(H); a.D = int(D); a.L = int(L); a.P = int(P);
+    const long long row_bytes = D * (long long)sizeof(T);
+    a.G = int(row_bytes / 16);
+    const bool vec = row_bytes % 16 == 0 && row_bytes <= 512 && (a.G & (a.G - 1)) == 0 && aligned16(value) &&
+                     aligned16(grad_out) && aligned16(grad_value) && (D * (long long)sizeof(CT)) % 16 == 0 &&
+                     (s_img * (long long)sizeof(T)) % 16 == 0 && (s_tok * (long long)sizeof(T)) % 16 == 0 &&
+                     (s_head * (long long)sizeof(T)) % 16 == 0;
+    const unsigned grid = unsigned((a.rows + kBackWarps - 1) / kBackWarps);
+    const size_t smem = backward_smem<T>(int(L), int(P));  // up to 56 KB (float64, L * P = 64)
+    static std::atomic<uint64_t> smem_vec{0}, smem_generic{0};
+    if (int rc = vec ? allow_smem(sample_backward_vec_kernel<T>, smem, smem_vec, err, err_len)
+                     : allow_smem(sample_backward_generic_kernel<T>, smem, smem_generic, err, err_len))
+        return rc;
+    e = vec ? launch_kernel(sample_backward_vec_kernel<T>, dim3(grid), dim3(kBackWarps * 32), smem, stream, false, a)
+            : launch_kernel(sample_backward_generic_kernel<T>, dim3(grid), dim3(kBackWarps * 32), smem, stream, false,
+                            a);
+    if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "backward launch: %s", cudaGetErrorString(e));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return check_launch(err, err_len, vec ? "sample_backward_vec_kernel" : "sample_backward_generic_kernel");
+}
+
 // Byte offsets of the decoder layer's intermediates in its workspace (each region 256-byte aligned, from the first
 // 256-byte boundary of the workspace): the query projection, the projected value (project order), locations and
 // weights (fused order), and the attention result when an output projection follows.
@@ -727,6 +764,35 @@ int td_sampling_producer(int dtype, const void* proj, const void* reference_poin
         return launch_producer<T>(static_cast<const T*>(proj), static_cast<const T*>(reference_points), ref_dim,
                                   spatial_shapes, static_cast<T*>(sampling_locations),
                                   static_cast<T*>(attention_weights), B, Q, H, L, P, s, err, err_len);
+    });
+}
+
+int td_sample_backward(int dtype, const void* value, int64_t s_img, int64_t s_tok, int64_t s_head,
+                       const int64_t* spatial_shapes, const int64_t* level_start_index,
+                       const void* sampling_locations, const void* attention_weights,
+                       const uint8_t* value_padding_mask, const void* grad_out, void* grad_value,
+                       void* grad_sampling_locations, void* grad_attention_weights, int64_t B, int64_t Q, int64_t N,
+                       int64_t H, int64_t D, int64_t L, int64_t P, void* stream, char* err, size_t err_len) {
+    if (dtype_size(dtype) == 0) return fail(err, err_len, TD_ERR_ARG, "unsupported dtype code %d", dtype);
+    if (int rc = check_geometry(B, Q, N, H, L, P, err, err_len)) return rc;
+    if (D <= 0 || s_img < 0 || s_tok < 0 || s_head < 0)
+        return fail(err, err_len, TD_ERR_ARG, "head size must be positive and strides non-negative");
+    if (!grad_value || (B * Q > 0 && (!value || !sampling_locations || !attention_weights || !grad_out ||
+                                      !grad_sampling_locations || !grad_attention_weights ||
+                                      (L * P > 0 && (!spatial_shapes || !level_start_index)))))
+        return fail(err, err_len, TD_ERR_ARG, "null tensor pointer");
+    if (B * N == 0 && B * Q == 0) return TD_OK;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return dispatch(dtype, [&](auto tag) {
+        using T = decltype(tag);
+        using CT = typename Coord<T>::type;
+        return launch_sample_backward<T>(static_cast<const T*>(value), s_img, s_tok, s_head, spatial_shapes,
+                                         level_start_index, static_cast<const T*>(sampling_locations),
+                                         static_cast<const T*>(attention_weights), value_padding_mask,
+                                         static_cast<const T*>(grad_out), static_cast<CT*>(grad_value),
+                                         static_cast<T*>(grad_sampling_locations),
+                                         static_cast<T*>(grad_attention_weights), B, Q, N, H, D, L, P, s, err,
+                                         err_len);
     });
 }
 

@@ -4,7 +4,7 @@ This is the public ``ma_deform_attn_reference`` of the drop-in API (upstream
 ``marearts_tinydeform/reference.py:13-40``). It defines what ``ma_deform_attn`` returns: ``nn.Linear`` on every
 memory token, then ``F.grid_sample`` with bilinear interpolation, zero padding and ``align_corners=False`` on each
 level, then the attention-weighted sum over levels x points. It runs on CPU and GPU in any float dtype and supports
-autograd, so it is also the training path (the CUDA path is inference only).
+autograd (the CUDA path has its own backward kernel).
 
 CPU tensors passed to ``ma_deform_attn`` come here, exactly as upstream ``marearts_tinydeform/__init__.py:62-64``
 routes them. CUDA tensors never do: the CUDA path raises when its native library is missing.

@@ -234,9 +234,6 @@ def test_rejects_bad_input(cuda):
             with pytest.raises(RuntimeError):
                 with torch.inference_mode():
                     ma_deform_attn(*a, mode=mode)
-    grad = [t.clone().requires_grad_(True) if i == 0 else t for i, t in enumerate(args)]
-    with pytest.raises(RuntimeError):
-        ma_deform_attn(*grad)
     with pytest.raises(ValueError):
         ma_deform_attn(*args, mode='nope')
 

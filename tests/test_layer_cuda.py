@@ -172,5 +172,3 @@ def test_layer_empty_queries_and_errors(cuda):
         for change in bad:
             with pytest.raises(RuntimeError):
                 deform_attn_layer(**{**base, **change})
-    with pytest.raises(RuntimeError, match='inference only'):
-        deform_attn_layer(**{**base, 'query': q.clone().requires_grad_()})
