@@ -10,13 +10,11 @@
 // which is what autograd computes through upstream's reference (reference.py:29-40: grid_sample with
 // align_corners=False, zero padding). Upstream's CUDA operator has no backward.
 //
-// Layout as the forward sampler: one warp per (b, q, h) row; the row's corners are computed once into shared memory
-// (lanes over the L * P points, each lane keeping its points' fractions for the last step); the corner rows are
-// then read as 16-byte vectors by G lanes each (G = D * sizeof(T) / 16), every lane holding the matching slice of g:
-// each corner row gives a dot product (summed over its G lanes by xor shuffles) and a scatter of a * w_c * g into
-// grad_value (float32 -- float64 for float64 inputs -- [B, N, H * D], vector atomics of 16 bytes); last, lanes over
-// the points turn the row's dot products into the two small gradients. The generic kernel (any D or alignment)
-// keeps lanes over D and reduces every dot product over the warp.
+// Unlike the forward, nothing here sums over a row's points: every point's gradients depend on its own four corners
+// only. The vector kernel therefore gives each point a group of G lanes (G = D * sizeof(T) / 16, one 16-byte slice
+// of a D-row each); the scatter into grad_value (float32 -- float64 for float64 inputs -- [B, N, H * D]) uses
+// 16-byte vector atomics. The generic kernel (any D or alignment) keeps one warp per (b, q, h) row with lanes over
+// D, the row's corners in shared memory, and one warp-wide sum per corner row.
 #pragma once
 
 #include "td_common.cuh"
@@ -104,79 +102,77 @@ __device__ __forceinline__ void scatter_add(double* p, const double* v, int n) {
 }
 
 // Vector kernel: D * sizeof(T) % 16 == 0, <= 512 bytes, G a power of two; value, grad_out 16-byte aligned with
-// 16-byte strides; grad_value rows 16-byte aligned.
+// 16-byte strides; grad_value rows 16-byte aligned. The gradients of different points are independent, so here a
+// group of G lanes owns one point from start to end, with no shared memory: each lane of the group loads the
+// point's location and weight (one broadcast transaction per group) and its 16-byte slice of grad_out, computes the
+// four corners, loads its slice of the four corner rows at once, and the group sums the four dot products by xor
+// shuffles; every lane scatters its slice of a * w_c * g, and the group's first lane writes the two small
+// gradients. A warp covers 32 / G consecutive points: two memory round trips per point, and many warps in flight.
 template <typename T>
 __global__ void __launch_bounds__(kBackWarps * 32) sample_backward_vec_kernel(const BackArgs<T> a) {
     using A = typename Elem<T>::acc;
     using CT = typename Coord<T>::type;
     constexpr int V = Elem<T>::kVec;
-    constexpr int kBatch = 4;  // corner rows in flight per lane
-    extern __shared__ __align__(16) unsigned char smem_raw[];
     grid_dependency_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long row = (long long)blockIdx.x * kBackWarps + warp;
-    if (row >= a.rows) return;  // warp-uniform
-    const int LP = a.L * a.P, S = 4 * LP;
-    int* s_tok = reinterpret_cast<int*>(smem_raw) + warp * S;
-    CT* s_wt = reinterpret_cast<CT*>(smem_raw + kBackWarps * S * sizeof(int)) + warp * S;
-    CT* s_coef = s_wt + kBackWarps * S;
-    CT* s_dot = s_coef + kBackWarps * S;
+    const int G = a.G, CG = 32 / G, cg = lane / G, v = lane - cg * G;
+    const int LP = a.L * a.P;
+    const long long pt = ((long long)blockIdx.x * kBackWarps + warp) * CG + cg;  // point: row * LP + j
+    const bool live = pt < a.rows * LP;
+    const long long row = live ? pt / LP : 0;
+    const int j = int(pt - row * LP);
     const long long b = row / ((long long)a.Q * a.H);
     const int h = int(row % a.H);
-    const uint8_t* mask_b = a.mask != nullptr ? a.mask + b * a.n_tok : nullptr;
-    CT att[2], fx[2], fy[2];
-    Level lv[2];
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-        const int j = lane + 32 * k;
-        if (j < LP) backward_point<T>(a, row, j, mask_b, s_tok, s_wt, s_coef, att[k], fx[k], fy[k], lv[k]);
-    }
-    __syncwarp();
-    const int G = a.G, CG = 32 / G, cg = lane / G, v = lane - cg * G;
+    // the point's geometry, location, weight and grad_out slice, all loads issued together
+    const Level lv = level_at(a.shapes, a.starts, live ? j / a.P : 0);
+    const long long i = row * LP + (live ? j : 0);
+    const CT lx = live ? CT(to_acc(a.loc[2 * i])) : CT(-1e4), ly = live ? CT(to_acc(a.loc[2 * i + 1])) : CT(-1e4);
+    const CT att = live ? CT(to_acc(a.attn[i])) : CT(0);
     A g[V];
-    unpack16<T>(*reinterpret_cast<const uint4*>(a.grad_out + row * a.D + v * V), g);
+    unpack16<T>(live ? *reinterpret_cast<const uint4*>(a.grad_out + row * a.D + v * V) : g_zero16, g);
+    const uint8_t* mask_b = a.mask != nullptr ? a.mask + b * a.n_tok : nullptr;
+    int tok[4];
+    CT wt[4];
+    corners4<CT>(lx, ly, CT(1), lv, a.n_tok, tok, wt, mask_b);  // a dead group's point lies outside every map
+    const CT x = cmin(cmax(lx * CT(lv.w) - CT(0.5), CT(-2)), CT(lv.w) + CT(1));
+    const CT y = cmin(cmax(ly * CT(lv.h) - CT(0.5), CT(-2)), CT(lv.h) + CT(1));
+    const CT fx = x - cfloor(x), fy = y - cfloor(y);
+    // the four corner rows' slices, then the four dot products summed over the group
     const T* vb = a.value + b * a.s_img + (long long)h * a.s_head + v * V;
+    uint4 raw[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        raw[c] = __ldg(tok[c] < 0 ? &g_zero16 : reinterpret_cast<const uint4*>(vb + (long long)tok[c] * a.s_tok));
+    CT d[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        A xs[V];
+        unpack16<T>(raw[c], xs);
+        A dp = A(0);
+#pragma unroll
+        for (int k = 0; k < V; ++k) dp = fma(g[k], xs[k], dp);
+        for (int o = G >> 1; o > 0; o >>= 1) dp += __shfl_xor_sync(0xffffffffu, dp, o);
+        d[c] = CT(dp);
+    }
+    // scatter a * w_c * g into the corner rows of grad_value
     CT* gb = a.grad_value + b * (a.n_tok * (long long)a.H * a.D) + (long long)h * a.D + v * V;
     const long long g_tok = (long long)a.H * a.D;
-    // every lane runs the same number of rounds (the dot products are summed across each group by shuffles)
-    for (int base = 0; base < S; base += kBatch * CG) {
-        uint4 raw[kBatch];
-        int tk[kBatch];
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-            const int s = base + cg + u * CG;
-            tk[u] = s < S ? s_tok[s] : -1;
-            const uint4* src =
-                tk[u] < 0 ? &g_zero16 : reinterpret_cast<const uint4*>(vb + (long long)tk[u] * a.s_tok);
-            raw[u] = __ldg(src);
-        }
+    for (int c = 0; c < 4; ++c) {
+        if (tok[c] < 0) continue;
+        const CT coef = att * wt[c];
+        CT add[V];
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-            const int s = base + cg + u * CG;
-            A x[V];
-            unpack16<T>(raw[u], x);
-            A dp = A(0);
-#pragma unroll
-            for (int i = 0; i < V; ++i) dp = fma(g[i], x[i], dp);
-            for (int o = G >> 1; o > 0; o >>= 1) dp += __shfl_xor_sync(0xffffffffu, dp, o);
-            if (s < S) {
-                if (v == 0) s_dot[s] = CT(dp);
-                if (tk[u] >= 0) {
-                    const CT coef = s_coef[s];
-                    CT add[V];
-#pragma unroll
-                    for (int i = 0; i < V; ++i) add[i] = coef * CT(g[i]);
-                    scatter_add(gb + (long long)tk[u] * g_tok, add, V);
-                }
-            }
-        }
+        for (int k = 0; k < V; ++k) add[k] = coef * CT(g[k]);
+        scatter_add(gb + (long long)tok[c] * g_tok, add, V);
     }
-    __syncwarp();
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-        const int j = lane + 32 * k;
-        if (j < LP) backward_finish<T>(a, row, j, s_wt, s_dot, att[k], fx[k], fy[k], lv[k]);
-    }
+    if (!live || v != 0) return;
+    const CT ga = wt[0] * d[0] + wt[1] * d[1] + wt[2] * d[2] + wt[3] * d[3];
+    const CT gfx = (CT(1) - fy) * (d[1] - d[0]) + fy * (d[3] - d[2]);
+    const CT gfy = (CT(1) - fx) * (d[2] - d[0]) + fx * (d[3] - d[1]);
+    a.grad_attn[i] = from_acc<T>(typename Elem<T>::acc(ga));
+    a.grad_loc[2 * i] = from_acc<T>(typename Elem<T>::acc(att * CT(lv.w) * gfx));
+    a.grad_loc[2 * i + 1] = from_acc<T>(typename Elem<T>::acc(att * CT(lv.h) * gfy));
 }
 
 // Generic kernel: lanes over D, scalar loads and atomics, one warp-wide sum per corner row.

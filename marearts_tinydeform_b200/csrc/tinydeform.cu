@@ -589,7 +589,7 @@ int launch_sample_backward(const T* value, long long s_img, long long s_tok, lon
     using CT = typename Coord<T>::type;
     cudaError_t e = cudaMemsetAsync(grad_value, 0, size_t(B) * size_t(N) * size_t(H * D) * sizeof(CT), stream);
     if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
-    if (B * Q == 0) return TD_OK;
+    if (B * Q * L * P == 0) return TD_OK;
     BackArgs<T> a;
     a.value = value; a.s_img = s_img; a.s_tok = s_tok; a.s_head = s_head; a.loc = loc; a.attn = attn;
     a.grad_out = grad_out; a.grad_value = grad_value; a.grad_loc = grad_loc; a.grad_attn = grad_attn;
@@ -601,15 +601,20 @@ int launch_sample_backward(const T* value, long long s_img, long long s_tok, lon
                      aligned16(grad_out) && aligned16(grad_value) && (D * (long long)sizeof(CT)) % 16 == 0 &&
                      (s_img * (long long)sizeof(T)) % 16 == 0 && (s_tok * (long long)sizeof(T)) % 16 == 0 &&
                      (s_head * (long long)sizeof(T)) % 16 == 0;
-    const unsigned grid = unsigned((a.rows + kBackWarps - 1) / kBackWarps);
-    const size_t smem = backward_smem<T>(int(L), int(P));  // up to 56 KB (float64, L * P = 64)
-    static std::atomic<uint64_t> smem_vec{0}, smem_generic{0};
-    if (int rc = vec ? allow_smem(sample_backward_vec_kernel<T>, smem, smem_vec, err, err_len)
-                     : allow_smem(sample_backward_generic_kernel<T>, smem, smem_generic, err, err_len))
-        return rc;
-    e = vec ? launch_kernel(sample_backward_vec_kernel<T>, dim3(grid), dim3(kBackWarps * 32), smem, stream, false, a)
-            : launch_kernel(sample_backward_generic_kernel<T>, dim3(grid), dim3(kBackWarps * 32), smem, stream, false,
-                            a);
+    if (vec) {
+        // 32 / G points per warp
+        const long long points = a.rows * L * P, per_cta = (long long)kBackWarps * (32 / a.G);
+        const long long grid = (points + per_cta - 1) / per_cta;
+        if (grid > INT32_MAX) return fail(err, err_len, TD_ERR_ARG, "too many sampling points for one launch");
+        e = launch_kernel(sample_backward_vec_kernel<T>, dim3(unsigned(grid)), dim3(kBackWarps * 32), 0, stream,
+                          false, a);
+    } else {
+        const size_t smem = backward_smem<T>(int(L), int(P));  // up to 56 KB (float64, L * P = 64)
+        static std::atomic<uint64_t> smem_generic{0};
+        if (int rc = allow_smem(sample_backward_generic_kernel<T>, smem, smem_generic, err, err_len)) return rc;
+        e = launch_kernel(sample_backward_generic_kernel<T>, dim3(unsigned((a.rows + kBackWarps - 1) / kBackWarps)),
+                          dim3(kBackWarps * 32), smem, stream, false, a);
+    }
     if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "backward launch: %s", cudaGetErrorString(e));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return check_launch(err, err_len, vec ? "sample_backward_vec_kernel" : "sample_backward_generic_kernel");
