@@ -109,6 +109,23 @@ TD_API int td_sampling_producer(int dtype, const void* proj, const void* referen
                                 size_t err_len);
 
 /*
+ * td_project_forward_masked followed by the decoder's output_proj in the same call: out [B, Q, C_out] =
+ * attention @ output_weight^T + output_bias, output_weight [C_out, HD] (nn.Linear), output_bias [C_out] or NULL;
+ * the output GEMM (the projection kernel, as td_linear) is queued right behind the sampler with programmatic
+ * dependent launch. output_weight NULL: exactly td_project_forward_masked. Workspace:
+ * td_project_ex_workspace_bytes(dtype, B, Q, N, HD, output_weight != NULL) bytes (the projected value, plus the
+ * attention result). No upstream counterpart (upstream's callers apply output_proj themselves, README.md:11).
+ */
+TD_API size_t td_project_ex_workspace_bytes(int dtype, int64_t B, int64_t Q, int64_t N, int64_t HD, int output_proj);
+TD_API int td_project_forward_ex(int dtype, const void* memory, const void* value_weight, const void* value_bias,
+                                 const int64_t* spatial_shapes, const int64_t* level_start_index,
+                                 const void* sampling_locations, const void* attention_weights,
+                                 const uint8_t* value_padding_mask, const void* output_weight,
+                                 const void* output_bias, int64_t C_out, void* out, int64_t B, int64_t Q, int64_t N,
+                                 int64_t C, int64_t H, int64_t HD, int64_t L, int64_t P, void* workspace,
+                                 size_t workspace_bytes, void* stream, char* err, size_t err_len);
+
+/*
  * Backward of the sampling half (upstream's CUDA operator is inference only; this is the derivative of its
  * reference, reference.py:29-40, as autograd computes it through grid_sample): given grad_out [B, Q, H * D] for
  * out = sample(value, sampling_locations, attention_weights), writes

@@ -91,7 +91,7 @@ def ma_deform_attn(memory, value_weight, value_bias, spatial_shapes, level_start
 
     output_weight / output_bias (an addition): the decoder's output_proj (an nn.Linear [C_out, H * D]) applied to the
     result, so the call returns [B, Q, C_out]; on CUDA it runs as a tensor-core GEMM queued right behind the
-    attention kernel, overlapping its start with it.
+    attention kernel (in the same library call in the project order), overlapping its start with it.
     """
     if mode not in MODES:
         raise ValueError(f'mode must be one of {MODES}, got {mode!r}')
@@ -113,9 +113,13 @@ def ma_deform_attn(memory, value_weight, value_bias, spatial_shapes, level_start
         out = ma_deform_attn_train(memory, value_weight, value_bias, spatial_shapes, level_start_index,
                                    sampling_locations, attention_weights, mode, value_padding_mask)
         return out if output_weight is None else torch.nn.functional.linear(out, output_weight, output_bias)
-    run = _native.fused_forward if mode == 'fused' else _native.project_forward
-    out = run(memory, value_weight, value_bias, spatial_shapes, level_start_index, sampling_locations,
-              attention_weights, value_padding_mask)
+    if mode == 'project':
+        # output_proj, if any, in the same library call
+        return _native.project_forward(memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                                       sampling_locations, attention_weights, value_padding_mask, output_weight,
+                                       output_bias)
+    out = _native.fused_forward(memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                                sampling_locations, attention_weights, value_padding_mask)
     return out if output_weight is None else _native.linear(out, output_weight, output_bias)
 
 

@@ -39,6 +39,9 @@ SIGNATURES = {
                                    _cp, _sz]),
     'td_sample_backward': (_ip, [_ip, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                  _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _cp, _sz]),
+    'td_project_ex_workspace_bytes': (_sz, [_ip, _i64, _i64, _i64, _i64, _ip]),
+    'td_project_forward_ex': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp,
+                                    _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp, _cp, _sz]),
     'td_layer_workspace_bytes': (_sz, [_ip, _ip, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _ip]),
     'td_layer_forward': (_ip, [_ip, _ip, _vp, _i64, _vp, _ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64,
                                _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp, _cp, _sz]),
@@ -204,21 +207,52 @@ def fused_forward(memory, value_weight, value_bias, spatial_shapes, level_start_
     return out
 
 
+def check_output_proj(output_weight, output_bias, HD, ref):
+    """output_weight [C_out, HD] / output_bias [C_out] or None on ref's device and dtype; returns C_out (0: none)."""
+    if output_weight is None:
+        if output_bias is not None:
+            raise RuntimeError('output_bias needs output_weight')
+        return 0
+    if output_weight.dim() != 2 or output_weight.size(1) != HD:
+        raise RuntimeError('output_weight must be [C_out, H * D]')
+    C_out = output_weight.size(0)
+    if output_bias is not None and output_bias.shape != (C_out,):
+        raise RuntimeError('output_bias must be [C_out] like output_weight')
+    for t in (output_weight, output_bias):
+        if t is not None and (t.device != ref.device or t.dtype != ref.dtype):
+            raise RuntimeError('output_weight / output_bias must have the device and dtype of memory')
+    return C_out
+
+
 def project_forward(memory, value_weight, value_bias, spatial_shapes, level_start_index,
-                    sampling_locations, attention_weights, value_padding_mask=None):
+                    sampling_locations, attention_weights, value_padding_mask=None, output_weight=None,
+                    output_bias=None):
     """Project order (upstream __init__.py:77-79: F.linear + _C.sample_forward) through td_project_forward (with a
-    value padding mask: td_project_forward_masked)."""
+    value padding mask: td_project_forward_masked; with output_proj: td_project_forward_ex)."""
     lib = load()
     B, Q, H, L, P = check_geometry(memory, spatial_shapes, level_start_index, sampling_locations, attention_weights)
     HD = check_projection(memory, value_weight, value_bias, H)
     mask = check_mask(value_padding_mask, memory)
+    C_out = check_output_proj(output_weight, output_bias, HD, memory)
     N, C = memory.size(1), memory.size(2)
     mem, w, b, shp, st, loc, att = _dense(memory, value_weight, value_bias, spatial_shapes, level_start_index,
                                           sampling_locations, attention_weights)
+    code = DTYPE_CODE[memory.dtype]
+    if C_out:
+        out = torch.empty((B, Q, C_out), dtype=memory.dtype, device=memory.device)
+        if B * Q == 0:
+            return out
+        ow, ob = _dense(output_weight, output_bias)
+        ws_bytes = lib.td_project_ex_workspace_bytes(code, B, Q, N, HD, 1)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=memory.device)
+        with torch.cuda.device(memory.device):
+            _call(lib.td_project_forward_ex, code, _ptr(mem), _ptr(w), _ptr(b), _ptr(shp), _ptr(st), _ptr(loc),
+                  _ptr(att), _ptr(mask), _ptr(ow), _ptr(ob), C_out, _ptr(out), B, Q, N, C, H, HD, L, P, _ptr(ws),
+                  ws_bytes, _stream(memory.device))
+        return out
     out = torch.empty((B, Q, HD), dtype=memory.dtype, device=memory.device)
     if B * Q == 0:
         return out
-    code = DTYPE_CODE[memory.dtype]
     ws_bytes = lib.td_project_workspace_bytes(code, B, N, HD)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=memory.device)
     with torch.cuda.device(memory.device):

@@ -726,9 +726,11 @@ int td_value_proj(int dtype, const void* memory, const void* value_weight, const
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     return dispatch(dtype, [&](auto tag) {
         using T = decltype(tag);
+        // with programmatic dependent launch, as td_linear: every role of the projection kernels waits for the
+        // previous kernel before its first global access, so its set-up overlaps that kernel's tail
         return launch_proj<T>(static_cast<const T*>(memory), static_cast<const T*>(value_weight),
                               static_cast<const T*>(value_bias), static_cast<T*>(value), B, N, C, H, HD,
-                              head_major ? 1 : 0, s, err, err_len);
+                              head_major ? 1 : 0, s, err, err_len, true);
     });
 }
 
@@ -976,6 +978,66 @@ int td_layer_forward(int dtype, int order, const void* query, int64_t Cq, const 
         if (output_weight == nullptr) return int(TD_OK);
         // then the output projection of the attention result
         return launch_proj<T>(target, static_cast<const T*>(output_weight), static_cast<const T*>(output_bias),
+                              static_cast<T*>(out), 1, B * Q, HD, 1, C_out, 0, s, err, err_len, true);
+    });
+}
+
+size_t td_project_ex_workspace_bytes(int dtype, int64_t B, int64_t Q, int64_t N, int64_t HD, int output_proj) {
+    const size_t e = dtype_size(dtype);
+    if (e == 0 || B < 0 || Q < 0 || N < 0 || HD < 0) return 0;
+    const size_t value = (size_t(B) * size_t(N) * size_t(HD) * e + 255) & ~size_t(255);
+    const size_t mid = output_proj ? size_t(B) * size_t(Q) * size_t(HD) * e : 0;
+    return value + mid + 256;
+}
+
+int td_project_forward_ex(int dtype, const void* memory, const void* value_weight, const void* value_bias,
+                          const int64_t* spatial_shapes, const int64_t* level_start_index,
+                          const void* sampling_locations, const void* attention_weights,
+                          const uint8_t* value_padding_mask, const void* output_weight, const void* output_bias,
+                          int64_t C_out, void* out, int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H,
+                          int64_t HD, int64_t L, int64_t P, void* workspace, size_t workspace_bytes, void* stream,
+                          char* err, size_t err_len) {
+    if (output_weight == nullptr) {
+        if (output_bias != nullptr) return fail(err, err_len, TD_ERR_ARG, "output_bias needs output_weight");
+        return td_project_forward_masked(dtype, memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                                         sampling_locations, attention_weights, value_padding_mask, out, B, Q, N, C,
+                                         H, HD, L, P, workspace, workspace_bytes, stream, err, err_len);
+    }
+    if (dtype_size(dtype) == 0) return fail(err, err_len, TD_ERR_ARG, "unsupported dtype code %d", dtype);
+    if (int rc = check_geometry(B, Q, N, H, L, P, err, err_len)) return rc;
+    if (C <= 0 || HD <= 0) return fail(err, err_len, TD_ERR_ARG, "channels and value_weight rows must be positive");
+    if (HD % H != 0) return fail(err, err_len, TD_ERR_ARG, "value_weight rows must be a multiple of the head count");
+    if (C_out <= 0 || C_out > INT32_MAX || HD > INT32_MAX)
+        return fail(err, err_len, TD_ERR_ARG, "output_proj needs 0 < C_out < 2^31");
+    if (B * Q == 0) return TD_OK;
+    if (!memory || !value_weight || !sampling_locations || !attention_weights || !out ||
+        (L * P > 0 && (!spatial_shapes || !level_start_index)))
+        return fail(err, err_len, TD_ERR_ARG, "null tensor pointer");
+    const size_t need = td_project_ex_workspace_bytes(dtype, B, Q, N, HD, 1);
+    if (workspace == nullptr || workspace_bytes < need)
+        return fail(err, err_len, TD_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need,
+                    workspace_bytes);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t D = HD / H;
+    unsigned char* ws =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+    const size_t value_bytes = (size_t(B) * size_t(N) * size_t(HD) * dtype_size(dtype) + 255) & ~size_t(255);
+    return dispatch(dtype, [&](auto tag) {
+        using T = decltype(tag);
+        T* v = reinterpret_cast<T*>(ws);
+        T* mid = reinterpret_cast<T*>(ws + value_bytes);
+        if (N > 0) {
+            if (int rc = launch_proj<T>(static_cast<const T*>(memory), static_cast<const T*>(value_weight),
+                                        static_cast<const T*>(value_bias), v, B, N, C, H, HD, 1, s, err, err_len,
+                                        true))
+                return rc;
+        }
+        if (int rc = launch_sampler<T>(v, H * N * D, D, N * D, spatial_shapes, level_start_index,
+                                       static_cast<const T*>(sampling_locations),
+                                       static_cast<const T*>(attention_weights), mid, B, Q, N, H, D, L, P, s, err,
+                                       err_len, N > 0, value_padding_mask))
+            return rc;
+        return launch_proj<T>(mid, static_cast<const T*>(output_weight), static_cast<const T*>(output_bias),
                               static_cast<T*>(out), 1, B * Q, HD, 1, C_out, 0, s, err, err_len, true);
     });
 }

@@ -99,8 +99,10 @@ def test_output_proj(policy, dtype):
     """The decoder's output_proj chained behind the attention (output_weight / output_bias): against the oracle's
     result projected in float64, both orders, with and without bias; odd widths take the CUDA-core GEMM."""
     g = torch.Generator().manual_seed(9)
+    # the last case takes the CUDA-core paths
     for B, Q, H, D, C, levels, P, c_out in ((2, 33, 8, 32, 256, [(12, 13), (6, 7)], 4, 256),
                                             (1, 150, 4, 16, 64, [(9, 11), (5, 6)], 4, 96),
+                                            (8, 300, 8, 32, 256, [(10, 12), (5, 6)], 4, 256),
                                             (2, 9, 3, 10, 30, [(5, 7), (3, 4)], 4, 20)):
         args = make(B, Q, H, D, C, levels, P, dtype=dtype, seed=Q)
         HD = H * D
