@@ -146,6 +146,15 @@ TD_API int td_sample_backward(int dtype, const void* value, int64_t s_img, int64
                               size_t err_len);
 
 /*
+ * One pass over td_sample_backward's float32 grad_value [rows, HD] (rows = B * N): rounds it into
+ * grad_value_dtype [rows, HD] (float16 / bfloat16; ignored for TD_F32, where the accumulator is used as it is) and
+ * writes its column sums -- the value bias gradient -- into grad_bias (float32 [HD], zeroed here; NULL: skipped).
+ * HD a multiple of 4, at most 1024; 16-byte aligned buffers.
+ */
+TD_API int td_grad_value_finish(int dtype, const float* grad_value, void* grad_value_dtype, float* grad_bias,
+                                int64_t rows, int64_t HD, void* stream, char* err, size_t err_len);
+
+/*
  * One multi-scale deformable attention layer of a DETR-style decoder (Deformable-DETR's MSDeformAttn forward, the
  * caller of upstream's operator), in one call:
  *   proj = query [B, Q, Cq] @ sampling_weight^T + sampling_bias       sampling_weight = [W_offsets; W_attention],

@@ -42,6 +42,7 @@ SIGNATURES = {
     'td_project_ex_workspace_bytes': (_sz, [_ip, _i64, _i64, _i64, _i64, _ip]),
     'td_project_forward_ex': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp,
                                     _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp, _cp, _sz]),
+    'td_grad_value_finish': (_ip, [_ip, _vp, _vp, _vp, _i64, _i64, _vp, _cp, _sz]),
     'td_layer_workspace_bytes': (_sz, [_ip, _ip, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _ip]),
     'td_layer_forward': (_ip, [_ip, _ip, _vp, _i64, _vp, _ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64,
                                _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp, _cp, _sz]),
@@ -458,6 +459,25 @@ def sample_backward(value, spatial_shapes, level_start_index, sampling_locations
               _ptr(loc), _ptr(att), _ptr(mask), _ptr(g), _ptr(grad_value), _ptr(grad_loc), _ptr(grad_attn),
               B, Q, N, H, D, L, P, _stream(v.device))
     return grad_value, grad_loc, grad_attn
+
+
+def grad_value_finish(grad_value, dtype, with_bias):
+    """(grad_value rounded to dtype -- the float32 accumulator itself for float32 --, its column sums in float32 or
+    None) through td_grad_value_finish; grad_value is the float32 [B, N, HD] of sample_backward. Returns None when
+    the shape does not fit the kernel (HD % 4 != 0 or HD > 1024)."""
+    lib = load()
+    HD = grad_value.size(-1)
+    if dtype not in (torch.float32, torch.float16, torch.bfloat16) or grad_value.dtype != torch.float32 \
+            or HD % 4 != 0 or HD > 1024 or not grad_value.is_contiguous():
+        return None
+    rows = grad_value.numel() // HD
+    out = grad_value if dtype == torch.float32 else torch.empty(grad_value.shape, dtype=dtype,
+                                                                device=grad_value.device)
+    bias = torch.empty(HD, dtype=torch.float32, device=grad_value.device) if with_bias else None
+    with torch.cuda.device(grad_value.device):
+        _call(lib.td_grad_value_finish, DTYPE_CODE[dtype], _ptr(grad_value),
+              None if dtype == torch.float32 else _ptr(out), _ptr(bias), rows, HD, _stream(grad_value.device))
+    return out, bias
 
 
 def sample_head_major(value_hm, spatial_shapes, level_start_index, sampling_locations, attention_weights):

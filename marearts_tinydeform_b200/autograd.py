@@ -15,8 +15,8 @@ GEMMs and a column sum:
 These two GEMMs are library GEMMs (torch.matmul, cuBLAS) in the inputs' dtype -- grad_value is rounded once from
 its float32 accumulator, as autograd's own half-precision backward keeps its gradients in half precision, and the
 tensor cores then run them -- except for float32 / float64 inputs, which keep float32 / float64; the bias gradient
-is summed from the float32 accumulator. The value padding mask blocks the gradient of padded tokens exactly as
-masked_fill does in the reference.
+is summed from the float32 accumulator, in the same pass as that rounding (td_grad_value_finish). The value
+padding mask blocks the gradient of padded tokens exactly as masked_fill does in the reference.
 """
 
 import torch
@@ -49,14 +49,21 @@ class MaDeformAttnFunction(torch.autograd.Function):
         grad_value, grad_loc, grad_attn = _native.sample_backward(
             value, shapes, starts, loc, attn, grad_out.to(memory.dtype).contiguous(), mask, heads=H)
         acc = grad_value.view(B * N, HD)
-        gv = acc.to(memory.dtype) if memory.dtype in (torch.float16, torch.bfloat16) else acc
+        want_bias = bias is not None and need[2]
+        # the rounding to the dtype and the bias gradient's column sums in one pass over the accumulator
+        done = _native.grad_value_finish(acc, memory.dtype, want_bias) if memory.dtype != torch.float64 else None
+        if done is not None:
+            gv, bias_sum = done
+        else:
+            gv = acc.to(memory.dtype) if memory.dtype in (torch.float16, torch.bfloat16) else acc
+            bias_sum = acc.sum(0) if want_bias else None
         grad_memory = grad_weight = grad_bias = None
         if need[0]:
             grad_memory = (gv @ weight.to(gv.dtype)).view(B, N, C).to(memory.dtype)
         if need[1]:
             grad_weight = (gv.t() @ memory.reshape(B * N, C).to(gv.dtype)).to(weight.dtype)
-        if bias is not None and need[2]:
-            grad_bias = acc.sum(0).to(bias.dtype)
+        if want_bias:
+            grad_bias = bias_sum.to(bias.dtype)
         return (grad_memory, grad_weight, grad_bias, None, None, grad_loc if need[5] else None,
                 grad_attn if need[6] else None, None, None)
 

@@ -227,4 +227,45 @@ __global__ void __launch_bounds__(kBackWarps * 32) sample_backward_generic_kerne
     }
 }
 
+// One pass over the float32 grad_value accumulator [rows, HD]: its rounding to the dtype (out, or none for float32)
+// and its column sums, the value bias gradient (added into bias_acc, zeroed by the host). 256 threads a CTA: a
+// thread owns 4 columns (HD / 4 <= 256 of them) of every (256 / (HD / 4))-th row of the CTA's block of rows;
+// the CTA's partial sums meet in shared memory and leave with one atomic per column.
+constexpr int kFinishThreads = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(kFinishThreads) grad_value_finish_kernel(const float* __restrict__ acc,
+                                                                           T* __restrict__ out,
+                                                                           float* __restrict__ bias_acc,
+                                                                           long long rows, int HD,
+                                                                           long long rows_per_cta) {
+    __shared__ float4 s_sum[kFinishThreads];
+    const int groups = HD >> 2;  // 4-column groups
+    const int lanes_per_row = groups, row_step = kFinishThreads / groups;
+    const int gcol = threadIdx.x % lanes_per_row, r0 = threadIdx.x / lanes_per_row;
+    const bool active = r0 < row_step;
+    const long long first = (long long)blockIdx.x * rows_per_cta;
+    const long long last = min(first + rows_per_cta, rows);
+    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (active) {
+        for (long long r = first + r0; r < last; r += row_step) {
+            const float4 v = __ldcs(reinterpret_cast<const float4*>(acc + r * HD) + gcol);  // read once: streaming
+            sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+            if constexpr (!std::is_same<T, float>::value) {  // four 16-bit values: one 8-byte store
+                const T q[4] = {from_acc<T>(v.x), from_acc<T>(v.y), from_acc<T>(v.z), from_acc<T>(v.w)};
+                *reinterpret_cast<uint2*>(out + r * HD + 4 * gcol) = *reinterpret_cast<const uint2*>(q);
+            }
+        }
+    }
+    s_sum[threadIdx.x] = sum;
+    __syncthreads();
+    if (bias_acc == nullptr || threadIdx.x >= groups) return;
+    float4 t = s_sum[threadIdx.x];
+    for (int k = 1; k < row_step; ++k) {
+        const float4 u = s_sum[threadIdx.x + k * lanes_per_row];
+        t.x += u.x; t.y += u.y; t.z += u.z; t.w += u.w;
+    }
+    atomicAdd(reinterpret_cast<float4*>(bias_acc) + threadIdx.x, t);
+}
+
 }  // namespace td

@@ -803,6 +803,43 @@ int td_sample_backward(int dtype, const void* value, int64_t s_img, int64_t s_to
     });
 }
 
+int td_grad_value_finish(int dtype, const float* grad_value, void* grad_value_dtype, float* grad_bias,
+                         int64_t rows, int64_t HD, void* stream, char* err, size_t err_len) {
+    if (dtype != TD_F32 && dtype != TD_F16 && dtype != TD_BF16)
+        return fail(err, err_len, TD_ERR_ARG, "grad_value finish takes float32, float16 or bfloat16 (code %d)", dtype);
+    if (rows < 0 || HD <= 0 || HD % 4 != 0 || HD > 4 * kFinishThreads)
+        return fail(err, err_len, TD_ERR_ARG, "grad_value finish needs rows >= 0 and 0 < HD <= %d, HD %% 4 == 0",
+                    4 * kFinishThreads);
+    if (rows > 0 && (!grad_value || (dtype != TD_F32 && !grad_value_dtype)))
+        return fail(err, err_len, TD_ERR_ARG, "null tensor pointer");
+    if ((rows > 0 && !aligned16(grad_value)) || (grad_bias && !aligned16(grad_bias)))
+        return fail(err, err_len, TD_ERR_ARG, "grad_value and grad_bias must be 16-byte aligned");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (grad_bias) {
+        const cudaError_t e = cudaMemsetAsync(grad_bias, 0, size_t(HD) * sizeof(float), s);
+        if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    }
+    if (rows == 0) return TD_OK;
+    DeviceFacts f;
+    if (int rc = device_facts(&f, err, err_len)) return rc;
+    // about four CTAs per SM, each over a contiguous block of rows
+    const long long ctas_wanted = 4LL * f.sm_count;
+    const long long per_cta = std::max<long long>(1, (rows + ctas_wanted - 1) / ctas_wanted);
+    const unsigned grid = unsigned((rows + per_cta - 1) / per_cta);
+    auto go = [&](auto kernel, auto* out) {
+        const cudaError_t e = launch_kernel(kernel, dim3(grid), dim3(kFinishThreads), 0, s, false, grad_value, out,
+                                            grad_bias, (long long)rows, int(HD), per_cta);
+        if (e != cudaSuccess)
+            return fail(err, err_len, TD_ERR_CUDA, "grad_value_finish_kernel launch: %s", cudaGetErrorString(e));
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+        return check_launch(err, err_len, "grad_value_finish_kernel");
+    };
+    if (dtype == TD_F16) return go(grad_value_finish_kernel<__half>, static_cast<__half*>(grad_value_dtype));
+    if (dtype == TD_BF16)
+        return go(grad_value_finish_kernel<__nv_bfloat16>, static_cast<__nv_bfloat16*>(grad_value_dtype));
+    return go(grad_value_finish_kernel<float>, static_cast<float*>(nullptr));
+}
+
 int td_sample_strided(int dtype, const void* value, int64_t s_img, int64_t s_tok, int64_t s_head,
                       const int64_t* spatial_shapes, const int64_t* level_start_index,
                       const void* sampling_locations, const void* attention_weights, void* out,

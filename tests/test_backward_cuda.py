@@ -176,3 +176,18 @@ def test_only_requested_gradients_and_no_grad_path(cuda):
     assert loc.grad is not None and loc.grad.shape == loc.shape
     with torch.no_grad():
         assert not ma_deform_attn(*args[:5], loc, args[6]).requires_grad
+
+
+def test_grad_value_finish(cuda):
+    """td_grad_value_finish: the rounding to the dtype and the column sums of a float32 accumulator, for widths that
+    fill the 256-thread CTA exactly (HD = 256) and not (HD = 80, 1024), against torch."""
+    g = torch.Generator(device=cuda).manual_seed(4)
+    for rows, HD in ((67200, 256), (999, 80), (130, 1024), (0, 256)):
+        acc = torch.randn(rows, HD, generator=g, device=cuda)
+        for dtype in (torch.float16, torch.bfloat16, torch.float32):
+            out, bias = _native.grad_value_finish(acc, dtype, True)
+            assert torch.equal(out, acc.to(dtype)), f'{rows}x{HD} {dtype}'
+            want = acc.double().sum(0)
+            assert torch.allclose(bias.double(), want, atol=1e-3 * max(1.0, rows ** 0.5), rtol=1e-5), \
+                f'{rows}x{HD} {dtype}: bias'
+    assert _native.grad_value_finish(torch.zeros(4, 6, device=cuda), torch.float16, True) is None
