@@ -494,11 +494,17 @@ def run_backward(args):
                               args.steps, args.warmup)
         times['forward_only'] = time_graph(gf, args.steps, reps=max(1, args.reps))
         del gf
-        # the backward kernel alone, on the values of the rotating sets in the layout the backward uses
-        vals = [torch.nn.functional.linear(p_[0], base[1], base[2]) for p_ in plain]
+        # the backward kernel alone, on the values of the rotating sets in the layout the backward uses (the
+        # project order's own head-major value; the fused order recomputes it in the nn.Linear layout)
+        if mode == 'project':
+            vals = [_native.value_proj(p_[0], base[1], base[2], H, head_major=True) for p_ in plain]
+            heads = None
+        else:
+            vals = [torch.nn.functional.linear(p_[0], base[1], base[2]) for p_ in plain]
+            heads = H
         gk, _ = graph_time_us(lambda i: _native.sample_backward(vals[i % len(vals)], shapes, starts,
                                                                 *plain[i % len(plain)][1:], gouts[i % len(gouts)],
-                                                                heads=H),
+                                                                heads=heads),
                               args.steps, args.warmup)
         t_kernel = time_graph(gk, args.steps, reps=max(1, args.reps))
         del gk, vals

@@ -227,9 +227,11 @@ def check_output_proj(output_weight, output_bias, HD, ref):
 
 def project_forward(memory, value_weight, value_bias, spatial_shapes, level_start_index,
                     sampling_locations, attention_weights, value_padding_mask=None, output_weight=None,
-                    output_bias=None):
+                    output_bias=None, return_value=False):
     """Project order (upstream __init__.py:77-79: F.linear + _C.sample_forward) through td_project_forward (with a
-    value padding mask: td_project_forward_masked; with output_proj: td_project_forward_ex)."""
+    value padding mask: td_project_forward_masked; with output_proj: td_project_forward_ex). return_value (no
+    output_proj): also return the projected value the call computed, head-major [B, H, N, D] (a view of its
+    workspace), for a backward pass."""
     lib = load()
     B, Q, H, L, P = check_geometry(memory, spatial_shapes, level_start_index, sampling_locations, attention_weights)
     HD = check_projection(memory, value_weight, value_bias, H)
@@ -253,7 +255,7 @@ def project_forward(memory, value_weight, value_bias, spatial_shapes, level_star
         return out
     out = torch.empty((B, Q, HD), dtype=memory.dtype, device=memory.device)
     if B * Q == 0:
-        return out
+        return (out, None) if return_value else out
     ws_bytes = lib.td_project_workspace_bytes(code, B, N, HD)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=memory.device)
     with torch.cuda.device(memory.device):
@@ -264,7 +266,13 @@ def project_forward(memory, value_weight, value_bias, spatial_shapes, level_star
             _call(lib.td_project_forward_masked, code, _ptr(mem), _ptr(w), _ptr(b), _ptr(shp), _ptr(st), _ptr(loc),
                   _ptr(att), _ptr(mask), _ptr(out), B, Q, N, C, H, HD, L, P, _ptr(ws), ws_bytes,
                   _stream(memory.device))
-    return out
+    if not return_value:
+        return out
+    # the library puts the value at the workspace's first 256-byte boundary
+    skip = (-ws.data_ptr()) % 256
+    e = memory.element_size()
+    value = ws[skip:skip + B * N * HD * e].view(memory.dtype).view(B, H, N, HD // H)
+    return out, value
 
 
 def linear(x, weight, bias):

@@ -2,9 +2,10 @@
 
 Upstream's CUDA operator is inference only (marearts_tinydeform/__init__.py:67-71 rejects inputs that require
 grad); this build differentiates it. Forward: the same B200 kernels as inference, in the order `mode` picks,
-saving only the inputs. Backward (activation recompute): the value projection is run again (nn.Linear layout,
-by torch's GEMM: the backward runs on autograd's worker thread, also under CUDA-graph capture, where a library
-GEMM needs no tensor-map set-up), then td_sample_backward gives grad_value (float32 accumulation),
+saving the inputs and, in the project order, the projected value the forward computed anyway (head-major, B * N *
+H * D elements kept until the backward). Backward: in the fused order the value projection is run again
+(nn.Linear layout, by torch's GEMM: the backward runs on autograd's worker thread, also under CUDA-graph capture,
+where a library GEMM needs no tensor-map set-up); then td_sample_backward gives grad_value (float32 accumulation),
 grad_sampling_locations and grad_attention_weights in one pass, and the three parameter gradients follow by plain
 GEMMs and a column sum:
 
@@ -31,23 +32,32 @@ class MaDeformAttnFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, memory, value_weight, value_bias, spatial_shapes, level_start_index, sampling_locations,
                 attention_weights, mode, value_padding_mask):
-        run = _native.fused_forward if mode == 'fused' else _native.project_forward
-        out = run(memory, value_weight, value_bias, spatial_shapes, level_start_index, sampling_locations,
-                  attention_weights, value_padding_mask)
+        value = None
+        if mode == 'fused':
+            out = _native.fused_forward(memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                                        sampling_locations, attention_weights, value_padding_mask)
+        else:
+            out, value = _native.project_forward(memory, value_weight, value_bias, spatial_shapes,
+                                                 level_start_index, sampling_locations, attention_weights,
+                                                 value_padding_mask, return_value=True)
         ctx.save_for_backward(memory, value_weight, value_bias, spatial_shapes, level_start_index,
-                              sampling_locations, attention_weights, value_padding_mask)
+                              sampling_locations, attention_weights, value_padding_mask, value)
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        memory, weight, bias, shapes, starts, loc, attn, mask = ctx.saved_tensors
+        memory, weight, bias, shapes, starts, loc, attn, mask, value_hm = ctx.saved_tensors
         need = ctx.needs_input_grad
         H = loc.shape[2]
         B, N, C = memory.shape
         HD = weight.shape[0]
-        value = torch.nn.functional.linear(memory, weight, bias)  # [B, N, H * D]
-        grad_value, grad_loc, grad_attn = _native.sample_backward(
-            value, shapes, starts, loc, attn, grad_out.to(memory.dtype).contiguous(), mask, heads=H)
+        g = grad_out.to(memory.dtype).contiguous()
+        if value_hm is not None:  # the forward's own value, head-major
+            grad_value, grad_loc, grad_attn = _native.sample_backward(value_hm, shapes, starts, loc, attn, g, mask)
+        else:
+            value = torch.nn.functional.linear(memory, weight, bias)  # [B, N, H * D]
+            grad_value, grad_loc, grad_attn = _native.sample_backward(value, shapes, starts, loc, attn, g, mask,
+                                                                      heads=H)
         acc = grad_value.view(B * N, HD)
         want_bias = bias is not None and need[2]
         # the rounding to the dtype and the bias gradient's column sums in one pass over the accumulator
