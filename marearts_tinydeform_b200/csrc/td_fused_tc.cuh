@@ -159,7 +159,8 @@ __global__ void __launch_bounds__(kFtcThreads, 1)
                 if (tid == 0) {
                     mbar_arrive_expect_tx(&wbar[g], w_bytes);
                     for (int kb = 0; kb < kblocks; ++kb)
-                        tma_load_2d(w_tile + (g * kblocks + kb) * D * 128, &map_w, &wbar[g], kb * 64, hg * D);
+                        tma_load_2d(w_tile + (g * kblocks + kb) * D * 128, &map_w, &wbar[g], kb * 64, hg * D,
+                                    l2_evict_last());
                 }
                 for (int d = tid; d < D; d += kFtcThreads)
                     sbias[g * D + d] = a.bias != nullptr ? to_acc(a.bias[hg * D + d]) : 0.f;

@@ -81,22 +81,33 @@ template <> struct GemmKind<float> {
     static constexpr uint32_t kFormat = 2;  // tf32
 };
 
-template <typename T, int BN, int EPI>
+// Resident-weight tiles (RES): every tile of a CTA has the same BN-row slice of W (the grid is a multiple of the
+// channel-tile count and channel tiles run fastest), so the CTA loads that slice once, for all of its tiles, and the
+// slot ring carries only memory boxes. A 128 x 256 tile that reloads its 128 KB of W reads 192 KB into the SM; a
+// resident-weight 128 x 128 tile reads 64 KB. At most kResKBlocks K blocks (C <= 256 for 16-bit types).
+constexpr int kResKBlocks = 4;
+
+template <typename T, int BN, int EPI, bool RES = false>
 struct ProjTcLayout {
     static constexpr bool kSplit = GemmKind<T>::kSplit;
+    static constexpr bool kRes = RES;
     static constexpr int kBK = GemmKind<T>::kBK;
     static constexpr uint32_t kABytes = kTcBM * 128;  // 16 KB
     static constexpr uint32_t kBBytes = BN * 128;
-    static constexpr uint32_t kStageBytes = (kABytes + kBBytes) * (kSplit ? 2 : 1);  // float32: + the lo copies
+    // a slot: the memory box and (unless the weights are resident) the weight box; float32: + the lo copies
+    static constexpr uint32_t kStageBytes = RES ? kABytes : (kABytes + kBBytes) * (kSplit ? 2 : 1);
+    static constexpr uint32_t kWBytes = RES ? kResKBlocks * kBBytes : 0;  // the resident weight slice
     static constexpr uint32_t kStgBytes = kTcBM * BN * sizeof(T);  // epilogue staging tile
     static constexpr uint32_t kBiasBytes = BN * 4;
-    static constexpr int kFit = int((kTcSmemBudget - kStgBytes - kBiasBytes) / kStageBytes);
+    static constexpr int kFit = int((kTcSmemBudget - kStgBytes - kBiasBytes - kWBytes) / kStageBytes);
     static constexpr int kStages = kFit < 8 ? kFit : 8;  // two producer lanes a slot: at most 16
-    static constexpr uint32_t kStgOffset = kStages * kStageBytes;  // 1024-aligned: stage sizes are multiples of 1 KB
+    static constexpr uint32_t kWOffset = kStages * kStageBytes;  // 1024-aligned: stage sizes are multiples of 1 KB
+    static constexpr uint32_t kStgOffset = kWOffset + kWBytes;
     static constexpr uint32_t kBiasOffset = kStgOffset + kStgBytes;
-    // barriers: full[S] (two arrivals: the memory and the weight box), split[S], empty[S], tfull[2], tempty[2]
+    // barriers: full[S] (two arrivals: the memory and the weight box; one with resident weights), split[S],
+    // empty[S], tfull[2], tempty[2], wfull (the resident weight slice: one arrival per K block)
     static constexpr uint32_t kBarOffset = kBiasOffset + kBiasBytes;
-    static constexpr uint32_t kSlotOffset = kBarOffset + (3 * kStages + 4) * 8;
+    static constexpr uint32_t kSlotOffset = kBarOffset + (3 * kStages + 5) * 8;
     static constexpr uint32_t kSmemBytes = kSlotOffset + 16 + 1024;  // + slack to align the base to 1024
     static constexpr uint32_t kTmemCols = 2 * BN;
     // warp 0 loads, warp 3 issues the MMAs, warps 4 .. 4+EPI-1 run the epilogue (a multiple of 4 apart, as epilogue
@@ -109,6 +120,7 @@ struct ProjTcLayout {
     static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
     static_assert(EPI == 4 || EPI == 8, "epilogue warps");
     static_assert(kStages >= 2, "pipeline depth");
+    static_assert(!RES || !kSplit, "resident weights: 16-bit types only");
     static_assert(kSlotOffset + 16 <= uint32_t(kTcSmemBudget) + 512, "shared memory");
 };
 
@@ -161,12 +173,12 @@ __device__ __forceinline__ void pack8(const float* f, uint4* w) {
 
 // The projection tiles of this CTA, from barrier setup to TMEM release (ends with a CTA-wide barrier; every value
 // store of the CTA has completed by then). smem is the 1024-byte aligned dynamic shared memory.
-template <typename T, int BN, int EPI>
+template <typename T, int BN, int EPI, bool RES>
 __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const CUtensorMap& map_b0,
                                               const CUtensorMap& map_out0, const CUtensorMap& map_a1,
                                               const CUtensorMap& map_b1, const CUtensorMap& map_out1,
                                               const ProjTcArgs<T>& a, unsigned char* smem) {
-    using Lay = ProjTcLayout<T, BN, EPI>;
+    using Lay = ProjTcLayout<T, BN, EPI, RES>;
     constexpr int S = Lay::kStages;
     constexpr int kBK = Lay::kBK;
     constexpr bool kSplit = Lay::kSplit;
@@ -176,6 +188,7 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const C
     uint64_t* empty = split + S;
     uint64_t* tfull = empty + S;
     uint64_t* tempty = tfull + 2;
+    uint64_t* wfull = tempty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Lay::kSlotOffset);
     unsigned char* stg = smem + Lay::kStgOffset;
     float* sbias = reinterpret_cast<float*>(smem + Lay::kBiasOffset);
@@ -184,12 +197,16 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const C
     auto slot_b = [&](int s) { return smem + s * Lay::kStageBytes + Lay::kABytes; };
     auto slot_alo = [&](int s) { return smem + s * Lay::kStageBytes + Lay::kABytes + Lay::kBBytes; };
     auto slot_blo = [&](int s) { return smem + s * Lay::kStageBytes + 2 * Lay::kABytes + Lay::kBBytes; };
+    // the weight box of K block kb: from slot s, or from the resident slice
+    auto b_tile = [&](int s, int kb) {
+        return RES ? smem + Lay::kWOffset + kb * Lay::kBBytes : slot_b(s);
+    };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KB = a.k_blocks;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], 2);
+            mbar_init(&full[s], RES ? 1 : 2);
             mbar_init(&split[s], 4);  // one arrival per split warp
             mbar_init(&empty[s], 1);
         }
@@ -197,6 +214,7 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const C
             mbar_init(&tfull[i], 1);
             mbar_init(&tempty[i], EPI);  // one arrival per epilogue warp
         }
+        mbar_init(wfull, RES ? KB : 1);
         mbar_fence_init();
         tma_prefetch_desc(&map_a0);
         tma_prefetch_desc(&map_b0);
@@ -238,13 +256,25 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const C
     // so the kernels that wrote them must have completed.
 
     if (warp < Lay::kMmaWarp) {
-        if (warp == 0 && lane < 2 * S) {
-            // TMA producer lane: slot s, the memory box (even lane) or the weight box (odd lane) of the K blocks
-            // it = s, s + S, ... of this CTA's sequence (tile-major); then one more round that only waits, so that
-            // no MMA commit is still to arrive on the slot when the CTA exits
-            const int s = lane >> 1;
-            const bool box_a = (lane & 1) == 0;
+        if (RES && warp == 0 && lane >= S && lane < S + KB) {
+            // resident weights: lane S + kb loads K block kb of the CTA's weight slice, once
+            if (my_tiles > 0) {
+                int j, b, n0, c0;
+                tile_at(int(blockIdx.x), j, b, n0, c0);
+                const int kb = lane - S;
+                grid_dependency_wait();
+                launch_dependents();
+                mbar_arrive_expect_tx(wfull, Lay::kBBytes);
+                tma_load_2d(b_tile(0, kb), &map_b0, wfull, kb * kBK, c0, l2_evict_last());
+            }
+        } else if (warp == 0 && lane < (RES ? S : 2 * S)) {
+            // TMA producer lane: slot s, the memory box (even lane; every lane s with resident weights) or the weight
+            // box (odd lane) of the K blocks it = s, s + S, ... of this CTA's sequence (tile-major); then one more
+            // round that only waits, so that no MMA commit is still to arrive on the slot when the CTA exits
+            const int s = RES ? lane : lane >> 1;
+            const bool box_a = RES || (lane & 1) == 0;
             const int total = my_tiles * KB;
+            const uint64_t pol_a = l2_evict_first(), pol_w = l2_evict_last();
             long long t0 = clock64();
             bool waited = false;
             for (int it = s; it < total + S;) {
@@ -260,10 +290,10 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const C
                         }
                         if (box_a) {
                             mbar_arrive_expect_tx(&full[s], Lay::kABytes);
-                            tma_load_3d(slot_a(s), j ? &map_a1 : &map_a0, &full[s], kb * kBK, n0, b);
+                            tma_load_3d(slot_a(s), j ? &map_a1 : &map_a0, &full[s], kb * kBK, n0, b, pol_a);
                         } else {
                             mbar_arrive_expect_tx(&full[s], Lay::kBBytes);
-                            tma_load_2d(slot_b(s), j ? &map_b1 : &map_b0, &full[s], kb * kBK, c0);
+                            tma_load_2d(slot_b(s), j ? &map_b1 : &map_b0, &full[s], kb * kBK, c0, pol_w);
                         }
                     }
                     it += S;
@@ -283,7 +313,8 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const C
             constexpr uint32_t idesc = (1u << 4) | (GemmKind<T>::kFormat << 7) | (GemmKind<T>::kFormat << 10) |
                                        (uint32_t(BN >> 3) << 17) | (uint32_t(kTcBM >> 4) << 24);
             int it = 0;
-            bool ok = true;
+            // resident weights: the slice has landed before the first MMA
+            bool ok = !RES || my_tiles == 0 || mbar_wait(wfull, 0u, kErrTmaWait);
             for (int tc = 0; ok && tc < my_tiles; ++tc) {
                 const int acc = tc & 1;
                 if (!mbar_wait(&tempty[acc], uint32_t((tc >> 1) & 1) ^ 1u, kErrSlotWait)) break;
@@ -297,7 +328,7 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const C
                     }
                     tc_fence_after();
                     const uint64_t da = sdesc_sw128(smem_addr(slot_a(s)));
-                    const uint64_t db = sdesc_sw128(smem_addr(slot_b(s)));
+                    const uint64_t db = sdesc_sw128(smem_addr(b_tile(s, kb)));
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {  // 4 K steps of 32 bytes per 128-byte row
                         const uint64_t kofs = uint64_t(2 * k);
@@ -414,9 +445,9 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const C
                     const unsigned char* src = stg + p * (kTcBM * pb) + quarter * 32 * pb;
                     if (J.head_major) {
                         const int h = col / J.D;
-                        tma_store_3d(map_out, src, col - h * J.D, n0 + quarter * 32, b * J.H + h);
+                        tma_store_3d(map_out, src, col - h * J.D, n0 + quarter * 32, b * J.H + h, l2_evict_last());
                     } else {
-                        tma_store_3d(map_out, src, col, n0 + quarter * 32, b);
+                        tma_store_3d(map_out, src, col, n0 + quarter * 32, b, l2_evict_last());
                     }
                     bulk_commit();
                 }
@@ -471,14 +502,14 @@ __device__ __forceinline__ unsigned char* align1024(unsigned char* p) {
 // 72 registers a thread (no spills): 12 warps, 3 per SM sub-partition (27 K registers), leave room on the SM for two
 // CTAs of the sampler that follows in the project order (launched early, under programmatic dependent launch).
 // Tensor maps of job 0 (memory, weight, output) and job 1 (the same; copies of job 0's when there is no job 1).
-template <typename T, int BN, int EPI>
+template <typename T, int BN, int EPI, bool RES>
 __global__ void __maxnreg__(72)
     proj_tc_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_b0,
                    const __grid_constant__ CUtensorMap map_out0, const __grid_constant__ CUtensorMap map_a1,
                    const __grid_constant__ CUtensorMap map_b1, const __grid_constant__ CUtensorMap map_out1,
                    const ProjTcArgs<T> a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    proj_tc_tiles<T, BN, EPI>(map_a0, map_b0, map_out0, map_a1, map_b1, map_out1, a, align1024(smem_raw));
+    proj_tc_tiles<T, BN, EPI, RES>(map_a0, map_b0, map_out0, map_a1, map_b1, map_out1, a, align1024(smem_raw));
 }
 
 }  // namespace td

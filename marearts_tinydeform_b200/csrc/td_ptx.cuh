@@ -88,30 +88,53 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
     return true;
 }
 
+// ---- L2 eviction priority ---------------------------------------------------------------------------------
+// Cache policies (createpolicy) for the .L2::cache_hint forms of the TMA copies below. evict_first marks data read
+// once (the projection's input rows, which would otherwise push out what comes next); evict_last marks data read
+// again soon (weights, read by every tile; the projected value, which the sampler gathers right after the
+// projection). On the DINO shape (B = 8, 91 MB of value against a 126 MB L2) this took the project order from 114 to
+// 109 us.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 // ---- TMA ----------------------------------------------------------------------------------------------------
-// 2-D tiled load of box (x = innermost, y) into shared memory, completing `bytes` on the mbarrier.
-// x * element size must be a multiple of 16 bytes (callers pass multiples of 64 elements).
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+// 2-D tiled load of box (x = innermost, y) into shared memory, completing `bytes` on the mbarrier, with L2 cache
+// policy `pol`. x * element size must be a multiple of 16 bytes (callers pass multiples of 64 elements).
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y,
+                                            uint64_t pol) {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
-        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4}], [%2], %5;"
+        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "l"(pol)
         : "memory");
 }
 
 // 3-D tiled load of box (x, y, z), completing its bytes on the mbarrier. Same alignment rule on x.
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
+                                            uint64_t pol) {
     asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
-        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z)
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4, %5}], [%2], %6;"
+        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z),
+          "l"(pol)
         : "memory");
 }
 
 // 3-D tiled store of the box at (x, y, z) from shared memory, tracked by the issuing thread's bulk async-group.
 // Elements of the box outside the tensor are not written. x * element size must be a multiple of 16 bytes and no
 // coordinate may be negative.
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
-    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
-                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(src)), "r"(x), "r"(y), "r"(z)
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z,
+                                             uint64_t pol) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3, %4}], [%1], %5;"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(src)), "r"(x), "r"(y), "r"(z), "l"(pol)
                  : "memory");
 }
 

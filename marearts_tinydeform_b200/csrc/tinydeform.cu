@@ -399,11 +399,11 @@ int prepare_proj_tc(const ProjShape& ps, CUtensorMap* map_a, CUtensorMap* map_b,
 }
 
 // One launch of the tcgen05 projection kernel for job0 and, when job1 is not null, job1 (same C): job1's tiles
-// follow job0's in the persistent grid.
-template <typename T, int BN, int EPI>
+// follow job0's in the persistent grid. RES: resident weight slices (job0 alone, at most kResKBlocks K blocks).
+template <typename T, int BN, int EPI, bool RES = false>
 int launch_proj_tc(const ProjShape& job0, const ProjShape* job1, cudaStream_t stream, bool pdl, char* err,
                    size_t err_len) {
-    using Lay = ProjTcLayout<T, BN, EPI>;
+    using Lay = ProjTcLayout<T, BN, EPI, RES>;
     static std::atomic<uint64_t> smem_done{0};
     DeviceFacts f;
     if (int rc = device_facts(&f, err, err_len)) return rc;
@@ -421,10 +421,16 @@ int launch_proj_tc(const ProjShape& job0, const ProjShape* job1, cudaStream_t st
     a.C = int(job0.C);
     a.k_blocks = int((job0.C + Lay::kBK - 1) / Lay::kBK);
     a.tiles = a.job[0].tiles + a.job[1].tiles;
-    if (int rc = allow_smem(proj_tc_kernel<T, BN, EPI>, Lay::kSmemBytes, smem_done, err, err_len)) return rc;
-    // persistent: at most one CTA per SM (the slot ring takes most of the shared memory)
-    const int grid = a.tiles < f.sm_count ? a.tiles : f.sm_count;
-    const cudaError_t err_launch = launch_kernel(proj_tc_kernel<T, BN, EPI>, dim3(unsigned(grid)), dim3(Lay::kThreads),
+    if (RES && (job1 != nullptr || a.k_blocks > kResKBlocks))
+        return fail(err, err_len, TD_ERR_ARG, "resident-weight projection: one job of at most %d K blocks",
+                    kResKBlocks);
+    if (int rc = allow_smem(proj_tc_kernel<T, BN, EPI, RES>, Lay::kSmemBytes, smem_done, err, err_len)) return rc;
+    // persistent: at most one CTA per SM (the slot ring takes most of the shared memory). With resident weights the
+    // grid is a multiple of the channel-tile count, so that every tile of a CTA has the same channel tile (the tile
+    // count itself is one, when it is the smaller).
+    const int cap = RES ? f.sm_count - f.sm_count % a.job[0].n_tiles : f.sm_count;
+    const int grid = a.tiles < cap ? a.tiles : cap;
+    const cudaError_t err_launch = launch_kernel(proj_tc_kernel<T, BN, EPI, RES>, dim3(unsigned(grid)), dim3(Lay::kThreads),
                                                  Lay::kSmemBytes, stream, pdl, map_a0, map_b0, map_out0, map_a1,
                                                  map_b1, map_out1, a);
     if (err_launch != cudaSuccess)
@@ -459,37 +465,59 @@ bool proj_tc_eligible(const T* memory, const T* weight, const T* value, int64_t 
     }
 }
 
-// Tile width of the tcgen05 projection: the busiest CTA runs ceil(tiles / SMs) tiles, each costing about the load
-// of its 128 memory rows (like 128 more output columns) plus BN output columns; the width that makes that smallest,
-// the widest of equals. float32 tiles are at most 128 wide (their slots hold hi and lo halves). (B2, N2, HD2): a
+// Tile plan of the tcgen05 projection: the busiest CTA runs ceil(tiles / SMs) tiles, each costing about the load
+// of its 128 memory rows (like 128 more output columns) plus the BN weight rows it loads with them; the plan that
+// makes that smallest, the widest of equals. float32 tiles are at most 128 wide (their slots hold hi and lo
+// halves). Resident weights (16-bit types, one job, C within kResKBlocks K blocks; 128 wide): a tile costs its 128
+// memory rows only, and the CTA loads its weight slice once (counted as one more tile's memory rows); they are
+// picked only when strictly cheaper, i.e. when CTAs run several tiles (batch 4 and up at C = 256). (B2, N2, HD2): a
 // second job in the same launch (B2 = 0: none).
+struct TilePlan {
+    int bn;
+    bool res;
+};
+
 template <typename T>
-int proj_tile_width(int64_t B, int64_t N, int64_t HD, int sm_count, int64_t B2 = 0, int64_t N2 = 0,
-                    int64_t HD2 = 0) {
-    if (TD_PROJ_TILE != 0) return TD_PROJ_TILE;
+TilePlan proj_tile_plan(int64_t B, int64_t N, int64_t C, int64_t HD, int sm_count, int64_t B2 = 0, int64_t N2 = 0,
+                        int64_t HD2 = 0) {
+    if (TD_PROJ_TILE != 0) return {TD_PROJ_TILE, false};
     const int64_t m_tiles = B * ((N + kTcBM - 1) / kTcBM);
     const int64_t m_tiles2 = B2 * ((N2 + kTcBM - 1) / kTcBM);
-    int bn = 64;
+    TilePlan plan{64, false};
     long long best = -1;
     for (int w : {256, 128, 64}) {
         if (std::is_same<T, float>::value && w > 128) continue;
         const long long tiles = m_tiles * ((HD + w - 1) / w) + m_tiles2 * ((HD2 + w - 1) / w);
         const long long cost = (tiles + sm_count - 1) / sm_count * (w + 128);
-        if (best < 0 || cost < best) { best = cost; bn = w; }
+        if (best < 0 || cost < best) { best = cost; plan = {w, false}; }
     }
-    return bn;
+    if (!std::is_same<T, float>::value && B2 == 0 && (C + GemmKind<T>::kBK - 1) / GemmKind<T>::kBK <= kResKBlocks) {
+        const long long n_tiles = (HD + 127) / 128;
+        const long long grid = sm_count - sm_count % n_tiles;
+        if (grid > 0) {
+            const long long tiles = m_tiles * n_tiles;
+            const long long cost = (tiles + grid - 1) / grid * 128 + 128;
+            if (cost < best) plan = {128, true};
+        }
+    }
+    return plan;
 }
 
-// Calls f(std::integral_constant<int, BN>, std::integral_constant<int, EPI>) for the instantiated tile shape of bn.
+// Calls f(std::integral_constant<int, BN>, std::integral_constant<int, EPI>, std::integral_constant<bool, RES>)
+// for the instantiated tile shape of the plan.
 template <typename T, typename F>
-int with_tile(int bn, F&& f) {
+int with_tile(TilePlan plan, F&& f) {
+    using no = std::integral_constant<bool, false>;
     if constexpr (std::is_same<T, float>::value) {
-        if (bn >= 128) return f(std::integral_constant<int, 128>{}, std::integral_constant<int, 4>{});
-        return f(std::integral_constant<int, 64>{}, std::integral_constant<int, 4>{});
+        if (plan.bn >= 128) return f(std::integral_constant<int, 128>{}, std::integral_constant<int, 4>{}, no{});
+        return f(std::integral_constant<int, 64>{}, std::integral_constant<int, 4>{}, no{});
     } else {
-        if (bn == 256) return f(std::integral_constant<int, 256>{}, std::integral_constant<int, 8>{});
-        if (bn == 128) return f(std::integral_constant<int, 128>{}, std::integral_constant<int, 8>{});
-        return f(std::integral_constant<int, 64>{}, std::integral_constant<int, 4>{});
+        if (plan.res)
+            return f(std::integral_constant<int, 128>{}, std::integral_constant<int, 8>{},
+                     std::integral_constant<bool, true>{});
+        if (plan.bn == 256) return f(std::integral_constant<int, 256>{}, std::integral_constant<int, 8>{}, no{});
+        if (plan.bn == 128) return f(std::integral_constant<int, 128>{}, std::integral_constant<int, 8>{}, no{});
+        return f(std::integral_constant<int, 64>{}, std::integral_constant<int, 4>{}, no{});
     }
 }
 
@@ -502,9 +530,9 @@ int launch_proj(const T* memory, const T* weight, const T* bias, T* value, int64
             DeviceFacts f;
             if (int rc = device_facts(&f, err, err_len)) return rc;
             const ProjShape job{memory, weight, bias, value, B, N, C, H, HD, head_major};
-            return with_tile<T>(proj_tile_width<T>(B, N, HD, f.sm_count), [&](auto bn, auto epi) {
-                return launch_proj_tc<T, decltype(bn)::value, decltype(epi)::value>(job, nullptr, stream, pdl, err,
-                                                                                    err_len);
+            return with_tile<T>(proj_tile_plan<T>(B, N, C, HD, f.sm_count), [&](auto bn, auto epi, auto res) {
+                return launch_proj_tc<T, decltype(bn)::value, decltype(epi)::value, decltype(res)::value>(
+                    job, nullptr, stream, pdl, err, err_len);
             });
         }
     }
@@ -540,8 +568,8 @@ int launch_proj_pair(const ProjShape& j0, const ProjShape& j1, cudaStream_t stre
         DeviceFacts f;
         if (int rc = device_facts(&f, err, err_len)) return rc;
         *paired = true;
-        return with_tile<T>(proj_tile_width<T>(j0.B, j0.N, j0.HD, f.sm_count, j1.B, j1.N, j1.HD),
-                            [&](auto bn, auto epi) {
+        return with_tile<T>(proj_tile_plan<T>(j0.B, j0.N, j0.C, j0.HD, f.sm_count, j1.B, j1.N, j1.HD),
+                            [&](auto bn, auto epi, auto) {
                                 return launch_proj_tc<T, decltype(bn)::value, decltype(epi)::value>(
                                     j0, &j1, stream, pdl, err, err_len);
                             });

@@ -348,14 +348,16 @@ def test_tensor_core_shapes(policy):
 
 
 def test_value_proj_tile_widths(cuda):
-    """The persistent tcgen05 projection at every tile width it picks (64 / 128 / 256 columns; float32 on the
+    """The persistent tcgen05 projection at every tile plan it picks (64 / 128 / 256 columns reloading the weights
+    with every tile; 128 columns with a resident weight slice, for 16-bit types with C <= 256; float32 on the
     three-product TF32 path), with more tiles than SMs so every CTA walks several, ragged last row and column
     tiles and a K that is not a multiple of the 128-byte block; plain and head-major layouts."""
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     g = torch.Generator().manual_seed(11)
-    M = 128 * (sms + 1) + 37  # more 128-row tiles than SMs: the widest tile is picked
+    M = 128 * (sms + 1) + 37  # more 128-row tiles than SMs: resident weights (C <= 256), else the widest tile
     for dtype in (torch.float32, torch.float16, torch.bfloat16):
-        for HD, H, C in ((256, 8, 256), (192, 4, 200), (128, 4, 96), (96, 2, 64), (64, 8, 72)):
+        for HD, H, C in ((256, 8, 256), (192, 4, 200), (128, 4, 96), (96, 2, 64), (64, 8, 72), (256, 8, 320),
+                         (128, 2, 512)):
             if dtype == torch.float32 and C % 4:
                 continue
             mem = (torch.rand(1, M, C, generator=g) * 2 - 1).to(dtype)
