@@ -50,6 +50,9 @@ struct ProjJob {
     // epilogue through TMA stores: boxes of `piece` columns (piece_bytes = piece * sizeof(T) in {16, 32, 64, 128})
     // x 32 tokens, 0 = direct stores
     int tma_store, piece, piece_bytes;
+    // direct32: each thread stores its row's 32-byte pieces straight from registers (value 32-byte aligned, every
+    // 32-byte piece inside one head: D a power of two, D * sizeof(T) a multiple of 32); d_shift = log2(D)
+    int direct32, d_shift;
 };
 
 template <typename T>
@@ -98,7 +101,7 @@ struct ProjTcLayout {
     static constexpr uint32_t kStageBytes = RES ? kABytes : (kABytes + kBBytes) * (kSplit ? 2 : 1);
     static constexpr uint32_t kWBytes = RES ? kResKBlocks * kBBytes : 0;  // the resident weight slice
     static constexpr uint32_t kStgBytes = kTcBM * BN * sizeof(T);  // epilogue staging tile
-    static constexpr uint32_t kBiasBytes = BN * 4;
+    static constexpr uint32_t kBiasBytes = 2 * BN * 4;  // double-buffered: tile tc uses half tc & 1
     static constexpr int kFit = int((kTcSmemBudget - kStgBytes - kBiasBytes - kWBytes) / kStageBytes);
     static constexpr int kStages = kFit < 8 ? kFit : 8;  // two producer lanes a slot: at most 16
     static constexpr uint32_t kWOffset = kStages * kStageBytes;  // 1024-aligned: stage sizes are multiples of 1 KB
@@ -355,6 +358,7 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const C
         const int c_lo = EPI == 8 ? (ew >> 2) * kCols : 0;
         const int r = quarter * 32 + lane;  // tile row = TMEM lane
         const bool any_tma_store = a.job[0].tma_store || (a.job[1].tiles > 0 && a.job[1].tma_store);
+        const uint64_t pol_out = l2_evict_last();  // the sampler reads the projected value right after
         // After a wait that gave up, a warp still walks its tiles and takes part in every named barrier (so no
         // other epilogue warp waits on it), but reads no TMEM and stores nothing.
         bool dead = false;
@@ -372,9 +376,11 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const C
             const int pshift = 31 - __clz(J.piece);  // piece is a power of two
             const int swz = pb / 16 - 1;             // 16-byte chunk index ^= (row * pb / 128) & swz
             if (tc == 0) grid_dependency_wait();  // the dry pass reads and writes no global memory
-            // this tile's bias; the previous tile's readers are past its second barrier
+            // this tile's bias, in the half of the double buffer that tile tc - 2 used: every warp is past that
+            // tile, as no warp has passed this tile's barrier below before all of them finished tile tc - 1
+            float* const tbias = sbias + (tc & 1) * BN;
             for (int i = etid; i < BN; i += kEpiThreads)
-                sbias[i] = (!dry && J.bias != nullptr && c0 + i < J.HD) ? to_acc(J.bias[c0 + i]) : 0.f;
+                tbias[i] = (!dry && J.bias != nullptr && c0 + i < J.HD) ? to_acc(J.bias[c0 + i]) : 0.f;
             // the staging tile is free once the previous tile's stores have read it
             if (any_tma_store) bulk_wait_read();
             named_barrier(1, kEpiThreads);
@@ -384,6 +390,14 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const C
             tc_fence_after();
             const int n = n0 + r;
             const long long m = (long long)b * J.N + n;
+            // first element of this thread's row at output column col (direct stores)
+            auto out_at = [&](int col) -> T* {
+                if (J.head_major) {
+                    const int h = col >> J.d_shift;
+                    return J.value + (((long long)b * J.H + h) * J.N + n) * J.D + (col - (h << J.d_shift));
+                }
+                return J.value + m * J.HD + col;
+            };
 #pragma unroll 1
             for (int j = 0; j < kCols / 32; ++j) {
                 const int cl = c_lo + 32 * j;  // tile column of this chunk
@@ -403,13 +417,14 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const C
                     if (lane == 0) mbar_arrive(&tempty[acc]);
                 }
                 if (!live) continue;
+                uint4 held = make_uint4(0u, 0u, 0u, 0u);  // direct32, 16-bit types: the first half of a piece
 #pragma unroll
                 for (int g = 0; g < 4; ++g) {
                     const int c = cl + 8 * g;  // tile column
                     // the 8 bias values as two 16-byte shared-memory reads (sbias is 16-byte aligned, c a multiple
                     // of 8; every lane reads the same words: broadcast)
-                    const float4 b0 = reinterpret_cast<const float4*>(sbias + c)[0];
-                    const float4 b1 = reinterpret_cast<const float4*>(sbias + c)[1];
+                    const float4 b0 = reinterpret_cast<const float4*>(tbias + c)[0];
+                    const float4 b1 = reinterpret_cast<const float4*>(tbias + c)[1];
                     const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
                     float f[8];
 #pragma unroll
@@ -423,6 +438,16 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const C
                         const int x = (r * pb >> 7) & swz;
 #pragma unroll
                         for (int k = 0; k < kWords; ++k) *reinterpret_cast<uint4*>(row + (((q + k) ^ x) << 4)) = w[k];
+                    } else if (J.direct32) {
+                        // whole 32-byte pieces: 16 columns of a 16-bit type (two groups), 8 of float32 (one group)
+                        if constexpr (kWords == 1) {
+                            if ((g & 1) == 0)
+                                held = w[0];
+                            else if (!dry && n < J.N && c0 + c - 8 < J.HD)
+                                st_global_32b(out_at(c0 + c - 8), held, w[0], pol_out);
+                        } else {
+                            if (!dry && n < J.N && c0 + c < J.HD) st_global_32b(out_at(c0 + c), w[0], w[1], pol_out);
+                        }
                     } else if (!dry && n < J.N && c0 + c < J.HD) {
                         const int col = c0 + c, h = col / J.D;
                         T* dst = J.head_major

@@ -138,6 +138,14 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
                  : "memory");
 }
 
+// 32-byte store from registers (sm_100 256-bit vector store): one whole L2 sector per thread. dst is 32-byte aligned.
+__device__ __forceinline__ void st_global_32b(void* dst, const uint4& lo, const uint4& hi, uint64_t pol) {
+    asm volatile("st.global.L2::cache_hint.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8}, %9;"
+                 ::"l"(dst), "r"(lo.x), "r"(lo.y), "r"(lo.z), "r"(lo.w), "r"(hi.x), "r"(hi.y), "r"(hi.z), "r"(hi.w),
+                   "l"(pol)
+                 : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until every committed bulk store of this thread has finished reading shared memory.
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }

@@ -329,6 +329,10 @@ int allow_smem(K kernel, size_t bytes, std::atomic<uint64_t>& done, char* err, s
     return TD_OK;
 }
 
+#ifndef TD_EPI_DIRECT
+#define TD_EPI_DIRECT 1  // 0: the projection epilogue always stages tiles for TMA stores (for comparison builds)
+#endif
+
 // One projection of the tcgen05 kernel: value[B, N, HD] (or head-major [B, H, N, D]) = memory[B, N, C] @ W^T + b.
 struct ProjShape {
     const void* memory;
@@ -362,8 +366,22 @@ int prepare_proj_tc(const ProjShape& ps, CUtensorMap* map_a, CUtensorMap* map_b,
     // Epilogue boxes: `piece` columns x 32 tokens. Head-major value [B, H, N, D]: a piece is a head, or a 128-byte
     // part of one; [B, N, HD]: 128-byte column groups. The row of a box must be 16, 32, 64 or 128 bytes (the TMA
     // swizzle widths that keep the staging writes free of bank conflicts).
+    // Direct 32-byte stores from the epilogue's registers when every 32-byte piece of a row lies inside one head (and
+    // the value is 32-byte aligned): cheaper than staging the tile in shared memory for TMA stores, which cost about
+    // as much per tile as the MMAs.
+    int direct32 = 0, d_shift = 0;
+    if (TD_EPI_DIRECT && reinterpret_cast<uintptr_t>(value) % 32 == 0 && (HD * e) % 32 == 0) {
+        if (!head_major) {
+            direct32 = 1;
+        } else if ((D & (D - 1)) == 0 && (D * e) % 32 == 0) {
+            direct32 = 1;
+            while ((int64_t(1) << d_shift) < D) ++d_shift;
+        }
+    }
     int piece = 0;
-    if (head_major) {
+    if (direct32) {
+        piece = 0;
+    } else if (head_major) {
         const int64_t db = D * e;
         if (db == 16 || db == 32 || db == 64 || db == 128) piece = int(D);
         else if (db % 128 == 0) piece = int(128 / e);
@@ -391,6 +409,8 @@ int prepare_proj_tc(const ProjShape& ps, CUtensorMap* map_a, CUtensorMap* map_b,
     ProjJob<T>& a = *job;
     a.bias = static_cast<const T*>(ps.bias); a.value = value; a.N = int(N); a.HD = int(HD); a.H = int(H);
     a.D = int(D); a.head_major = head_major;
+    a.direct32 = direct32;
+    a.d_shift = d_shift;
     a.n_tiles = int((HD + BN - 1) / BN);
     a.m_tiles = int((N + kTcBM - 1) / kTcBM);
     a.tiles = int(B * a.m_tiles * a.n_tiles);
