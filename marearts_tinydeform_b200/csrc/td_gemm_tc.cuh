@@ -90,7 +90,9 @@ template <> struct GemmKind<float> {
 // resident-weight 128 x 128 tile reads 64 KB. At most kResKBlocks K blocks (C <= 256 for 16-bit types).
 constexpr int kResKBlocks = 4;
 
-template <typename T, int BN, int EPI, bool RES = false>
+// STG: the layout holds a staging tile for TMA stores (jobs whose output the direct 32-byte stores cannot write);
+// without it the slot ring gets the space.
+template <typename T, int BN, int EPI, bool RES = false, bool STG = true>
 struct ProjTcLayout {
     static constexpr bool kSplit = GemmKind<T>::kSplit;
     static constexpr bool kRes = RES;
@@ -100,7 +102,7 @@ struct ProjTcLayout {
     // a slot: the memory box and (unless the weights are resident) the weight box; float32: + the lo copies
     static constexpr uint32_t kStageBytes = RES ? kABytes : (kABytes + kBBytes) * (kSplit ? 2 : 1);
     static constexpr uint32_t kWBytes = RES ? kResKBlocks * kBBytes : 0;  // the resident weight slice
-    static constexpr uint32_t kStgBytes = kTcBM * BN * sizeof(T);  // epilogue staging tile
+    static constexpr uint32_t kStgBytes = STG ? kTcBM * BN * sizeof(T) : 0;
     static constexpr uint32_t kBiasBytes = 2 * BN * 4;  // double-buffered: tile tc uses half tc & 1
     static constexpr int kFit = int((kTcSmemBudget - kStgBytes - kBiasBytes - kWBytes) / kStageBytes);
     static constexpr int kStages = kFit < 8 ? kFit : 8;  // two producer lanes a slot: at most 16
@@ -121,9 +123,11 @@ struct ProjTcLayout {
     static constexpr int kSplitWarp0 = kEpiWarp0 + EPI;
     static constexpr int kThreads = 32 * (kSplitWarp0 + (kSplit ? 4 : 0));
     static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
-    static_assert(EPI == 4 || EPI == 8, "epilogue warps");
+    static_assert(EPI == 4 || EPI == 8 || EPI == 16, "epilogue warps");
+    static_assert(BN * 4 / EPI >= 32, "every epilogue warp converts whole 32-column chunks");
     static_assert(kStages >= 2, "pipeline depth");
     static_assert(!RES || !kSplit, "resident weights: 16-bit types only");
+    static_assert(!RES || !STG, "resident weights: direct stores only");
     static_assert(kSlotOffset + 16 <= uint32_t(kTcSmemBudget) + 512, "shared memory");
 };
 
@@ -176,12 +180,12 @@ __device__ __forceinline__ void pack8(const float* f, uint4* w) {
 
 // The projection tiles of this CTA, from barrier setup to TMEM release (ends with a CTA-wide barrier; every value
 // store of the CTA has completed by then). smem is the 1024-byte aligned dynamic shared memory.
-template <typename T, int BN, int EPI, bool RES>
+template <typename T, int BN, int EPI, bool RES, bool STG>
 __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const CUtensorMap& map_b0,
                                               const CUtensorMap& map_out0, const CUtensorMap& map_a1,
                                               const CUtensorMap& map_b1, const CUtensorMap& map_out1,
                                               const ProjTcArgs<T>& a, unsigned char* smem) {
-    using Lay = ProjTcLayout<T, BN, EPI, RES>;
+    using Lay = ProjTcLayout<T, BN, EPI, RES, STG>;
     constexpr int S = Lay::kStages;
     constexpr int kBK = Lay::kBK;
     constexpr bool kSplit = Lay::kSplit;
@@ -354,10 +358,10 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const C
         const int etid = threadIdx.x - 32 * Lay::kEpiWarp0;
         const int ew = warp - Lay::kEpiWarp0;
         const int quarter = warp & 3;
-        constexpr int kCols = EPI == 8 ? BN / 2 : BN;  // columns this warp converts
-        const int c_lo = EPI == 8 ? (ew >> 2) * kCols : 0;
+        constexpr int kCols = BN * 4 / EPI;  // columns this warp converts (EPI / 4 warps share each 32-row quarter)
+        const int c_lo = (ew >> 2) * kCols;
         const int r = quarter * 32 + lane;  // tile row = TMEM lane
-        const bool any_tma_store = a.job[0].tma_store || (a.job[1].tiles > 0 && a.job[1].tma_store);
+        const bool any_tma_store = STG && (a.job[0].tma_store || (a.job[1].tiles > 0 && a.job[1].tma_store));
         const uint64_t pol_out = l2_evict_last();  // the sampler reads the projected value right after
         // After a wait that gave up, a warp still walks its tiles and takes part in every named barrier (so no
         // other epilogue warp waits on it), but reads no TMEM and stores nothing.
@@ -431,7 +435,7 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const C
                     for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(v[8 * g + i]) + bb[i];
                     uint4 w[kWords];
                     pack8<T>(f, w);
-                    if (J.tma_store) {
+                    if (STG && J.tma_store) {
                         // piece p = c / piece, 16-byte chunk q within the piece's row r
                         const int p = c >> pshift, q = ((c - (p << pshift)) * int(sizeof(T))) >> 4;
                         unsigned char* row = stg + p * (kTcBM * pb) + r * pb;
@@ -458,7 +462,7 @@ __device__ __forceinline__ void proj_tc_tiles(const CUtensorMap& map_a0, const C
                     }
                 }
             }
-            if (J.tma_store) {
+            if (STG && J.tma_store) {
                 // this warp's boxes -- its columns [c_lo, c_lo + kCols) by its 32 rows -- as soon as it has staged
                 // them, without waiting for the other epilogue warps
                 fence_proxy_async_smem();  // the TMA stores (async proxy) read what these threads wrote
@@ -527,14 +531,14 @@ __device__ __forceinline__ unsigned char* align1024(unsigned char* p) {
 // 72 registers a thread (no spills): 12 warps, 3 per SM sub-partition (27 K registers), leave room on the SM for two
 // CTAs of the sampler that follows in the project order (launched early, under programmatic dependent launch).
 // Tensor maps of job 0 (memory, weight, output) and job 1 (the same; copies of job 0's when there is no job 1).
-template <typename T, int BN, int EPI, bool RES>
+template <typename T, int BN, int EPI, bool RES, bool STG>
 __global__ void __maxnreg__(72)
     proj_tc_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_b0,
                    const __grid_constant__ CUtensorMap map_out0, const __grid_constant__ CUtensorMap map_a1,
                    const __grid_constant__ CUtensorMap map_b1, const __grid_constant__ CUtensorMap map_out1,
                    const ProjTcArgs<T> a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    proj_tc_tiles<T, BN, EPI, RES>(map_a0, map_b0, map_out0, map_a1, map_b1, map_out1, a, align1024(smem_raw));
+    proj_tc_tiles<T, BN, EPI, RES, STG>(map_a0, map_b0, map_out0, map_a1, map_b1, map_out1, a, align1024(smem_raw));
 }
 
 }  // namespace td

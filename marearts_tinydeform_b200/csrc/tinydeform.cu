@@ -333,6 +333,14 @@ int allow_smem(K kernel, size_t bytes, std::atomic<uint64_t>& done, char* err, s
 #define TD_EPI_DIRECT 1  // 0: the projection epilogue always stages tiles for TMA stores (for comparison builds)
 #endif
 
+// Whether the projection epilogue can write value with direct 32-byte stores (ProjJob::direct32): a 32-byte aligned
+// value whose rows split into 32-byte pieces that each lie inside one head (D a power of two, D * e a multiple of 32)
+// when head-major.
+inline bool proj_direct32(const void* value, int64_t HD, int64_t D, int head_major, int64_t e) {
+    if (!TD_EPI_DIRECT || reinterpret_cast<uintptr_t>(value) % 32 != 0 || (HD * e) % 32 != 0) return false;
+    return !head_major || ((D & (D - 1)) == 0 && (D * e) % 32 == 0);
+}
+
 // One projection of the tcgen05 kernel: value[B, N, HD] (or head-major [B, H, N, D]) = memory[B, N, C] @ W^T + b.
 struct ProjShape {
     const void* memory;
@@ -369,15 +377,10 @@ int prepare_proj_tc(const ProjShape& ps, CUtensorMap* map_a, CUtensorMap* map_b,
     // Direct 32-byte stores from the epilogue's registers when every 32-byte piece of a row lies inside one head (and
     // the value is 32-byte aligned): cheaper than staging the tile in shared memory for TMA stores, which cost about
     // as much per tile as the MMAs.
-    int direct32 = 0, d_shift = 0;
-    if (TD_EPI_DIRECT && reinterpret_cast<uintptr_t>(value) % 32 == 0 && (HD * e) % 32 == 0) {
-        if (!head_major) {
-            direct32 = 1;
-        } else if ((D & (D - 1)) == 0 && (D * e) % 32 == 0) {
-            direct32 = 1;
-            while ((int64_t(1) << d_shift) < D) ++d_shift;
-        }
-    }
+    const int direct32 = proj_direct32(value, HD, D, head_major, e) ? 1 : 0;
+    int d_shift = 0;
+    if (direct32 && head_major)
+        while ((int64_t(1) << d_shift) < D) ++d_shift;
     int piece = 0;
     if (direct32) {
         piece = 0;
@@ -420,10 +423,11 @@ int prepare_proj_tc(const ProjShape& ps, CUtensorMap* map_a, CUtensorMap* map_b,
 
 // One launch of the tcgen05 projection kernel for job0 and, when job1 is not null, job1 (same C): job1's tiles
 // follow job0's in the persistent grid. RES: resident weight slices (job0 alone, at most kResKBlocks K blocks).
-template <typename T, int BN, int EPI, bool RES = false>
+// STG = false: no staging tile (every job stores directly).
+template <typename T, int BN, int EPI, bool RES = false, bool STG = true>
 int launch_proj_tc(const ProjShape& job0, const ProjShape* job1, cudaStream_t stream, bool pdl, char* err,
                    size_t err_len) {
-    using Lay = ProjTcLayout<T, BN, EPI, RES>;
+    using Lay = ProjTcLayout<T, BN, EPI, RES, STG>;
     static std::atomic<uint64_t> smem_done{0};
     DeviceFacts f;
     if (int rc = device_facts(&f, err, err_len)) return rc;
@@ -444,13 +448,17 @@ int launch_proj_tc(const ProjShape& job0, const ProjShape* job1, cudaStream_t st
     if (RES && (job1 != nullptr || a.k_blocks > kResKBlocks))
         return fail(err, err_len, TD_ERR_ARG, "resident-weight projection: one job of at most %d K blocks",
                     kResKBlocks);
-    if (int rc = allow_smem(proj_tc_kernel<T, BN, EPI, RES>, Lay::kSmemBytes, smem_done, err, err_len)) return rc;
+    if (!STG && (!a.job[0].direct32 || (job1 != nullptr && !a.job[1].direct32)))
+        return fail(err, err_len, TD_ERR_ARG, "projection without a staging tile: every job must store directly");
+    if (int rc = allow_smem(proj_tc_kernel<T, BN, EPI, RES, STG>, Lay::kSmemBytes, smem_done, err, err_len))
+        return rc;
     // persistent: at most one CTA per SM (the slot ring takes most of the shared memory). With resident weights the
     // grid is a multiple of the channel-tile count, so that every tile of a CTA has the same channel tile (the tile
     // count itself is one, when it is the smaller).
     const int cap = RES ? f.sm_count - f.sm_count % a.job[0].n_tiles : f.sm_count;
     const int grid = a.tiles < cap ? a.tiles : cap;
-    const cudaError_t err_launch = launch_kernel(proj_tc_kernel<T, BN, EPI, RES>, dim3(unsigned(grid)), dim3(Lay::kThreads),
+    const cudaError_t err_launch = launch_kernel(proj_tc_kernel<T, BN, EPI, RES, STG>, dim3(unsigned(grid)),
+                                                 dim3(Lay::kThreads),
                                                  Lay::kSmemBytes, stream, pdl, map_a0, map_b0, map_out0, map_a1,
                                                  map_b1, map_out1, a);
     if (err_launch != cudaSuccess)
@@ -485,59 +493,75 @@ bool proj_tc_eligible(const T* memory, const T* weight, const T* value, int64_t 
     }
 }
 
-// Tile plan of the tcgen05 projection: the busiest CTA runs ceil(tiles / SMs) tiles, each costing about the load
-// of its 128 memory rows (like 128 more output columns) plus the BN weight rows it loads with them; the plan that
-// makes that smallest, the widest of equals. float32 tiles are at most 128 wide (their slots hold hi and lo
-// halves). Resident weights (16-bit types, one job, C within kResKBlocks K blocks; 128 wide): a tile costs its 128
-// memory rows only, and the CTA loads its weight slice once (counted as one more tile's memory rows); they are
-// picked only when strictly cheaper, i.e. when CTAs run several tiles (batch 4 and up at C = 256). (B2, N2, HD2): a
-// second job in the same launch (B2 = 0: none).
+// Tile plan of the tcgen05 projection. Tile width: the busiest CTA runs ceil(tiles / SMs) tiles, each costing about
+// the load of its 128 memory rows (like 128 more output columns) plus the BN weight rows it loads with them; the
+// width that makes that smallest, the widest of equals (float32 tiles are at most 128 wide: their slots hold hi and
+// lo halves). 256-wide tiles get 16 epilogue warps (four per 32-row quarter of the accumulator): the conversion of a
+// 128 x 256 tile is latency-bound, and with 8 warps it paced the tiles (B200, graphs of 50 calls: c3 39.6 -> 35.4 us
+// a call, c4 110.7 -> 103.1, B=2 12.8 -> 12.4). Without a staging tile (every job stores directly) the slot ring
+// takes its space. Resident weights (16-bit types, one job, C within kResKBlocks K blocks, direct stores, 256 wide):
+// when CTAs run at least three tiles, loading the weight slice once beats reloading it with every tile (c3 35.4 ->
+// 35.0 us, c4 103.1 -> 100.1). (B2, N2, HD2): a second job in the same launch (B2 = 0: none). direct: every job can
+// take direct stores.
 struct TilePlan {
     int bn;
     bool res;
+    int epi;
+    bool stg;
 };
 
+#ifndef TD_PROJ_PLAN_BN
+#define TD_PROJ_PLAN_BN 0  // tuning builds: force single-job 16-bit plans to {BN, RES} where the job can take them
+#define TD_PROJ_PLAN_RES 0
+#endif
+
 template <typename T>
-TilePlan proj_tile_plan(int64_t B, int64_t N, int64_t C, int64_t HD, int sm_count, int64_t B2 = 0, int64_t N2 = 0,
-                        int64_t HD2 = 0) {
-    if (TD_PROJ_TILE != 0) return {TD_PROJ_TILE, false};
+TilePlan proj_tile_plan(int64_t B, int64_t N, int64_t C, int64_t HD, int sm_count, bool direct, int64_t B2 = 0,
+                        int64_t N2 = 0, int64_t HD2 = 0) {
+    constexpr bool f32 = std::is_same<T, float>::value;
+    const bool res_fits = !f32 && B2 == 0 && direct && (C + GemmKind<T>::kBK - 1) / GemmKind<T>::kBK <= kResKBlocks;
+    auto finish = [&](int bn, bool res) {
+        return TilePlan{bn, res, bn == 256 ? 16 : (bn == 128 && !f32 ? 8 : 4), !direct || f32};
+    };
+    if (TD_PROJ_TILE != 0) return finish(TD_PROJ_TILE, false);
+    if (TD_PROJ_PLAN_BN != 0 && B2 == 0 && !f32 && (res_fits || !TD_PROJ_PLAN_RES))
+        return finish(TD_PROJ_PLAN_BN, TD_PROJ_PLAN_RES != 0);
     const int64_t m_tiles = B * ((N + kTcBM - 1) / kTcBM);
     const int64_t m_tiles2 = B2 * ((N2 + kTcBM - 1) / kTcBM);
-    TilePlan plan{64, false};
+    int bn = 64;
     long long best = -1;
     for (int w : {256, 128, 64}) {
-        if (std::is_same<T, float>::value && w > 128) continue;
+        if (f32 && w > 128) continue;
         const long long tiles = m_tiles * ((HD + w - 1) / w) + m_tiles2 * ((HD2 + w - 1) / w);
         const long long cost = (tiles + sm_count - 1) / sm_count * (w + 128);
-        if (best < 0 || cost < best) { best = cost; plan = {w, false}; }
+        if (best < 0 || cost < best) { best = cost; bn = w; }
     }
-    if (!std::is_same<T, float>::value && B2 == 0 && (C + GemmKind<T>::kBK - 1) / GemmKind<T>::kBK <= kResKBlocks) {
-        const long long n_tiles = (HD + 127) / 128;
-        const long long grid = sm_count - sm_count % n_tiles;
-        if (grid > 0) {
-            const long long tiles = m_tiles * n_tiles;
-            const long long cost = (tiles + grid - 1) / grid * 128 + 128;
-            if (cost < best) plan = {128, true};
-        }
-    }
-    return plan;
+    const bool res = res_fits && bn == 256 && m_tiles * ((HD + 255) / 256) >= 3LL * sm_count;
+    return finish(bn, res);
 }
 
-// Calls f(std::integral_constant<int, BN>, std::integral_constant<int, EPI>, std::integral_constant<bool, RES>)
-// for the instantiated tile shape of the plan.
+// Calls f(std::integral_constant<int, BN>, std::integral_constant<int, EPI>, std::integral_constant<bool, RES>,
+// std::integral_constant<bool, STG>) for the instantiated kernel of the plan.
 template <typename T, typename F>
 int with_tile(TilePlan plan, F&& f) {
     using no = std::integral_constant<bool, false>;
+    using yes = std::integral_constant<bool, true>;
+    using n64 = std::integral_constant<int, 64>;
+    using n128 = std::integral_constant<int, 128>;
+    using n256 = std::integral_constant<int, 256>;
+    using e4 = std::integral_constant<int, 4>;
+    using e8 = std::integral_constant<int, 8>;
+    using e16 = std::integral_constant<int, 16>;
     if constexpr (std::is_same<T, float>::value) {
-        if (plan.bn >= 128) return f(std::integral_constant<int, 128>{}, std::integral_constant<int, 4>{}, no{});
-        return f(std::integral_constant<int, 64>{}, std::integral_constant<int, 4>{}, no{});
+        if (plan.bn >= 128) return f(n128{}, e4{}, no{}, yes{});
+        return f(n64{}, e4{}, no{}, yes{});
     } else {
-        if (plan.res)
-            return f(std::integral_constant<int, 128>{}, std::integral_constant<int, 8>{},
-                     std::integral_constant<bool, true>{});
-        if (plan.bn == 256) return f(std::integral_constant<int, 256>{}, std::integral_constant<int, 8>{}, no{});
-        if (plan.bn == 128) return f(std::integral_constant<int, 128>{}, std::integral_constant<int, 8>{}, no{});
-        return f(std::integral_constant<int, 64>{}, std::integral_constant<int, 4>{}, no{});
+        if (plan.bn == 256) {
+            if (plan.res) return f(n256{}, e16{}, yes{}, no{});
+            return plan.stg ? f(n256{}, e16{}, no{}, yes{}) : f(n256{}, e16{}, no{}, no{});
+        }
+        if (plan.bn == 128) return plan.stg ? f(n128{}, e8{}, no{}, yes{}) : f(n128{}, e8{}, no{}, no{});
+        return f(n64{}, e4{}, no{}, yes{});
     }
 }
 
@@ -550,10 +574,13 @@ int launch_proj(const T* memory, const T* weight, const T* bias, T* value, int64
             DeviceFacts f;
             if (int rc = device_facts(&f, err, err_len)) return rc;
             const ProjShape job{memory, weight, bias, value, B, N, C, H, HD, head_major};
-            return with_tile<T>(proj_tile_plan<T>(B, N, C, HD, f.sm_count), [&](auto bn, auto epi, auto res) {
-                return launch_proj_tc<T, decltype(bn)::value, decltype(epi)::value, decltype(res)::value>(
-                    job, nullptr, stream, pdl, err, err_len);
-            });
+            const bool direct = proj_direct32(value, HD, HD / H, head_major, int64_t(sizeof(T)));
+            return with_tile<T>(proj_tile_plan<T>(B, N, C, HD, f.sm_count, direct),
+                                [&](auto bn, auto epi, auto res, auto stg) {
+                                    return launch_proj_tc<T, decltype(bn)::value, decltype(epi)::value,
+                                                          decltype(res)::value, decltype(stg)::value>(
+                                        job, nullptr, stream, pdl, err, err_len);
+                                });
         }
     }
     ProjArgs<T> a;
@@ -588,9 +615,14 @@ int launch_proj_pair(const ProjShape& j0, const ProjShape& j1, cudaStream_t stre
         DeviceFacts f;
         if (int rc = device_facts(&f, err, err_len)) return rc;
         *paired = true;
-        return with_tile<T>(proj_tile_plan<T>(j0.B, j0.N, j0.C, j0.HD, f.sm_count, j1.B, j1.N, j1.HD),
-                            [&](auto bn, auto epi, auto) {
-                                return launch_proj_tc<T, decltype(bn)::value, decltype(epi)::value>(
+        const bool direct =
+            proj_direct32(j0.value, j0.HD, j0.HD / j0.H, j0.head_major, int64_t(sizeof(T))) &&
+            proj_direct32(j1.value, j1.HD, j1.HD / j1.H, j1.head_major, int64_t(sizeof(T)));
+        return with_tile<T>(proj_tile_plan<T>(j0.B, j0.N, j0.C, j0.HD, f.sm_count, direct, j1.B, j1.N, j1.HD),
+                            [&](auto bn, auto epi, auto res, auto stg) {
+                                // a paired launch never takes resident weights (the plan gives res = false)
+                                return launch_proj_tc<T, decltype(bn)::value, decltype(epi)::value, false,
+                                                      decltype(stg)::value || decltype(res)::value>(
                                     j0, &j1, stream, pdl, err, err_len);
                             });
     } else {

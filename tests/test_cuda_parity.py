@@ -348,29 +348,33 @@ def test_tensor_core_shapes(policy):
 
 
 def test_value_proj_tile_widths(cuda):
-    """The persistent tcgen05 projection at every tile plan it picks (64 / 128 / 256 columns reloading the weights
-    with every tile; 128 columns with a resident weight slice, for 16-bit types with C <= 256; float32 on the
-    three-product TF32 path), with more tiles than SMs so every CTA walks several, ragged last row and column
-    tiles and a K that is not a multiple of the 128-byte block; plain and head-major layouts."""
+    """The persistent tcgen05 projection at every tile plan it picks: 64 / 128 / 256 columns reloading the weights
+    with every tile (with a staging tile for TMA stores, or storing straight from registers), 256 columns with a
+    resident weight slice (16-bit types, C <= 256, at least three tiles per CTA), float32 on the three-product TF32
+    path; more tiles than SMs so every CTA walks several, ragged last row and column tiles and a K that is not a
+    multiple of the 128-byte block; plain and head-major layouts (head-major D = 24 / 36 cannot store directly)."""
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     g = torch.Generator().manual_seed(11)
-    M = 128 * (sms + 1) + 37  # more 128-row tiles than SMs: resident weights (C <= 256), else the widest tile
+    shapes = ((256, 8, 256), (192, 4, 200), (128, 4, 96), (96, 2, 64), (64, 8, 72), (256, 8, 320), (128, 2, 512),
+              (192, 8, 256), (144, 4, 128))
     for dtype in (torch.float32, torch.float16, torch.bfloat16):
-        for HD, H, C in ((256, 8, 256), (192, 4, 200), (128, 4, 96), (96, 2, 64), (64, 8, 72), (256, 8, 320),
-                         (128, 2, 512)):
-            if dtype == torch.float32 and C % 4:
-                continue
-            mem = (torch.rand(1, M, C, generator=g) * 2 - 1).to(dtype)
-            w = ((torch.rand(HD, C, generator=g) * 2 - 1) * 0.1).to(dtype)
-            b = ((torch.rand(HD, generator=g) * 2 - 1) * 0.05).to(dtype)
-            ref = mem[0].double() @ w.double().T + b.double()
-            with torch.inference_mode():
-                got = _native.value_proj(mem.cuda(), w.cuda(), b.cuda(), H)
-                hm = _native.value_proj(mem.cuda(), w.cuda(), b.cuda(), H, head_major=True)
-            atol, rtol = TOL[dtype]
-            err = (got[0].double().cpu() - ref).abs().max().item()
-            assert torch.allclose(got[0].double().cpu(), ref, atol=atol, rtol=rtol), f'{dtype} HD{HD} C{C}: {err:.3g}'
-            assert torch.equal(hm.permute(0, 2, 1, 3).reshape(got.shape), got), f'{dtype} HD{HD} C{C} head-major'
+        # more 128-row tiles than SMs; 16-bit types also with three 256-wide tiles per SM (resident weights)
+        for M in ((128 * (sms + 1) + 37,) if dtype == torch.float32 else (128 * (sms + 1) + 37, 128 * 3 * sms + 101)):
+            for HD, H, C in shapes:
+                if dtype == torch.float32 and C % 4:
+                    continue
+                mem = (torch.rand(1, M, C, generator=g) * 2 - 1).to(dtype).cuda()
+                w = ((torch.rand(HD, C, generator=g) * 2 - 1) * 0.1).to(dtype).cuda()
+                b = ((torch.rand(HD, generator=g) * 2 - 1) * 0.05).to(dtype).cuda()
+                ref = mem[0].double() @ w.double().T + b.double()
+                with torch.inference_mode():
+                    got = _native.value_proj(mem, w, b, H)
+                    hm = _native.value_proj(mem, w, b, H, head_major=True)
+                atol, rtol = TOL[dtype]
+                err = (got[0].double() - ref).abs().max().item()
+                tag = f'{dtype} M{M} HD{HD} C{C}'
+                assert torch.allclose(got[0].double(), ref, atol=atol, rtol=rtol), f'{tag}: {err:.3g}'
+                assert torch.equal(hm.permute(0, 2, 1, 3).reshape(got.shape), got), f'{tag} head-major'
     torch.cuda.synchronize()
     assert _native.device_error(clear=True) == 0
 
