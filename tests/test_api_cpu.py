@@ -101,7 +101,8 @@ def test_tensor_contract_rejects_cpu_tensors_in_the_native_path():
 
 def test_b200_table_picks_the_measured_faster_order(monkeypatch):
     """The sm_100 table on the BASELINE shapes: 'project' for every BASELINE config (float32 included: its
-    projection runs on the tensor cores too), 'fused' only for few queries at batch >= 4-8."""
+    projection runs on the tensor cores too), 'fused' only for float32 with few queries at batch >= 4-8 (in 16-bit
+    types the project order measured faster across the whole sweep, batch 8 with 50 queries included)."""
     from marearts_tinydeform_b200 import workloads
     monkeypatch.setattr(td, '_limits', lambda device_index: td.FUSED_LIMIT_SM100)
 
@@ -120,7 +121,8 @@ def test_b200_table_picks_the_measured_faster_order(monkeypatch):
     assert pick('c2') == 'project'
     assert pick('c3') == 'project'
     assert pick('c4') == 'project'
-    assert pick('c1h', B=8, Q=50) == 'fused'
+    assert pick('c1h', B=8, Q=50) == 'project'
+    assert pick('c3', Q=50) == 'project'
     assert pick('c1', Q=300) == 'project'
     assert pick('c1', B=8, Q=100) == 'fused'
     assert pick('c1', B=4, Q=100) == 'project'
