@@ -36,8 +36,31 @@ struct SampleArgs {
 
 constexpr int kSampleWarps = 8;
 
-// what a corner outside the map reads (16 bytes of zeros)
+// what a corner outside the map reads (16 or 32 bytes of zeros)
 __device__ __align__(16) const uint4 g_zero16 = {0u, 0u, 0u, 0u};
+__device__ __align__(32) const uint4 g_zero32[2] = {{0u, 0u, 0u, 0u}, {0u, 0u, 0u, 0u}};
+
+// Read-only loads of corner rows. kNoAlloc: without L1 allocation -- on the DINO shape (91 MB of value, most of the
+// 126 MB L2) the gather measured 5 % faster that way, while on the RT-DETR shapes (4-34 MB) it was 0.2-0.3 us
+// slower, so the host picks it by the size of the value.
+template <bool kNoAlloc>
+__device__ __forceinline__ void ld_corner(const void* p, uint4 (&r)[1]) {
+    if constexpr (kNoAlloc) {
+        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(r[0].x), "=r"(r[0].y), "=r"(r[0].z), "=r"(r[0].w)
+                     : "l"(p));
+    } else {
+        r[0] = __ldg(static_cast<const uint4*>(p));
+    }
+}
+// 32 bytes (sm_100 256-bit load), never allocating in L1; p is 32-byte aligned
+template <bool kNoAlloc>
+__device__ __forceinline__ void ld_corner(const void* p, uint4 (&r)[2]) {
+    asm volatile("ld.global.nc.L1::no_allocate.v8.u32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0].x), "=r"(r[0].y), "=r"(r[0].z), "=r"(r[0].w), "=r"(r[1].x), "=r"(r[1].y), "=r"(r[1].z),
+                   "=r"(r[1].w)
+                 : "l"(p));
+}
 
 // Dynamic shared memory of the vector kernel: per warp, S = 4 L P corner tokens and weights.
 template <typename T>
@@ -80,15 +103,17 @@ __device__ __forceinline__ void sample_row_corners(const SampleArgs<T>& a, long 
     }
 }
 
-// out[row] = sum over the row's corners of weight * value[token] (head slice): G lanes per corner row, 16-byte
-// vectors, kBatch corner rows in flight per lane, groups summed with an xor butterfly. kCoherent reads value
-// through L2 only (ld.global.cg), for a value written earlier by the same kernel.
-template <typename T, bool kCoherent>
+// out[row] = sum over the row's corners of weight * value[token] (head slice): G lanes per corner row, each loading
+// 16 bytes of it (kWide: 32 bytes, for rows of 128 bytes and more -- half the load instructions, which measured 16 %
+// faster on the stress shape's 128-byte rows and made no difference on 64-byte rows), kBatch corner rows in flight
+// per lane, the lanes' groups summed with an xor butterfly.
+template <typename T, bool kWide, bool kNoAlloc>
 __device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long long row, int lane, const int* s_tok,
                                                   const typename Coord<T>::type* s_wt) {
     using A = typename Elem<T>::acc;
-    constexpr int V = Elem<T>::kVec;
-    constexpr int kBatch = 8;  // corner rows in flight per lane
+    constexpr int V = Elem<T>::kVec;         // elements per 16-byte word
+    constexpr int kWords = kWide ? 2 : 1;    // 16-byte words per lane and corner row
+    constexpr int kBatch = kWide ? 4 : 8;    // corner rows in flight per lane
     const int S = 4 * a.L * a.P;
     int h;
     long long b;
@@ -102,35 +127,42 @@ __device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long l
     }
     const T* vb = a.value + b * a.s_img + (long long)h * a.s_head;
     const int G = a.G, CG = 32 / G, cg = lane / G, v = lane - cg * G;
-    A acc[V];
+    A acc[kWords * V];
 #pragma unroll
-    for (int i = 0; i < V; ++i) acc[i] = A(0);
+    for (int i = 0; i < kWords * V; ++i) acc[i] = A(0);
     for (int s0 = cg; s0 < S; s0 += kBatch * CG) {
-        uint4 raw[kBatch];
+        uint4 raw[kBatch][kWords];
         A w[kBatch];
         // every load of the batch is issued unconditionally (no branch between them, so they are all in flight
-        // together): a corner outside the map, or past the row's last, reads a 16-byte word of zeros
+        // together): a corner outside the map, or past the row's last, reads a word of zeros
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
             const int s = s0 + u * CG;
             const int t = s < S ? s_tok[s] : -1;
             w[u] = t < 0 ? A(0) : A(s_wt[s]);
-            const uint4* src = t < 0 ? &g_zero16 : reinterpret_cast<const uint4*>(vb + (long long)t * a.s_tok + v * V);
-            raw[u] = kCoherent ? __ldcg(src) : __ldg(src);
+            const void* src = t < 0 ? static_cast<const void*>(g_zero32)
+                                    : static_cast<const void*>(vb + (long long)t * a.s_tok + v * kWords * V);
+            ld_corner<kNoAlloc>(src, raw[u]);
         }
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
-            A x[V];
-            unpack16<T>(raw[u], x);
 #pragma unroll
-            for (int i = 0; i < V; ++i) acc[i] = fma(w[u], x[i], acc[i]);
+            for (int k = 0; k < kWords; ++k) {
+                A x[V];
+                unpack16<T>(raw[u][k], x);
+#pragma unroll
+                for (int i = 0; i < V; ++i) acc[k * V + i] = fma(w[u], x[i], acc[k * V + i]);
+            }
         }
     }
     for (int o = G; o < 32; o <<= 1) {
 #pragma unroll
-        for (int i = 0; i < V; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+        for (int i = 0; i < kWords * V; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
     }
-    if (cg == 0) store16<T>(a.out + row * a.D + v * V, acc);
+    if (cg == 0) {
+#pragma unroll
+        for (int k = 0; k < kWords; ++k) store16<T>(a.out + row * a.D + (v * kWords + k) * V, acc + k * V);
+    }
 }
 
 // With prod.proj set, the corners come from the query projection (produce_row). Either that projection ran in the
@@ -139,12 +171,13 @@ __device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long l
 // value projection -> this kernel): the value projection, launched with programmatic serialization, lets this
 // kernel start only after its own grid dependency wait has seen the query projection complete, so the corner
 // prologue may read proj before this kernel's own wait.
-// Vector kernel: needs D * sizeof(T) % 16 == 0, D * sizeof(T) <= 512, 16-byte aligned value/out and strides.
+// Vector kernel: needs D * sizeof(T) % 16 == 0, D * sizeof(T) <= 512, 16-byte aligned value/out and strides (kWide:
+// D * sizeof(T) a multiple of 32, 32-byte aligned value and strides).
 // The dependent-latency chain is kept to two memory round trips: (level geometry + locations + attention weights,
 // all issued together) -> corners -> (every corner row of the lane's group issued together) -> butterfly -> store.
 // When launched with programmatic serialization right after the projection kernel, everything before
 // grid_dependency_wait() overlaps that kernel; value is only read after it.
-template <typename T>
+template <typename T, bool kWide, bool kNoAlloc>
 __global__ void __launch_bounds__(kSampleWarps * 32) sample_vec_kernel(const SampleArgs<T> a) {
     using CT = typename Coord<T>::type;
     // per warp: S corner tokens, then S corner weights (dynamic, sample_vec_smem bytes, so that the CTAs stay small
@@ -163,7 +196,7 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_vec_kernel(const Sam
     __syncwarp();
     grid_dependency_wait();
     if (!live) return;
-    sample_row_gather<T, false>(a, row, lane, s_tok, s_wt);
+    sample_row_gather<T, kWide, kNoAlloc>(a, row, lane, s_tok, s_wt);
 }
 
 // Generic kernel: lanes over the head's D channels, scalar loads.

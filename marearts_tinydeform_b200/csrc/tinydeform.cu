@@ -46,6 +46,7 @@ int check_launch(char* err, size_t err_len, const char* what) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
 
 size_t dtype_size(int dtype) {
     switch (dtype) {
@@ -133,13 +134,25 @@ int launch_sampler(const T* value, long long s_img, long long s_tok, long long s
                      aligned16(out) &&
                      (s_img * (long long)sizeof(T)) % 16 == 0 && (s_tok * (long long)sizeof(T)) % 16 == 0 &&
                      (s_head * (long long)sizeof(T)) % 16 == 0;
+    // 32-byte loads for rows of 128 bytes and more (G = row_bytes / 32 lanes a row, still a power of two)
+    const bool wide = vec && row_bytes % 32 == 0 && row_bytes >= 128 && aligned32(value) &&
+                      (s_img * (long long)sizeof(T)) % 32 == 0 && (s_tok * (long long)sizeof(T)) % 32 == 0 &&
+                      (s_head * (long long)sizeof(T)) % 32 == 0;
+    if (wide) a.G = int(row_bytes / 32);
     const unsigned grid = unsigned((a.rows + kSampleWarps - 1) / kSampleWarps);
     // Right after td_project_forward's projection kernel, launch with programmatic stream serialization: the
     // sampler's corner prologue then overlaps the projection, and it waits for it before reading value.
-    cudaError_t e = vec ? launch_kernel(sample_vec_kernel<T>, dim3(grid), dim3(kSampleWarps * 32),
-                                        sample_vec_smem<T>(int(L), int(P)), stream, after_producer, a)
-                        : launch_kernel(sample_generic_kernel<T>, dim3(grid), dim3(kSampleWarps * 32), 0, stream,
-                                        after_producer, a);
+    const size_t smem = sample_vec_smem<T>(int(L), int(P));
+    // corner loads without L1 allocation when the value is large against L2 (more than 64 MB)
+    const bool no_alloc = vec && B * H * N * D * (long long)sizeof(T) > (64LL << 20);
+    cudaError_t e = wide       ? launch_kernel(sample_vec_kernel<T, true, true>, dim3(grid), dim3(kSampleWarps * 32),
+                                               smem, stream, after_producer, a)
+                    : no_alloc ? launch_kernel(sample_vec_kernel<T, false, true>, dim3(grid),
+                                               dim3(kSampleWarps * 32), smem, stream, after_producer, a)
+                    : vec      ? launch_kernel(sample_vec_kernel<T, false, false>, dim3(grid),
+                                               dim3(kSampleWarps * 32), smem, stream, after_producer, a)
+                          : launch_kernel(sample_generic_kernel<T>, dim3(grid), dim3(kSampleWarps * 32), 0, stream,
+                                          after_producer, a);
     if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "sampler launch: %s", cudaGetErrorString(e));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return check_launch(err, err_len, vec ? "sample_vec_kernel" : "sample_generic_kernel");
