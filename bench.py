@@ -203,17 +203,30 @@ def run_reference_arm(args):
     rank = int(os.environ.get('RANK', '0'))
     if rank != 0:
         return
-    us, threads, n = cpu_time_us(args.config, budget_s=max(5.0, min(60.0, 0.05 * (args.steps + args.warmup))),
-                                 max_calls=args.steps + args.warmup)
+    # exactly W untimed and K timed calls of the CPU path (the upstream algorithm on torch's CPU operators, all host
+    # threads), one call of the workload per step
+    from oracle import deform_oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    inputs = workloads.make_inputs(args.config, seed=0)
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            deform_oracle.torch_port(*inputs)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            deform_oracle.torch_port(*inputs)
+        us = (time.perf_counter() - t0) / max(1, args.steps) * 1e6
+    n = args.steps
     cfg = workloads.CONFIGS[args.config]
     line = {
         'metric': METRIC, 'value': round(us, 2), 'unit': 'us', 'impl': 'reference', 'n_gpus': args.gpus,
-        'steps': n, 'warmup': 2, 'ms_per_step': round(us / 1e3, 4), 'higher_is_better': False,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(us / 1e3, 4), 'higher_is_better': False,
         'scaling': 'weak', 'vs_baseline': None, 'dtype': str(cfg['dtype']).replace('torch.', ''),
         'data': 'synthetic (seeded, BASELINE config shapes)',
         'config': config_dict(args.config, 1, args.mode, 'CPU'),
         'cpu_baseline': {'value': round(us, 2), 'unit': 'us', 'cores': threads, 'kind': 'port',
-                         'sample': f'{n} calls of {args.config} (B=1), median, torch CPU ops, {threads} threads'},
+                         'sample': f'{n} timed calls of {args.config} (B={cfg["B"]}), mean, torch CPU ops, '
+                                   f'{threads} threads'},
         'e2e': {'value': round(us, 2), 'unit': 'us', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
     print(json.dumps(line), flush=True)
