@@ -8,17 +8,19 @@
 // once):
 //   * warp 0, two lanes per slot: TMA producers -- per tile and per 128-byte-wide K block, the 128-token slice of
 //     memory (lane 2s) and the BN-row slice of W (lane 2s + 1), K-major with 128-byte swizzle, into slot s of a ring
-//     of kStages shared-memory slots. The TMA operations of one issuing thread are served one after another (about
-//     0.15-0.3 us each on B200, whatever their size) while those of different threads overlap, so every box of a
-//     ring round has its own issuer; a lane walks its slot's rounds in order (so a parity wait on the slot's barrier
-//     never runs two phases ahead) and polls without blocking, so a slot that is not free yet holds up no other;
-//   * EPI warps from warp 4 on: epilogue -- tcgen05.ld of the accumulator (TMEM lane = tile row; warp w reads
-//     lanes 32 (w % 4) .. + 31, and with 8 warps each takes half of the columns), + bias (staged in shared memory),
-//     narrowed to T and written into a staging tile laid out as the output's boxes (TMA swizzle, so the 16-byte
-//     writes of a warp hit distinct banks); the accumulator is handed back as soon as it is read, and each warp
-//     writes its own 32-row boxes with TMA tensor stores as soon as it has staged them -- whole lines, where
-//     per-thread row stores would write half sectors. Shapes whose boxes cannot be described that way store straight
-//     from registers instead;
+//     of kStages shared-memory slots (memory with an L2 evict_first hint, W evict_last). The TMA operations of one
+//     issuing thread are served one after another (about 0.15-0.3 us each on B200, whatever their size) while those
+//     of different threads overlap, so every box of a ring round has its own issuer; a lane walks its slot's rounds
+//     in order (so a parity wait on the slot's barrier never runs two phases ahead) and polls without blocking, so a
+//     slot that is not free yet holds up no other. RES (resident weights): lane s loads only memory boxes, and
+//     lanes S .. S + KB - 1 load the CTA's weight slice once;
+//   * EPI warps from warp 4 on (8, or 16 for 256-wide tiles): epilogue -- tcgen05.ld of the accumulator (TMEM lane =
+//     tile row; warp w reads lanes 32 (w % 4) .. + 31, and the EPI / 4 warps of a quarter split its columns), + bias
+//     (double-buffered in shared memory), narrowed to T, and either stored straight from registers as 32-byte
+//     pieces (direct32: each piece one whole L2 sector, evict_last, so the sampler finds the value in L2) or, for
+//     outputs whose pieces would straddle heads, written into a staging tile laid out as the output's boxes (TMA
+//     swizzle) and stored with TMA tensor stores by each warp as soon as it has staged them. The accumulator is
+//     handed back as soon as it is read. STG = false: no staging tile (every job stores directly);
 //   * warp 3, one thread: MMA issuer -- four K steps per block (tcgen05.mma, M = 128, N = BN) into one of two TMEM
 //     accumulators (2 x BN float32 columns), so the epilogue of one tile runs under the MMAs of the next;
 //   * float32 only, four more warps: split -- every landed slot is rewritten as hi = x with its 13 low mantissa bits

@@ -3,8 +3,9 @@
 // Same result as upstream sample_kernel (csrc/ma_deform_fused.cu:212-233), laid out for B200:
 //   * one warp per (batch, query, head) row; the row's levels x points x 4 corners are computed once, by lanes in
 //     parallel, into shared memory;
-//   * the head slice of a corner row (D * e bytes) is read as G 16-byte vectors by G lanes, so one warp keeps 32/G
-//     corner rows in flight at a time, and the corner groups are summed with xor shuffles at the end;
+//   * the head slice of a corner row (D * e bytes) is read as G 16-byte vectors by G lanes (rows of 128 bytes and
+//     more: 32-byte vectors, sm_100's 256-bit loads), so one warp keeps 32/G corner rows in flight at a time, and the
+//     corner groups are summed with xor shuffles at the end; when the value is large against L2 the loads skip L1;
 //   * value is addressed through (image, token, head) strides, so the same kernel reads the nn.Linear layout
 //     [B, N, H*D] and the head-major [B, H, N, D] layout the projection kernel writes (x-adjacent corners are then
 //     adjacent D-rows in memory).
