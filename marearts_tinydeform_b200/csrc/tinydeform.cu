@@ -469,6 +469,9 @@ int launch_proj_tc(const ProjShape& job0, const ProjShape* job1, cudaStream_t st
     // grid is a multiple of the channel-tile count, so that every tile of a CTA has the same channel tile (the tile
     // count itself is one, when it is the smaller).
     const int cap = RES ? f.sm_count - f.sm_count % a.job[0].n_tiles : f.sm_count;
+    if (cap <= 0)
+        return fail(err, err_len, TD_ERR_ARG, "resident-weight projection: %d channel tiles do not fit %d SMs",
+                    a.job[0].n_tiles, f.sm_count);
     const int grid = a.tiles < cap ? a.tiles : cap;
     const cudaError_t err_launch = launch_kernel(proj_tc_kernel<T, BN, EPI, RES, STG>, dim3(unsigned(grid)),
                                                  dim3(Lay::kThreads),
@@ -549,7 +552,9 @@ TilePlan proj_tile_plan(int64_t B, int64_t N, int64_t C, int64_t HD, int sm_coun
         const long long cost = (tiles + sm_count - 1) / sm_count * (w + 128);
         if (best < 0 || cost < best) { best = cost; bn = w; }
     }
-    const bool res = res_fits && bn == 256 && m_tiles * ((HD + 255) / 256) >= 3LL * sm_count;
+    // (the grid of a resident-weight launch is a multiple of the channel-tile count, so that count must fit the SMs)
+    const bool res = res_fits && bn == 256 && (HD + 255) / 256 <= sm_count &&
+                     m_tiles * ((HD + 255) / 256) >= 3LL * sm_count;
     return finish(bn, res);
 }
 
