@@ -236,9 +236,11 @@ TD_API int td_project_forward_masked(int dtype, const void* memory, const void* 
  * are rejected with TD_ERR_WORKSPACE and a message naming both sizes; the RT-DETR 640x640 layer (B=1, N=8400,
  * H*D=256) needs 4.3 MB in 16-bit types and 8.6 MB in float32.
  * The first call on a device looks up the array's device address (cudaGetSymbolAddress) with that device current;
- * make that first call before any stream capture on the device. The array is shared by all calls and keeps the
- * last call's contents; it is fully rewritten before it is read, so nothing needs clearing. Calls whose work
- * overlaps on the GPU (other streams, other threads) race on it: serialise them.
+ * make that first call before any stream capture on the device. A first call made while its stream is capturing
+ * is refused with TD_ERR_CUDA (nothing is launched or recorded); a failed lookup is not remembered, so a later call
+ * tries again. Arguments are checked before the lookup. The array is shared by all calls and keeps the last call's
+ * contents; it is fully rewritten before it is read, so nothing needs clearing. Calls whose work overlaps on the
+ * GPU (other streams, other threads) race on it: serialise them.
  */
 #define TD_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
 TD_API int td_project_forward_noalloc(int dtype, const void* memory, const void* value_weight, const void* value_bias,
@@ -246,6 +248,17 @@ TD_API int td_project_forward_noalloc(int dtype, const void* memory, const void*
                                       const void* sampling_locations, const void* attention_weights, void* out,
                                       int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H, int64_t HD, int64_t L,
                                       int64_t P, void* stream, char* err, size_t err_len);
+
+/*
+ * Measurement kernel (no counterpart in upstream): reads `visits` pseudo-random rows of row_bytes (a power of two,
+ * 16..512; 32..512 with wide = 1, which uses 32-byte loads) from buf ([rows, row_bytes], 16- or 32-byte aligned)
+ * with every SM, the way the sampler reads corner rows, and writes one 16-byte word per thread into sink
+ * (sink_bytes >= grid * 256 * 16). visits must be a multiple of grid * 8 * (32 / lanes per row) * (wide ? 4 : 8);
+ * the message of a rejected call names the multiple. Timing it over an L2-resident buffer gives the L2 random-row
+ * gather rate the gather kernels' roofline is measured against (bench.py --l2-peak).
+ */
+TD_API int td_probe_row_gather(const void* buf, int64_t rows, int row_bytes, int wide, int64_t visits, unsigned seed,
+                               void* sink, size_t sink_bytes, int grid, void* stream, char* err, size_t err_len);
 
 /*
  * Kernel policy for every later call in this process: TD_POLICY_BEST (default) uses the tcgen05 tensor-core

@@ -22,6 +22,7 @@
 #include "td_producer.cuh"
 #include "td_backward.cuh"
 #include "td_sampler.cuh"
+#include "td_probe.cuh"
 
 namespace td {
 namespace {
@@ -65,24 +66,34 @@ struct DeviceFacts {
 };
 
 constexpr int kMaxDevices = 64;
-std::once_flag g_dev_once[kMaxDevices];
+std::atomic<bool> g_dev_known[kMaxDevices];
 DeviceFacts g_dev[kMaxDevices];
+std::mutex g_dev_mutex;
 
 int device_facts(DeviceFacts* out, char* err, size_t err_len) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
     if (dev < 0 || dev >= kMaxDevices) return fail(err, err_len, TD_ERR_CUDA, "device index %d out of range", dev);
-    std::call_once(g_dev_once[dev], [dev] {
-        DeviceFacts f;
-        cudaDeviceGetAttribute(&f.sm_count, cudaDevAttrMultiProcessorCount, dev);
-        cudaDeviceGetAttribute(&f.major, cudaDevAttrComputeCapabilityMajor, dev);
-        cudaDeviceGetAttribute(&f.minor, cudaDevAttrComputeCapabilityMinor, dev);
-        cudaDeviceGetAttribute(&f.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-        g_dev[dev] = f;
-    });
+    if (!g_dev_known[dev].load(std::memory_order_acquire)) {
+        // stored only once every query has succeeded; a failed query is retried by the next call
+        std::lock_guard<std::mutex> lock(g_dev_mutex);
+        if (!g_dev_known[dev].load(std::memory_order_relaxed)) {
+            DeviceFacts f;
+            e = cudaDeviceGetAttribute(&f.sm_count, cudaDevAttrMultiProcessorCount, dev);
+            if (e == cudaSuccess) e = cudaDeviceGetAttribute(&f.major, cudaDevAttrComputeCapabilityMajor, dev);
+            if (e == cudaSuccess) e = cudaDeviceGetAttribute(&f.minor, cudaDevAttrComputeCapabilityMinor, dev);
+            if (e == cudaSuccess)
+                e = cudaDeviceGetAttribute(&f.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+            if (e != cudaSuccess || f.sm_count <= 0) {
+                cudaGetLastError();
+                return fail(err, err_len, TD_ERR_CUDA, "could not query device %d: %s", dev, cudaGetErrorString(e));
+            }
+            g_dev[dev] = f;
+            g_dev_known[dev].store(true, std::memory_order_release);
+        }
+    }
     *out = g_dev[dev];
-    if (out->sm_count <= 0) return fail(err, err_len, TD_ERR_CUDA, "could not query device %d", dev);
     return TD_OK;
 }
 
@@ -281,20 +292,40 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
+// cuTensorMapEncodeTiled on the calling thread. A thread on which the CUDA runtime has not yet made a context
+// current (autograd's worker thread, for one, when its device is the runtime's default) gets
+// CUDA_ERROR_INVALID_CONTEXT from the driver; the thread's current device's primary context is then made current
+// (cudaSetDevice, no stream work, legal during capture) and the encoding tried once more.
+CUresult encode_tiled(CUtensorMap* map, CUtensorMapDataType type, cuuint32_t rank, void* base,
+                      const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
+                      const cuuint32_t* estr, CUtensorMapSwizzle swizzle) {
+    auto encode = tensor_map_encoder();
+    if (encode == nullptr) return CUDA_ERROR_NOT_FOUND;
+    CUresult r = encode(map, type, rank, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r == CUDA_ERROR_INVALID_CONTEXT) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess)
+            r = encode(map, type, rank, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        cudaGetLastError();
+    }
+    return r;
+}
+
 // 2-D row-major tensor [rows, cols] of 16-bit (or 32-bit) elements, 128-byte-swizzled boxes of box_rows rows x
 // 128 bytes (64 or 32 elements).
 int tensor_map_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows, char* err,
                   size_t err_len, uint32_t elem_bytes) {
-    auto encode = tensor_map_encoder();
-    if (encode == nullptr) return fail(err, err_len, TD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    if (tensor_map_encoder() == nullptr)
+        return fail(err, err_len, TD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     const cuuint64_t dims[2] = {cols, rows};
     const cuuint64_t strides[1] = {cols * elem_bytes};
     const cuuint32_t box[2] = {128u / elem_bytes, box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUtensorMapDataType type = elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
-    const CUresult r = encode(map, type, 2, const_cast<void*>(base), dims, strides, box, estr,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUresult r = encode_tiled(map, type, 2, const_cast<void*>(base), dims, strides, box, estr,
+                                    CU_TENSOR_MAP_SWIZZLE_128B);
     if (r != CUDA_SUCCESS) return fail(err, err_len, TD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
     return TD_OK;
 }
@@ -303,15 +334,14 @@ int tensor_map_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t ro
 // the given shared-memory swizzle.
 int tensor_map_3d(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
                   const uint32_t box[3], uint32_t elem_bytes, CUtensorMapSwizzle swizzle, char* err, size_t err_len) {
-    auto encode = tensor_map_encoder();
-    if (encode == nullptr) return fail(err, err_len, TD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    if (tensor_map_encoder() == nullptr)
+        return fail(err, err_len, TD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     const cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
     const cuuint64_t st[2] = {strides[0], strides[1]};
     const cuuint32_t bx[3] = {box[0], box[1], box[2]};
     const cuuint32_t estr[3] = {1, 1, 1};
     const CUtensorMapDataType type = elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
-    const CUresult r = encode(map, type, 3, const_cast<void*>(base), d, st, bx, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUresult r = encode_tiled(map, type, 3, const_cast<void*>(base), d, st, bx, estr, swizzle);
     if (r != CUDA_SUCCESS) return fail(err, err_len, TD_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d)", int(r));
     return TD_OK;
 }
@@ -1185,9 +1215,44 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[TD_NOALLOC_SCRA
 
 namespace td {
 namespace {
-std::once_flag g_scratch_once[kMaxDevices];
-void* g_scratch_ptr[kMaxDevices];
-cudaError_t g_scratch_status[kMaxDevices];
+// The scratch array's device address per device, stored only once a lookup has succeeded (a failed lookup leaves
+// nullptr, and the next call tries again).
+std::atomic<void*> g_scratch_ptr[kMaxDevices];
+std::mutex g_scratch_mutex;
+
+int scratch_address(cudaStream_t stream, void** out, char* err, size_t err_len) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices) return fail(err, err_len, TD_ERR_CUDA, "device index %d out of range", dev);
+    void* p = g_scratch_ptr[dev].load(std::memory_order_acquire);
+    if (p == nullptr) {
+        std::lock_guard<std::mutex> lock(g_scratch_mutex);
+        p = g_scratch_ptr[dev].load(std::memory_order_acquire);
+        if (p == nullptr) {
+            cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+            e = cudaStreamIsCapturing(stream, &capturing);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                return fail(err, err_len, TD_ERR_CUDA, "cudaStreamIsCapturing: %s", cudaGetErrorString(e));
+            }
+            if (capturing != cudaStreamCaptureStatusNone)
+                return fail(err, err_len, TD_ERR_CUDA,
+                            "the first td_project_forward_noalloc call on device %d looks up its scratch array "
+                            "and must come before any stream capture on that device",
+                            dev);
+            e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+            if (e != cudaSuccess || p == nullptr) {
+                cudaGetLastError();  // not sticky: leave no error behind for the next launch check
+                return fail(err, err_len, TD_ERR_CUDA, "cudaGetSymbolAddress of the scratch array on device %d: %s",
+                            dev, cudaGetErrorString(e));
+            }
+            g_scratch_ptr[dev].store(p, std::memory_order_release);
+        }
+    }
+    *out = p;
+    return TD_OK;
+}
 }  // namespace
 }  // namespace td
 
@@ -1198,26 +1263,65 @@ int td_project_forward_noalloc(int dtype, const void* memory, const void* value_
                                const void* sampling_locations, const void* attention_weights, void* out,
                                int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H, int64_t HD, int64_t L,
                                int64_t P, void* stream, char* err, size_t err_len) {
-    const size_t need = td_project_workspace_bytes(dtype, B, N, HD);
+    // argument checks first (the same as td_project_forward's), so that a bad call never reaches the device
+    const size_t e = dtype_size(dtype);
+    if (e == 0) return fail(err, err_len, TD_ERR_ARG, "unsupported dtype code %d", dtype);
+    if (int rc = check_geometry(B, Q, N, H, L, P, err, err_len)) return rc;
+    if (C <= 0 || HD <= 0) return fail(err, err_len, TD_ERR_ARG, "channels and value_weight rows must be positive");
+    if (HD % H != 0) return fail(err, err_len, TD_ERR_ARG, "value_weight rows must be a multiple of the head count");
+    if (B * Q == 0) return TD_OK;
+    // B * N * HD * e + 256 with every product checked, so that absurd sizes cannot wrap below the limit
+    size_t need = 0;
+    const bool wraps = __builtin_mul_overflow(size_t(B), size_t(N), &need) ||
+                       __builtin_mul_overflow(need, size_t(HD), &need) || __builtin_mul_overflow(need, e, &need) ||
+                       __builtin_add_overflow(need, size_t(256), &need);
+    if (wraps)
+        return fail(err, err_len, TD_ERR_WORKSPACE,
+                    "the allocation-free project order holds at most %zu bytes of projected value, this call needs "
+                    "more than SIZE_MAX (B * N * H * D elements)",
+                    size_t(TD_NOALLOC_SCRATCH_BYTES));
     if (need > TD_NOALLOC_SCRATCH_BYTES)
         return fail(err, err_len, TD_ERR_WORKSPACE,
                     "the allocation-free project order holds at most %zu bytes of projected value, this call "
                     "needs %zu (B * N * H * D elements plus 256 bytes of alignment)",
                     size_t(TD_NOALLOC_SCRATCH_BYTES), need);
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
-    if (dev < 0 || dev >= kMaxDevices) return fail(err, err_len, TD_ERR_CUDA, "device index %d out of range", dev);
-    // once per device, with that device current: the scratch array's device address
-    std::call_once(g_scratch_once[dev], [dev] {
-        g_scratch_status[dev] = cudaGetSymbolAddress(&g_scratch_ptr[dev], g_noalloc_scratch);
-    });
-    if (g_scratch_status[dev] != cudaSuccess)
-        return fail(err, err_len, TD_ERR_CUDA, "cudaGetSymbolAddress of the scratch array: %s",
-                    cudaGetErrorString(g_scratch_status[dev]));
+    void* scratch = nullptr;
+    if (int rc = scratch_address(static_cast<cudaStream_t>(stream), &scratch, err, err_len)) return rc;
     return td_project_forward(dtype, memory, value_weight, value_bias, spatial_shapes, level_start_index,
-                              sampling_locations, attention_weights, out, B, Q, N, C, H, HD, L, P,
-                              g_scratch_ptr[dev], TD_NOALLOC_SCRATCH_BYTES, stream, err, err_len);
+                              sampling_locations, attention_weights, out, B, Q, N, C, H, HD, L, P, scratch,
+                              TD_NOALLOC_SCRATCH_BYTES, stream, err, err_len);
+}
+
+int td_probe_row_gather(const void* buf, int64_t rows, int row_bytes, int wide, int64_t visits, unsigned seed,
+                        void* sink, size_t sink_bytes, int grid, void* stream, char* err, size_t err_len) {
+    const int word = wide ? 32 : 16;
+    if (row_bytes < word || row_bytes > 512 || (row_bytes & (row_bytes - 1)) != 0)
+        return fail(err, err_len, TD_ERR_ARG, "row_bytes must be a power of two from %d to 512", word);
+    if (buf == nullptr || sink == nullptr || rows <= 0 || grid <= 0 || visits < 0)
+        return fail(err, err_len, TD_ERR_ARG, "need a buffer, a sink, rows > 0 and grid > 0");
+    if ((reinterpret_cast<uintptr_t>(buf) & uintptr_t(word - 1)) != 0)
+        return fail(err, err_len, TD_ERR_ARG, "buf must be %d-byte aligned", word);
+    if (sink_bytes < size_t(grid) * kProbeThreads * 16 || !aligned16(sink))
+        return fail(err, err_len, TD_ERR_ARG, "sink needs grid * %d 16-byte words, 16-byte aligned", kProbeThreads);
+    const long long chunk = (long long)grid * (kProbeThreads / 32) * (32 / (row_bytes / word)) * (wide ? 4 : 8);
+    if (visits % chunk != 0)
+        return fail(err, err_len, TD_ERR_ARG, "visits must be a multiple of %lld for this grid", chunk);
+    ProbeArgs a;
+    a.buf = static_cast<const unsigned char*>(buf);
+    a.rows = (unsigned long long)rows;
+    a.visits = visits;
+    a.row_bytes = row_bytes;
+    a.seed = seed;
+    a.sink = static_cast<uint4*>(sink);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const cudaError_t e = wide ? launch_kernel(row_gather_probe_kernel<true>, dim3(grid), dim3(kProbeThreads), 0, s,
+                                               false, a)
+                               : launch_kernel(row_gather_probe_kernel<false>, dim3(grid), dim3(kProbeThreads), 0,
+                                               s, false, a);
+    if (e != cudaSuccess)
+        return fail(err, err_len, TD_ERR_CUDA, "row_gather_probe_kernel launch: %s", cudaGetErrorString(e));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return check_launch(err, err_len, "row_gather_probe_kernel");
 }
 
 int td_device_info(int device, int* sm_count, int* cc_major, int* cc_minor, char* err, size_t err_len) {
