@@ -145,17 +145,63 @@ def graph_time_us(fn, steps, warmup):
     return g, launches
 
 
-def time_graph(g, steps, reps=1):
+def replay_times(g, steps, reps=1):
+    """Device time per call (µs) of each of `reps` replays of a graph of `steps` calls, CUDA events on the current
+    stream. Before each start event a short spin kernel keeps the stream busy while the host submits the graph, so
+    the timed region holds the calls only, not the host's submission latency."""
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    best = float('inf')
+    out = []
     for _ in range(reps):
         torch.cuda.synchronize()
+        torch.cuda._sleep(100_000)
         start.record()
         g.replay()
         end.record()
         end.synchronize()
-        best = min(best, start.elapsed_time(end) * 1e3 / steps)
-    return best
+        out.append(start.elapsed_time(end) * 1e3 / steps)
+    return out
+
+
+def time_graph(g, steps, reps=1):
+    """Median device time per call (µs) over `reps` replays (see replay_times)."""
+    return statistics.median(replay_times(g, steps, reps))
+
+
+def l2_gather_peak(dev, kinds, visits=1 << 24, reps=10):
+    """Measured L2 random-row gather rate of this GPU for each (row_bytes, wide) in kinds: td_probe_row_gather over
+    an 8 MiB buffer (L2-resident; the c1h value and memory are 4.3 MB each) with every SM, `reps` launches timed
+    with CUDA events after two warm-up launches. Returns {key: {'GBps', 'G_rows_per_s'}}, key '64B' or '128B_v8'."""
+    buf = torch.randint(0, 255, (8 << 20,), dtype=torch.uint8, device=dev)
+    grid = torch.cuda.get_device_properties(dev).multi_processor_count * 8
+    sink = torch.empty(grid * 1024, dtype=torch.int32, device=dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    out = {}
+    for row_bytes, wide in kinds:
+        for _ in range(2):
+            n = _native.probe_row_gather(buf, row_bytes, visits, wide, grid=grid, sink=sink)
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(reps):
+            _native.probe_row_gather(buf, row_bytes, visits, wide, grid=grid, sink=sink)
+        end.record()
+        end.synchronize()
+        t = start.elapsed_time(end) * 1e-3 / reps
+        out[probe_key(row_bytes, wide)] = {'GBps': round(n * row_bytes / t / 1e9, 1),
+                                           'G_rows_per_s': round(n / t / 1e9, 3)}
+    return out
+
+
+def probe_key(row_bytes, wide):
+    return f'{row_bytes}B' + ('_v8' if wide else '')
+
+
+def gather_kind(kind, C, D, e):
+    """(row_bytes, 32-byte loads) of the corner rows a gather kernel reads: the sampler reads D-wide head slices
+    (32-byte loads from 128 bytes on), the fused kernel C-wide memory rows (16-byte loads)."""
+    if kind == 'sample':
+        rb = D * e
+        return rb, rb >= 128 and rb % 32 == 0
+    return C * e, False
 
 
 def dist_setup(n_gpus):
@@ -199,8 +245,20 @@ def cpu_time_us(cfg_name, budget_s=10.0, max_calls=50):
     return statistics.median(times) * 1e6, threads, len(times)
 
 
+def resolved_mode(cfg_name, mode):
+    """The order `mode` runs on B200 for this workload ('auto' resolved with FUSED_LIMIT_SM100, the table compute
+    capability 10.x uses), so that the CPU arm names the configuration of the GPU arm."""
+    if mode != 'auto':
+        return mode
+    import marearts_tinydeform_b200 as td
+    a = workloads.make_inputs(cfg_name, seed=0, device='meta')
+    return td._pick(a[0], a[1], a[5].shape[1], a[5].shape[2], a[5].shape[3], a[5].shape[4],
+                    limits=td.FUSED_LIMIT_SM100)
+
+
 def run_reference_arm(args):
     rank = int(os.environ.get('RANK', '0'))
+    world = int(os.environ.get('WORLD_SIZE', '1'))
     if rank != 0:
         return
     # exactly W untimed and K timed calls of the CPU path (the upstream algorithm on torch's CPU operators, all host
@@ -223,7 +281,7 @@ def run_reference_arm(args):
         'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(us / 1e3, 4), 'higher_is_better': False,
         'scaling': 'weak', 'vs_baseline': None, 'dtype': str(cfg['dtype']).replace('torch.', ''),
         'data': 'synthetic (seeded, BASELINE config shapes)',
-        'config': config_dict(args.config, 1, args.mode, 'CPU'),
+        'config': config_dict(args.config, world, resolved_mode(args.config, args.mode)),
         'cpu_baseline': {'value': round(us, 2), 'unit': 'us', 'cores': threads, 'kind': 'port',
                          'sample': f'{n} timed calls of {args.config} (B={cfg["B"]}), mean, torch CPU ops, '
                                    f'{threads} threads'},
@@ -250,6 +308,39 @@ def kernel_bytes(kind, B, Q, N, C, H, D, L, P, e, bias=True):
     if kind == 'sample':
         return e * (B * N * HD + 3 * B * Q * H * L * P + B * Q * HD)
     raise ValueError(kind)
+
+
+def call_roofline(kernels, t_call, hbm, peak_kind, l2_peaks, config, B, Q, N, C, H, D, L, P, e, bias, gather,
+                  gather_row_bytes, l2_key):
+    """The call's roofline: its compulsory HBM bytes (memory and weights read once, locations and weights read,
+    output written) over its device time, against the measured HBM peak; beside it each kernel's own algorithmic
+    bytes over its standalone time, and the gather kernel's corner-row bytes over its time against the measured L2
+    random-row gather rate for rows of that size."""
+    alg = workloads.algorithmic_bytes(B, Q, N, C, H, D, L, P, e, bias)
+    achieved = alg / (t_call * 1e-6) / 1e9
+    per = {}
+    traffic = 0
+    for k, t in kernels.items():
+        kb = kernel_bytes(k, B, Q, N, C, H, D, L, P, e, bias)
+        tr = committed_traffic(k, config)
+        traffic = None if tr is None or traffic is None else traffic + tr
+        d = {'us': round(t, 3), 'algorithmic_bytes': kb, 'achieved': round(kb / (t * 1e-6) / 1e9, 1),
+             'frac': round(kb / (t * 1e-6) / 1e9 / hbm, 4), 'traffic': tr}
+        if k == gather:
+            gb = B * Q * H * L * P * 4 * gather_row_bytes
+            l2a = gb / (t * 1e-6) / 1e9
+            d.update({'bound': 'l2 gather', 'gather_bytes': gb, 'gather_row_bytes': gather_row_bytes,
+                      'l2_achieved': round(l2a, 1), 'l2_peak': l2_peaks[l2_key]['GBps'], 'l2_peak_rows': l2_key,
+                      'l2_frac': round(l2a / l2_peaks[l2_key]['GBps'], 4)})
+        else:
+            d['bound'] = 'hbm'
+        per[k] = d
+    return {'bound': 'hbm', 'scope': 'whole call: compulsory HBM bytes / device time per call',
+            'achieved': round(achieved, 1), 'peak': hbm, 'unit': 'GB/s', 'frac': round(achieved / hbm, 4),
+            'peak_source': peak_kind, 'algorithmic_bytes': alg, 'traffic': traffic,
+            'traffic_source': 'profiles/traffic.json (ncu dram bytes per launch, summed over the call)',
+            'kernels': per, 'l2_frac': per[gather]['l2_frac'], 'l2_peak': per[gather]['l2_peak'],
+            'l2_peak_source': 'measured in this run (td_probe_row_gather, 8 MiB L2-resident buffer, all SMs)'}
 
 
 def run_ours(args):
@@ -290,8 +381,9 @@ def run_ours(args):
         torch.cuda.synchronize()
         with ClockSampler(local) as clocks:
             time.sleep(0.25)
-            t_call = time_graph(g, args.steps, reps=max(1, args.reps))
-        t_call = barrier_max(t_call, world)
+            replays = replay_times(g, args.steps, reps=max(1, args.reps))
+        t_call = barrier_max(statistics.median(replays), world)
+        t_min = barrier_max(min(replays), world)
         del g
 
         # per-kernel times of the path the call took (same rotation, same stream), for the roofline
@@ -309,10 +401,13 @@ def run_ours(args):
                                   args.steps, args.warmup)
             kernels['sample'] = time_graph(gs, args.steps, reps=max(1, args.reps))
             del gs, hm
-        top = max(kernels, key=kernels.get)
         hbm, peak_kind = peaks()
-        alg = kernel_bytes(top, B, Q, N, C, H, D, L, P, e, bias is not None)
-        achieved = alg / (kernels[top] * 1e-6) / 1e9
+        gather = 'fused' if mode == 'fused' else 'sample'
+        g_rb, g_wide = gather_kind(gather, C, D, e)
+        probe_rb = min(512, 1 << (g_rb.bit_length() - 1))  # the probe reads power-of-two rows of at most 512 bytes
+        l2_peaks = l2_gather_peak(dev, [(probe_rb, g_wide and probe_rb >= 32)])
+        roofline = call_roofline(kernels, t_call, hbm, peak_kind, l2_peaks, args.config, B, Q, N, C, H, D, L, P, e,
+                                 bias is not None, gather, g_rb, probe_key(probe_rb, g_wide and probe_rb >= 32))
 
         # hot-L2 time (upstream's method: one input set replayed)
         gh, _ = graph_time_us(lambda i: ma_deform_attn(base[0], W, bias, shapes, starts, base[5], base[6],
@@ -371,6 +466,8 @@ def run_ours(args):
         end.synchronize()
         t_e2e = barrier_max(start.elapsed_time(end) * 1e3 / e2e_steps, world)
 
+    sharded = None if args.no_sharded else sharded_record(args, world, dev)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         us, threads, n = cpu_time_us(args.config)
@@ -386,20 +483,70 @@ def run_ours(args):
                            **({'value_padding_mask': args.padding_mask} if mask is not None else {}),
                            **({'output_proj': [C, H * D]} if wo is not None else {})),
             'mode': mode, 'queries_per_s': round(B * Q * world / (t_call * 1e-6), 1),
+            'replays': {'n': len(replays), 'steps_each': args.steps, 'median_us': round(t_call, 3),
+                        'min_us': round(t_min, 3), 'value_is': 'median over replays (max over ranks)'},
             'hot_l2_us': round(t_hot, 3), 'kernel_us': {k: round(v, 3) for k, v in kernels.items()},
-            'roofline': {'bound': 'hbm', 'kernel': top, 'achieved': round(achieved, 1), 'peak': hbm,
-                         'unit': 'GB/s', 'frac': round(achieved / hbm, 4), 'peak_source': peak_kind,
-                         'algorithmic_bytes': alg, 'traffic': committed_traffic(top, args.config)},
+            'roofline': roofline,
             'cpu_baseline': cpu,
             'e2e': {'value': round(t_e2e, 2), 'unit': 'us', 'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h},
             'gpu_launches': launches,
             'clocks': clocks.summary(),
         }
+        if sharded is not None:
+            line['sharded'] = sharded
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
         dist.destroy_process_group()
+
+
+def sharded_record(args, world, dev, cfg_name='c3'):
+    """The batch-sharded configuration: c3 (bfloat16, 8 images, Q=300) split over the ranks by batch_range, each
+    step one ma_deform_attn_sharded call per rank with gather=True (the outputs all-gathered to every rank over NCCL;
+    no collective at one rank), K steps in one CUDA graph on rotating inputs, device-timed, max over ranks; beside
+    it the same steps without the gather, so the all-gather's share of the step is measured, not inferred."""
+    from marearts_tinydeform_b200.shard import batch_range, ma_deform_attn_sharded
+    rank = int(os.environ.get('RANK', '0'))
+    cfg = workloads.CONFIGS[cfg_name]
+    Bg = cfg['B']
+    start, stop = batch_range(Bg, world, rank)
+    b = stop - start
+    base, pool = input_pool(cfg_name, b, dev, 2 * L2_BYTES)
+    W, bias, shapes, starts = base[1], base[2], base[3], base[4]
+    gather = world > 1
+
+    def step(i, with_gather):
+        mem, loc, attn = pool[i % len(pool)]
+        return ma_deform_attn_sharded(mem, W, bias, shapes, starts, loc, attn, gather=with_gather,
+                                      global_batch=Bg)
+
+    times = {}
+    with torch.inference_mode():
+        for name, flag in (('no_gather', False), ('gather', gather)):
+            if world > 1:
+                import torch.distributed as dist
+                dist.barrier()
+            g, _ = graph_time_us(lambda i, f=flag: step(i, f), args.steps, args.warmup)
+            if world > 1:
+                dist.barrier()
+            times[name] = barrier_max(time_graph(g, args.steps, reps=max(5, args.reps // 5)), world)
+            del g
+        out = step(0, gather)
+    N, C, H, D, L, P, Q = base[0].shape[1], cfg['C'], cfg['H'], cfg['D'], len(cfg['levels']), cfg['P'], cfg['Q']
+    e = base[0].element_size()
+    hbm, _ = peaks()
+    alg = workloads.algorithmic_bytes(b, Q, N, C, H, D, L, P, e, bias is not None)
+    t = times['gather']
+    return {'workload': f'{cfg_name}: {cfg["dtype"]} B={Bg} global, {b} image(s) on rank {rank} of {world}, Q={Q}, '
+                        f'C={C}, H={H}, D={D}, levels={cfg["levels"]}, P={P}',
+            'global_batch': Bg, 'images_per_rank': b, 'scaling': 'strong', 'us_per_step': round(t, 3),
+            'us_per_step_without_gather': round(times['no_gather'], 3),
+            'allgather_share': round(max(0.0, t - times['no_gather']) / t, 4) if gather else 0.0,
+            'queries_per_s': round(Bg * Q / (t * 1e-6), 1), 'gathered_shape': list(out.shape),
+            'gathered_bytes_per_rank': out.numel() * out.element_size() if gather else 0,
+            'per_gpu_roofline_frac': round(alg / (times['no_gather'] * 1e-6) / 1e9 / hbm, 4),
+            'timing': 'CUDA graph of K steps (NCCL all-gather captured), median of replays, max over ranks'}
 
 
 def run_layer(args):
@@ -564,6 +711,23 @@ def run_backward(args):
     print(json.dumps(line), flush=True)
 
 
+def run_l2_peak(args):
+    """The L2 random-row gather rates (td_probe_row_gather) for every row size the gather kernels read; one line."""
+    torch.cuda.set_device(0)
+    dev = torch.device('cuda', 0)
+    _native.load()
+    kinds = [(16, False), (32, False), (64, False), (128, False), (128, True), (256, False), (256, True),
+             (512, False), (512, True)]
+    with ClockSampler(0) as clocks:
+        time.sleep(0.25)
+        rates = l2_gather_peak(dev, kinds)
+    hbm, kind = peaks()
+    print(json.dumps({'metric': 'L2 random-row gather rate (td_probe_row_gather, 8 MiB buffer, all SMs)',
+                      'rates': rates, 'hbm_peak_gbs': hbm, 'hbm_peak_source': kind,
+                      'sm_count': torch.cuda.get_device_properties(dev).multi_processor_count,
+                      'clocks': clocks.summary()}), flush=True)
+
+
 def run_sweep(args):
     """Fused vs project over upstream's sweep grid (bench/results/rtx4090.md) and the c5 grid; prints a table."""
     torch.cuda.set_device(0)
@@ -572,7 +736,8 @@ def run_sweep(args):
     grids = [('c1', dtype, B, Q) for dtype in args.dtype for B in (1, 4, 8) for Q in (50, 100, 200, 300, 600, 900)]
     grids += [('c5', dtype, B, Q) for dtype in args.dtype for B in workloads.C5_BATCHES for Q in workloads.C5_QUERIES]
     grids += [('c4', dtype, B, Q) for dtype in args.dtype for B in (1, 8) for Q in (300, 900)]
-    with torch.inference_mode():
+    clocks = ClockSampler(0)
+    with torch.inference_mode(), clocks:
         for cfg, dname, B, Q in grids:
             dtype = getattr(torch, dname)
             a = workloads.make_inputs(cfg, seed=0, B=B, Q=Q, dtype=dtype, device='cuda', generate_on_device=True)
@@ -593,7 +758,7 @@ def run_sweep(args):
             del a
             torch.cuda.empty_cache()
     ok = sum(r['auto_within_10pct'] for r in rows)
-    print(json.dumps({'sweep_cases': len(rows), 'auto_within_10pct': ok}), flush=True)
+    print(json.dumps({'sweep_cases': len(rows), 'auto_within_10pct': ok, 'clocks': clocks.summary()}), flush=True)
 
 
 def main():
@@ -601,11 +766,13 @@ def main():
     ap.add_argument('--gpus', type=int, default=1)
     ap.add_argument('--steps', type=int, default=200)
     ap.add_argument('--warmup', type=int, default=5)
-    ap.add_argument('--reps', type=int, default=5)
+    ap.add_argument('--reps', type=int, default=50)
     ap.add_argument('--config', default='c1h', choices=sorted(workloads.CONFIGS))
     ap.add_argument('--mode', default='auto', choices=('auto', 'fused', 'project'))
     ap.add_argument('--impl', default='ours', choices=('ours', 'reference'))
     ap.add_argument('--no-cpu', action='store_true')
+    ap.add_argument('--no-sharded', action='store_true', help='skip the batch-sharded c3 record')
+    ap.add_argument('--l2-peak', action='store_true', help='print the L2 random-row gather rates and exit')
     ap.add_argument('--output-proj', action='store_true',
                     help='chain the decoder output_proj ([C, H*D] nn.Linear) behind the attention')
     ap.add_argument('--padding-mask', type=float, default=0.0,
@@ -621,6 +788,8 @@ def main():
         args.warmup = 3
     if args.impl == 'reference':
         run_reference_arm(args)
+    elif args.l2_peak:
+        run_l2_peak(args)
     elif args.sweep:
         run_sweep(args)
     elif args.layer:

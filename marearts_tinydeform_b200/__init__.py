@@ -1,7 +1,9 @@
 """marearts-tinydeform on B200: value projection + multi-scale deformable attention for DETR-style decoders.
 
-A drop-in for upstream ``marearts_tinydeform`` (``marearts_tinydeform/__init__.py:1-79``): the same public names,
-arguments, results and errors, computed by hand-written sm_100a kernels behind a C ABI (include/tinydeform.h):
+The operator of upstream ``marearts_tinydeform`` (``marearts_tinydeform/__init__.py:1-79``), computed by hand-written
+sm_100a kernels behind a C ABI (include/tinydeform.h). The drop-in for upstream's callers is the import name
+``marearts_tinydeform``, whose ``ma_deform_attn`` keeps upstream's contract exactly (inference only); this package's
+own ``ma_deform_attn`` takes the same arguments plus the additions below and also differentiates:
 
     ma_deform_attn(memory, value_weight, value_bias, spatial_shapes, level_start_index,
                    sampling_locations, attention_weights, mode='auto')  -> [B, Q, H * D]
@@ -21,8 +23,9 @@ Around the operator (additions; upstream has only the operator):
 the whole MSDeformAttn layer (query -> offsets and softmaxed weights -> attention -> output_proj) in one library call.
 
 CPU tensors run ``ma_deform_attn_reference`` (as upstream does). CUDA tensors run only the native library; if it is
-missing, the call raises. Unlike upstream (inference only), CUDA inputs that require grad are differentiated: the
-forward runs the same kernels and the backward runs this library's backward kernel (``autograd.py``).
+missing, the call raises. Unlike upstream (inference only), this package's ``ma_deform_attn`` differentiates CUDA
+inputs that require grad: the forward runs the same kernels and the backward runs this library's backward kernels
+(``autograd.py``).
 """
 
 import functools
@@ -69,10 +72,11 @@ def choose_mode(memory, value_weight, sampling_locations):
     return _pick(memory, value_weight, n_qry, n_head, n_lvl, n_pt)
 
 
-def _pick(memory, value_weight, n_qry, n_head, n_lvl, n_pt):
+def _pick(memory, value_weight, n_qry, n_head, n_lvl, n_pt, limits=None):
     n_img, n_tok, _ = memory.shape
     head_dim = value_weight.shape[0] // n_head
-    limits = _limits(memory.get_device()) if memory.is_cuda else FUSED_LIMIT
+    if limits is None:
+        limits = _limits(memory.get_device()) if memory.is_cuda else FUSED_LIMIT
     a, b = limits.get(memory.dtype, limits[torch.float16])
     ratio = n_qry * n_lvl * n_pt * 4 / max(n_tok * head_dim, 1)
     return 'fused' if ratio < a + b / max(n_img, 1) else 'project'

@@ -52,6 +52,7 @@ SIGNATURES = {
                                         _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp, _cp, _sz]),
     'td_project_forward_noalloc': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                          _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _cp, _sz]),
+    'td_probe_row_gather': (_ip, [_vp, _i64, _ip, _ip, _i64, ctypes.c_uint, _vp, _sz, _ip, _vp, _cp, _sz]),
     'td_set_kernel_policy': (_ip, [_ip]),
     'td_device_error': (_ip, [_ip, ctypes.POINTER(ctypes.c_uint), _cp, _sz]),
     'td_device_info': (_ip, [_ip, ctypes.POINTER(_ip), ctypes.POINTER(_ip), ctypes.POINTER(_ip), _cp, _sz]),
@@ -548,3 +549,23 @@ def launch_count():
 
 def version():
     return load().td_version().decode()
+
+
+def probe_row_gather(buf, row_bytes, visits, wide=False, seed=12345, grid=None, sink=None):
+    """One launch of the L2 random-row gather probe over buf (a CUDA tensor, bytes viewed as [rows, row_bytes]):
+    `visits` rows rounded up to the kernel's multiple. Returns the number of rows actually read (queued on the
+    current stream, not synchronised). sink: int32 [grid * 1024] scratch (allocated when None)."""
+    lib = load()
+    dev = buf.device
+    if grid is None:
+        grid = torch.cuda.get_device_properties(dev).multi_processor_count * 8
+    word = 32 if wide else 16
+    chunk = grid * 8 * (32 // (row_bytes // word)) * (4 if wide else 8)
+    visits = -(-visits // chunk) * chunk
+    if sink is None:
+        sink = torch.empty(grid * 256 * 4, dtype=torch.int32, device=dev)
+    rows = buf.numel() * buf.element_size() // row_bytes
+    with torch.cuda.device(dev):
+        _call(lib.td_probe_row_gather, _ptr(buf), rows, row_bytes, 1 if wide else 0, visits, seed, _ptr(sink),
+              sink.numel() * 4, grid, _stream(dev))
+    return visits

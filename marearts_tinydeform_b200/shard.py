@@ -35,23 +35,36 @@ def shard_inputs(inputs, rank, world):
 
 def ma_deform_attn_sharded(memory, value_weight, value_bias, spatial_shapes, level_start_index,
                            sampling_locations, attention_weights, mode='auto', group=None, gather=False,
-                           value_padding_mask=None):
+                           value_padding_mask=None, global_batch=None):
     """ma_deform_attn on this rank's images; with gather=True, the outputs of every rank concatenated in rank order.
 
     Each rank passes its own shard (possibly empty). Without gather there is no collective at all. With gather, the
-    shard sizes are exchanged first (one small all-gather), shards are padded to the largest one for a single
-    all_gather_into_tensor, and the padding is dropped; every rank must call it, in the same order.
+    shard sizes are exchanged first (one small all-gather and a host read), shards are padded to the largest one for
+    a single all_gather_into_tensor, and the padding is dropped; every rank must call it, in the same order.
+    global_batch: the whole batch's size, when the shards are batch_range's split of it (as shard_inputs makes
+    them). The sizes are then known without the exchange, nothing reads device memory on the host, and the call can
+    be captured in a CUDA graph; with equal shards the gathered tensor is the result itself, with no copy.
     """
     out = ma_deform_attn(memory, value_weight, value_bias, spatial_shapes, level_start_index,
                          sampling_locations, attention_weights, mode=mode, value_padding_mask=value_padding_mask)
     if not gather:
         return out
     world = dist.get_world_size(group)
-    sizes = torch.zeros(world, dtype=torch.long, device=out.device)
-    mine = torch.tensor([out.shape[0]], dtype=torch.long, device=out.device)
-    dist.all_gather_into_tensor(sizes, mine, group=group)
-    sizes = sizes.tolist()
+    if global_batch is None:
+        sizes = torch.zeros(world, dtype=torch.long, device=out.device)
+        mine = torch.tensor([out.shape[0]], dtype=torch.long, device=out.device)
+        dist.all_gather_into_tensor(sizes, mine, group=group)
+        sizes = sizes.tolist()
+    else:
+        sizes = [stop - start for start, stop in (batch_range(global_batch, world, r) for r in range(world))]
+        if sizes[dist.get_rank(group)] != out.shape[0]:
+            raise ValueError(f'this rank holds {out.shape[0]} images, but batch_range gives it '
+                             f'{sizes[dist.get_rank(group)]} of {global_batch}')
     widest = max(sizes)
+    if all(n == widest for n in sizes):
+        everything = out.new_empty((world * widest,) + tuple(out.shape[1:]))
+        dist.all_gather_into_tensor(everything, out.contiguous(), group=group)
+        return everything
     padded = out.new_zeros((widest,) + tuple(out.shape[1:]))
     padded[:out.shape[0]] = out
     everything = out.new_empty((world * widest,) + tuple(out.shape[1:]))

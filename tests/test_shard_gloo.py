@@ -56,6 +56,16 @@ def _worker(rank, world, port, batch, mode, results):
             masked = ma_deform_attn_sharded(*local_m[:7], gather=True, value_padding_mask=local_m[7])
             want_m = ma_deform_attn_reference(*full, value_padding_mask=mask)
         ok_all = ok_all and masked.shape == want_m.shape and torch.allclose(masked, want_m, atol=1e-6)
+        # the known split (no size exchange): same result, and a shard that does not match the split is refused
+        with torch.inference_mode():
+            known = ma_deform_attn_sharded(*local, gather=True, global_batch=batch)
+        ok_all = ok_all and known.shape == want.shape and torch.allclose(known, want, atol=1e-6)
+        try:
+            with torch.inference_mode():
+                ma_deform_attn_sharded(*local, gather=True, global_batch=batch + world)
+            ok_all = False
+        except ValueError:
+            pass
         results[rank] = (bool(ok_local), bool(ok_all))
     finally:
         dist.destroy_process_group()
