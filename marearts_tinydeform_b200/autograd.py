@@ -54,10 +54,9 @@ class MaDeformAttnFunction(torch.autograd.Function):
         g = grad_out.to(memory.dtype).contiguous()
         if value_hm is not None:  # the forward's own value, head-major
             grad_value, grad_loc, grad_attn = _native.sample_backward(value_hm, shapes, starts, loc, attn, g, mask)
-        else:
-            value = torch.nn.functional.linear(memory, weight, bias)  # [B, N, H * D]
-            grad_value, grad_loc, grad_attn = _native.sample_backward(value, shapes, starts, loc, attn, g, mask,
-                                                                      heads=H)
+        else:  # the fused order never formed the value: project it again, head-major, with the library's GEMM
+            value = _native.value_proj(memory, weight, bias, H, head_major=True)
+            grad_value, grad_loc, grad_attn = _native.sample_backward(value, shapes, starts, loc, attn, g, mask)
         acc = grad_value.view(B * N, HD)
         want_bias = bias is not None and need[2]
         # the rounding to the dtype and the bias gradient's column sums in one pass over the accumulator

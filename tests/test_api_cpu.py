@@ -6,15 +6,33 @@ import torch
 import marearts_tinydeform
 import marearts_tinydeform_b200 as td
 from cases import make
-from marearts_tinydeform import choose_mode, ma_deform_attn, ma_deform_attn_reference
+from marearts_tinydeform_b200 import choose_mode, ma_deform_attn, ma_deform_attn_reference
 
 
 def test_upstream_import_name_serves_this_package():
-    for name in ('ma_deform_attn', 'ma_deform_attn_reference', 'choose_mode', 'FUSED_LIMIT', 'FUSED_LIMIT_SM75',
-                 '_limits', 'MODES', '__version__'):
+    for name in ('ma_deform_attn_reference', 'choose_mode', 'FUSED_LIMIT', 'FUSED_LIMIT_SM75', '_limits', 'MODES',
+                 '__version__'):
         assert getattr(marearts_tinydeform, name) is getattr(td, name)
     assert td.MODES == ('auto', 'fused', 'project')
     assert marearts_tinydeform.__all__ == ['ma_deform_attn', 'ma_deform_attn_reference', 'choose_mode']
+    # upstream's signature exactly (the B200 package's own ma_deform_attn adds keyword arguments)
+    import inspect
+    assert list(inspect.signature(marearts_tinydeform.ma_deform_attn).parameters) == [
+        'memory', 'value_weight', 'value_bias', 'spatial_shapes', 'level_start_index', 'sampling_locations',
+        'attention_weights', 'mode']
+
+
+def test_upstream_import_name_keeps_the_cpu_route_and_mode_check():
+    """Upstream order: the mode is checked first, then CPU tensors go to the reference -- with grad too, since the
+    inference-only rule guards the CUDA path only."""
+    args = make(1, 10, 2, 8, 16, [(6, 7), (3, 4)], 2)
+    with pytest.raises(ValueError):
+        marearts_tinydeform.ma_deform_attn(*args, mode='nope')
+    with torch.inference_mode():
+        assert torch.equal(marearts_tinydeform.ma_deform_attn(*args), ma_deform_attn_reference(*args))
+    grad = [t.clone().requires_grad_(True) if i == 0 else t for i, t in enumerate(args)]
+    marearts_tinydeform.ma_deform_attn(*grad).sum().backward()
+    assert grad[0].grad is not None
 
 
 def test_cpu_path_is_reference():

@@ -302,12 +302,22 @@ def test_baseline_configs_full_size(policy, name):
         check(f'{name} seed {seed} {policy}', to(args, 'cuda'), oracle(upcast(args)), *TOL[dtype])
 
 
+def _rows_oracle(args, picks):
+    """oracle_rows for the (b, q) picks, given only the picked images (so that a B=64 batch is never upcast whole)."""
+    images = sorted({b for b, _ in picks})
+    slot = {b: i for i, b in enumerate(images)}
+    idx = torch.tensor(images)
+    sub = [None if t is None else (t.index_select(0, idx) if i in (0, 5, 6) else t) for i, t in enumerate(args)]
+    return torch.from_numpy(O.oracle_rows(*[t if t is None else t.cpu() for t in upcast(sub)],
+                                          [(slot[b], q) for b, q in picks]))
+
+
 def _spot_check(name, args, dtype, n=24, seed=0):
     """Full-size config: all modes agree with each other, and sampled (b, q) rows match the row oracle."""
     rng = np.random.default_rng(seed)
     B, Q = args[5].shape[:2]
     picks = sorted({(int(rng.integers(B)), int(rng.integers(Q))) for _ in range(n)})
-    ref = torch.from_numpy(O.oracle_rows(*[t if t is None else t.cpu() for t in upcast(args)], picks))
+    ref = _rows_oracle(args, picks)
     dev = to(args, 'cuda')
     atol, rtol = TOL[dtype]
     with torch.inference_mode():
@@ -327,12 +337,37 @@ def test_c4_dino_full_size(cuda):
         assert choose_mode(args[0].cuda(), args[1].cuda(), args[5].cuda()) in ('fused', 'project')
 
 
+def test_c4_dino_full_tensor(cuda):
+    """c4 (fp16, B=8, Q=900, DINO 4-level shapes) in full: every output element of both orders against the
+    float64 oracle, one seed."""
+    args = workloads.make_inputs('c4', seed=1)
+    check('c4 full tensor', to(args, cuda), oracle(upcast(args)), *TOL[torch.float16], modes=('fused', 'project'))
+
+
+def _c5_cases():
+    return [(B, Q) for B in workloads.C5_BATCHES for Q in workloads.C5_QUERIES]
+
+
 @pytest.mark.parametrize('dtype', [torch.float32, torch.float16, torch.bfloat16])
 def test_c5_stress_sweep(policy, dtype):
-    """The stress config at the operator limits (L*P = 64, C = 512, D = 64) over its batch/query sweep."""
+    """The stress config at the operator limits (L*P = 64, C = 512, D = 64) at four points of its batch/query grid,
+    under both kernel policies."""
     for B, Q in ((1, 50), (4, 300), (8, 900), (64, 100)):
         args = workloads.make_inputs('c5', seed=B + Q, B=B, Q=Q, dtype=dtype)
         _spot_check(f'c5 B{B} Q{Q} {dtype}', args, dtype, n=12, seed=B)
+
+
+@pytest.mark.parametrize('B,Q', _c5_cases())
+def test_c5_full_grid(cuda, B, Q):
+    """Every (B, Q) pair of the stress grid (B in 1, 4, 8, 64; Q in 50, 100, 300, 900 -- B=64 at Q=900 is the
+    8-GPU split's whole batch) in all three dtypes with the default kernels: sampled rows of both orders against the
+    row oracle, and the two orders against each other over the whole output."""
+    base = workloads.make_inputs('c5', seed=1000 + B * 7 + Q, B=B, Q=Q, dtype=torch.float32)
+    for dtype in (torch.float32, torch.float16, torch.bfloat16):
+        args = [t if t is None or t.dtype == torch.long else t.to(dtype) for t in base]
+        _spot_check(f'c5 grid B{B} Q{Q} {dtype}', args, dtype, n=8, seed=B * Q)
+        del args
+    torch.cuda.empty_cache()
 
 
 def test_tensor_core_shapes(policy):
