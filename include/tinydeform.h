@@ -250,6 +250,27 @@ TD_API int td_project_forward_noalloc(int dtype, const void* memory, const void*
                                       int64_t P, void* stream, char* err, size_t err_len);
 
 /*
+ * The GEMMs of a linear layer's backward, for the training path (no counterpart in upstream, whose operator is
+ * inference only, marearts_tinydeform/__init__.py:67-71; they replace the cuBLAS GEMMs torch's autograd would run for
+ * nn.Linear). For y = x @ weight^T (+ bias), x [M, K], weight [Nout, K] and grad_out = dL/dy [M, Nout]:
+ *   td_linear_grad_input:  grad_input [M, K] = grad_out @ weight
+ *   td_linear_grad_weight: grad_weight [Nout, K] = grad_out^T @ x, summed over all M rows; grad_bias [Nout] (the
+ *                          column sums of grad_out) when grad_bias is not NULL. Outputs in the input dtype.
+ * In the operator's backward x is memory, weight value_weight and grad_out the gradient of the projected value.
+ * float16 / bfloat16 run on tcgen05 tensor cores (float32 accumulation) when every row is 16-byte aligned
+ * (Nout, K multiples of 8); float32 / float64 and other shapes on CUDA cores. The weight gradient splits the M rows
+ * over CTAs and adds float32 partial sums atomically, so its last bits may vary between runs.
+ * td_linear_grad_weight needs td_linear_grad_workspace_bytes(dtype, Nout, K) bytes of workspace (0 for float32 and
+ * float64, whose sums accumulate in the outputs themselves).
+ */
+TD_API size_t td_linear_grad_workspace_bytes(int dtype, int64_t Nout, int64_t K);
+TD_API int td_linear_grad_input(int dtype, const void* grad_out, const void* weight, void* grad_input, int64_t M,
+                                int64_t Nout, int64_t K, void* stream, char* err, size_t err_len);
+TD_API int td_linear_grad_weight(int dtype, const void* grad_out, const void* input, void* grad_weight,
+                                 void* grad_bias, int64_t M, int64_t Nout, int64_t K, void* workspace,
+                                 size_t workspace_bytes, void* stream, char* err, size_t err_len);
+
+/*
  * Measurement kernel (no counterpart in upstream): reads `visits` pseudo-random rows of row_bytes (a power of two,
  * 16..512; 32..512 with wide = 1, which uses 32-byte loads) from buf ([rows, row_bytes], 16- or 32-byte aligned)
  * with every SM, the way the sampler reads corner rows, and writes one 16-byte word per thread into sink

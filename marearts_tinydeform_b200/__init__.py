@@ -33,7 +33,7 @@ import functools
 import torch
 
 from . import _native
-from .autograd import ma_deform_attn_train
+from .autograd import linear_train, ma_deform_attn_train
 from .reference import deform_attn_layer_reference, ma_deform_attn_reference, sampling_producer_reference
 
 __all__ = ['ma_deform_attn', 'ma_deform_attn_reference', 'choose_mode', 'deform_attn_layer', 'sampling_producer',
@@ -112,13 +112,16 @@ def ma_deform_attn(memory, value_weight, value_bias, spatial_shapes, level_start
         mode = choose_mode(memory, value_weight, sampling_locations)
     if _wants_grad(memory, value_weight, value_bias, sampling_locations, attention_weights, output_weight,
                    output_bias):
-        # training: the same forward kernels behind an autograd Function whose backward runs td_sample_backward;
-        # output_proj through torch's nn.Linear (cuBLAS), differentiable as it is
+        # training: the same forward kernels behind autograd Functions whose backward runs this library's
+        # backward kernels (autograd.py), output_proj included
         _native.check_geometry(memory, spatial_shapes, level_start_index, sampling_locations, attention_weights)
         _native.check_projection(memory, value_weight, value_bias, sampling_locations.shape[2])
         out = ma_deform_attn_train(memory, value_weight, value_bias, spatial_shapes, level_start_index,
                                    sampling_locations, attention_weights, mode, value_padding_mask)
-        return out if output_weight is None else torch.nn.functional.linear(out, output_weight, output_bias)
+        if output_weight is None:
+            return out
+        _native.check_output_proj(output_weight, output_bias, out.shape[-1], out)
+        return linear_train(out, output_weight, output_bias)
     if mode == 'project':
         # output_proj, if any, in the same library call
         return _native.project_forward(memory, value_weight, value_bias, spatial_shapes, level_start_index,

@@ -52,6 +52,9 @@ SIGNATURES = {
                                         _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp, _cp, _sz]),
     'td_project_forward_noalloc': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                          _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _cp, _sz]),
+    'td_linear_grad_workspace_bytes': (_sz, [_ip, _i64, _i64]),
+    'td_linear_grad_input': (_ip, [_ip, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _cp, _sz]),
+    'td_linear_grad_weight': (_ip, [_ip, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp, _cp, _sz]),
     'td_probe_row_gather': (_ip, [_vp, _i64, _ip, _ip, _i64, ctypes.c_uint, _vp, _sz, _ip, _vp, _cp, _sz]),
     'td_set_kernel_policy': (_ip, [_ip]),
     'td_device_error': (_ip, [_ip, ctypes.POINTER(ctypes.c_uint), _cp, _sz]),
@@ -569,3 +572,46 @@ def probe_row_gather(buf, row_bytes, visits, wide=False, seed=12345, grid=None, 
         _call(lib.td_probe_row_gather, _ptr(buf), rows, row_bytes, 1 if wide else 0, visits, seed, _ptr(sink),
               sink.numel() * 4, grid, _stream(dev))
     return visits
+
+
+def linear_grad_input(grad_out, weight):
+    """grad_out [..., Nout] @ weight [Nout, K] -> [..., K] through td_linear_grad_input: the input gradient of
+    y = x @ weight.T (+ b)."""
+    lib = load()
+    Nout, K = weight.shape
+    if grad_out.size(-1) != Nout or grad_out.dtype != weight.dtype or grad_out.device != weight.device:
+        raise RuntimeError('grad_out must be [..., Nout] with the dtype and device of weight [Nout, K]')
+    if grad_out.dtype not in DTYPE_CODE:
+        raise RuntimeError(f'unsupported dtype {grad_out.dtype}')
+    g, w = _dense(grad_out, weight)
+    out = torch.empty(tuple(grad_out.shape[:-1]) + (K,), dtype=weight.dtype, device=weight.device)
+    M = g.numel() // Nout
+    if M == 0:
+        return out
+    with torch.cuda.device(weight.device):
+        _call(lib.td_linear_grad_input, DTYPE_CODE[weight.dtype], _ptr(g), _ptr(w), _ptr(out), M, Nout, K,
+              _stream(weight.device))
+    return out
+
+
+def linear_grad_weight(grad_out, x, with_bias=False):
+    """(grad_out^T @ x [Nout, K], the column sums of grad_out [Nout] or None) over every row of grad_out [..., Nout]
+    and x [..., K], through td_linear_grad_weight: the weight and bias gradients of y = x @ weight.T + b."""
+    lib = load()
+    Nout, K = grad_out.size(-1), x.size(-1)
+    if grad_out.dtype != x.dtype or grad_out.device != x.device or grad_out.numel() // max(Nout, 1) != \
+            x.numel() // max(K, 1):
+        raise RuntimeError('grad_out and x must have the same rows, dtype and device')
+    if x.dtype not in DTYPE_CODE:
+        raise RuntimeError(f'unsupported dtype {x.dtype}')
+    g, xs = _dense(grad_out, x)
+    M = g.numel() // Nout
+    code = DTYPE_CODE[x.dtype]
+    grad_w = torch.empty((Nout, K), dtype=x.dtype, device=x.device)
+    grad_b = torch.empty((Nout,), dtype=x.dtype, device=x.device) if with_bias else None
+    ws_bytes = lib.td_linear_grad_workspace_bytes(code, Nout, K)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
+    with torch.cuda.device(x.device):
+        _call(lib.td_linear_grad_weight, code, _ptr(g), _ptr(xs), _ptr(grad_w), _ptr(grad_b), M, Nout, K, _ptr(ws),
+              ws_bytes, _stream(x.device))
+    return grad_w, grad_b

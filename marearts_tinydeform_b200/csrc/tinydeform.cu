@@ -7,7 +7,9 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
+#include <initializer_list>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -19,6 +21,7 @@
 #include "td_fused_tc.cuh"
 #include "td_gemm_simt.cuh"
 #include "td_gemm_tc.cuh"
+#include "td_gemm_grad.cuh"
 #include "td_producer.cuh"
 #include "td_backward.cuh"
 #include "td_sampler.cuh"
@@ -679,6 +682,109 @@ int launch_proj_pair(const ProjShape& j0, const ProjShape& j1, cudaStream_t stre
     }
 }
 
+// ---- the GEMMs of a linear layer's backward (td_linear_grad_input / td_linear_grad_weight) ----------------------
+
+// Whether the tcgen05 gradient kernels take these operands: 16-bit types, every row 16-byte aligned (the TMA rule),
+// sizes in int range.
+template <typename T>
+bool grad_tc_eligible(std::initializer_list<const void*> ptrs, int64_t M, int64_t Nout, int64_t K) {
+    if constexpr (!std::is_same<T, __half>::value && !std::is_same<T, __nv_bfloat16>::value) {
+        return false;
+    } else {
+        if (g_policy.load(std::memory_order_relaxed) != TD_POLICY_BEST) return false;
+        if (Nout % 8 != 0 || K % 8 != 0 || M >= (int64_t(1) << 31) || Nout >= (int64_t(1) << 31) ||
+            K >= (int64_t(1) << 31))
+            return false;
+        for (const void* p : ptrs)
+            if (!aligned16(p)) return false;
+        return true;
+    }
+}
+
+template <typename T, bool A_MN, int BN, bool SPLIT>
+int launch_grad_tc(const void* a_ptr, uint64_t a_cols, uint64_t a_rows, uint32_t a_box_rows, const void* b_ptr,
+                   uint64_t b_cols, uint64_t b_rows, const GradGemmArgs<T>& args, cudaStream_t stream, char* err,
+                   size_t err_len) {
+    using Lay = GradTcLayout<BN>;
+    static std::atomic<uint64_t> smem_done{0};
+    CUtensorMap map_a, map_b;
+    if (int rc = tensor_map_2d(&map_a, a_ptr, a_cols, a_rows, a_box_rows, err, err_len, 2)) return rc;
+    if (int rc = tensor_map_2d(&map_b, b_ptr, b_cols, b_rows, 64, err, err_len, 2)) return rc;
+    if (int rc = allow_smem(grad_gemm_tc_kernel<T, A_MN, BN, SPLIT>, Lay::kSmemBytes, smem_done, err, err_len))
+        return rc;
+    const unsigned grid = unsigned(args.m_tiles * args.n_tiles * args.splits);
+    const cudaError_t e = launch_kernel(grad_gemm_tc_kernel<T, A_MN, BN, SPLIT>, dim3(grid), dim3(Lay::kThreads),
+                                        Lay::kSmemBytes, stream, true, map_a, map_b, args);
+    if (e != cudaSuccess)
+        return fail(err, err_len, TD_ERR_CUDA, "grad_gemm_tc_kernel launch: %s", cudaGetErrorString(e));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return check_launch(err, err_len, "grad_gemm_tc_kernel");
+}
+
+template <typename T, bool ATOMIC>
+int launch_grad_simt(const GradSimtArgs<T>& p, int splits, cudaStream_t stream, char* err, size_t err_len) {
+    const dim3 grid(unsigned((p.rows + 63) / 64), unsigned((p.cols + 63) / 64), unsigned(splits));
+    const cudaError_t e = launch_kernel(grad_gemm_simt_kernel<T, ATOMIC>, grid, dim3(256), 0, stream, true, p);
+    if (e != cudaSuccess)
+        return fail(err, err_len, TD_ERR_CUDA, "grad_gemm_simt_kernel launch: %s", cudaGetErrorString(e));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return check_launch(err, err_len, "grad_gemm_simt_kernel");
+}
+
+// Splits of a K range of k_blocks blocks over CTAs: enough to give the SMs about one CTA each, none shorter than
+// min_blocks blocks, none empty. Returns the splits and sets *per (blocks per split).
+inline int grad_splits(int64_t tiles, int64_t k_blocks, int sm_count, int64_t min_blocks, int64_t* per) {
+    int64_t splits = std::max<int64_t>(1, std::min<int64_t>(sm_count / std::max<int64_t>(tiles, 1),
+                                                           k_blocks / std::max<int64_t>(min_blocks, 1)));
+    *per = (k_blocks + splits - 1) / splits;
+    splits = (k_blocks + *per - 1) / *per;
+    return int(std::max<int64_t>(splits, 1));
+}
+
+// Workspace of td_linear_grad_weight, laid out as: float32 accumulator [Nout, K] | arrival counters | float32 bias
+// sums [Nout] | bias arrival counters; every region 256-byte aligned (16-bit types only; float32 / float64
+// accumulate in the outputs themselves).
+struct GradWeightWs {
+    size_t acc = 0, arrivals = 0, bias = 0, bias_arrivals = 0, total = 0;
+};
+inline GradWeightWs grad_weight_ws(int dtype, int64_t Nout, int64_t K) {
+    GradWeightWs w;
+    if (dtype != TD_F16 && dtype != TD_BF16) return w;
+    auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+    const size_t tiles = size_t((Nout + 127) / 128) * size_t((K + 127) / 128);
+    w.acc = 0;
+    w.arrivals = up(size_t(Nout) * size_t(K) * 4);
+    w.bias = w.arrivals + up(tiles * 4);
+    w.bias_arrivals = w.bias + up(size_t(Nout) * 4);
+    w.total = w.bias_arrivals + up(size_t((Nout + 255) / 256) * 4) + 256;  // + 256: alignment of the base
+    return w;
+}
+
+// Column sums of x [rows, cols] into out [cols] (the input type), through float32 (float64) `sums` and, for 16-bit
+// types, a conversion by the last CTA of each column block (`arrivals`, one counter per column block). sums and
+// arrivals are zeroed here.
+template <typename T>
+int launch_column_sum(const T* x, T* out, typename Elem<T>::acc* sums, unsigned* arrivals, int64_t rows, int64_t cols,
+                      cudaStream_t stream, char* err, size_t err_len) {
+    using A = typename Elem<T>::acc;
+    DeviceFacts f;
+    if (int rc = device_facts(&f, err, err_len)) return rc;
+    cudaError_t e = cudaMemsetAsync(sums, 0, size_t(cols) * sizeof(A), stream);
+    const int64_t col_blocks = (cols + 255) / 256;
+    if (e == cudaSuccess && arrivals != nullptr) e = cudaMemsetAsync(arrivals, 0, size_t(col_blocks) * 4, stream);
+    if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    const int64_t row_blocks = std::max<int64_t>(1, std::min<int64_t>((rows + 63) / 64, 2 * f.sm_count / col_blocks));
+    const long long per = (long long)((rows + row_blocks - 1) / row_blocks);
+    const dim3 grid(unsigned(col_blocks), unsigned((rows + per - 1) / per));
+    e = launch_kernel(column_sum_kernel<T>, grid, dim3(256), 0, stream, true, x, sums,
+                      std::is_same<A, T>::value ? static_cast<T*>(nullptr) : out, arrivals, (long long)rows,
+                      int(cols), per);
+    if (e != cudaSuccess)
+        return fail(err, err_len, TD_ERR_CUDA, "column_sum_kernel launch: %s", cudaGetErrorString(e));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return check_launch(err, err_len, "column_sum_kernel");
+}
+
 template <typename F>
 int dispatch(int dtype, F&& f) {
     switch (dtype) {
@@ -899,6 +1005,134 @@ int td_sampling_producer(int dtype, const void* proj, const void* reference_poin
         return launch_producer<T>(static_cast<const T*>(proj), static_cast<const T*>(reference_points), ref_dim,
                                   spatial_shapes, static_cast<T*>(sampling_locations),
                                   static_cast<T*>(attention_weights), B, Q, H, L, P, s, err, err_len);
+    });
+}
+
+size_t td_linear_grad_workspace_bytes(int dtype, int64_t Nout, int64_t K) {
+    if (dtype_size(dtype) == 0 || Nout <= 0 || K <= 0) return 0;
+    return grad_weight_ws(dtype, Nout, K).total;
+}
+
+int td_linear_grad_input(int dtype, const void* grad_out, const void* weight, void* grad_input, int64_t M,
+                         int64_t Nout, int64_t K, void* stream, char* err, size_t err_len) {
+    if (dtype_size(dtype) == 0) return fail(err, err_len, TD_ERR_ARG, "unsupported dtype code %d", dtype);
+    if (M < 0 || Nout <= 0 || K <= 0) return fail(err, err_len, TD_ERR_ARG, "linear grad needs M >= 0, Nout, K > 0");
+    if (M > INT32_MAX || Nout > INT32_MAX || K > INT32_MAX) return fail(err, err_len, TD_ERR_ARG, "size too large");
+    if (M == 0) return TD_OK;
+    if (!grad_out || !weight || !grad_input) return fail(err, err_len, TD_ERR_ARG, "null tensor pointer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return dispatch(dtype, [&](auto tag) {
+        using T = decltype(tag);
+        if (grad_tc_eligible<T>({grad_out, weight, grad_input}, M, Nout, K)) {
+            if constexpr (std::is_same<T, __half>::value || std::is_same<T, __nv_bfloat16>::value) {
+                DeviceFacts f;
+                if (int rc = device_facts(&f, err, err_len)) return rc;
+                GradGemmArgs<T> g{};
+                g.out = static_cast<T*>(grad_input);
+                g.rows = int(M);
+                g.cols = int(K);
+                g.m_tiles = int((M + 127) / 128);
+                g.splits = 1;
+                g.k_blocks = int((Nout + 63) / 64);
+                g.kb_per_split = g.k_blocks;
+                // A = grad_out [M, Nout] (K-major, 128-row boxes), B = weight [Nout, K] (MN-major)
+                if (int64_t(g.m_tiles) * ((K + 127) / 128) <= f.sm_count || K <= 128) {
+                    g.n_tiles = int((K + 127) / 128);
+                    return launch_grad_tc<T, false, 128, false>(grad_out, uint64_t(Nout), uint64_t(M), 128, weight,
+                                                                uint64_t(K), uint64_t(Nout), g, s, err, err_len);
+                }
+                g.n_tiles = int((K + 255) / 256);
+                return launch_grad_tc<T, false, 256, false>(grad_out, uint64_t(Nout), uint64_t(M), 128, weight,
+                                                            uint64_t(K), uint64_t(Nout), g, s, err, err_len);
+            }
+        }
+        GradSimtArgs<T> p{};
+        p.a = static_cast<const T*>(grad_out);
+        p.b = static_cast<const T*>(weight);
+        p.out = static_cast<T*>(grad_input);
+        p.sam = Nout; p.sak = 1; p.sbk = K; p.sbn = 1;
+        p.rows = int(M); p.cols = int(K); p.K = Nout; p.k_per_split = (Nout + 15) / 16 * 16;
+        return launch_grad_simt<T, false>(p, 1, s, err, err_len);
+    });
+}
+
+int td_linear_grad_weight(int dtype, const void* grad_out, const void* input, void* grad_weight, void* grad_bias,
+                          int64_t M, int64_t Nout, int64_t K, void* workspace, size_t workspace_bytes, void* stream,
+                          char* err, size_t err_len) {
+    if (dtype_size(dtype) == 0) return fail(err, err_len, TD_ERR_ARG, "unsupported dtype code %d", dtype);
+    if (M < 0 || Nout <= 0 || K <= 0) return fail(err, err_len, TD_ERR_ARG, "linear grad needs M >= 0, Nout, K > 0");
+    if (M > INT32_MAX || Nout > INT32_MAX || K > INT32_MAX || Nout * K > INT32_MAX)
+        return fail(err, err_len, TD_ERR_ARG, "size too large");
+    if (!grad_weight || (M > 0 && (!grad_out || !input))) return fail(err, err_len, TD_ERR_ARG, "null tensor pointer");
+    const GradWeightWs w = grad_weight_ws(dtype, Nout, K);
+    if (w.total > 0 && (workspace == nullptr || workspace_bytes < w.total))
+        return fail(err, err_len, TD_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", w.total,
+                    workspace_bytes);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    unsigned char* ws =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+    return dispatch(dtype, [&](auto tag) {
+        using T = decltype(tag);
+        using A = typename Elem<T>::acc;
+        constexpr bool k16 = std::is_same<T, __half>::value || std::is_same<T, __nv_bfloat16>::value;
+        if (M == 0) {  // no rows: zero gradients
+            cudaError_t e = cudaMemsetAsync(grad_weight, 0, size_t(Nout) * size_t(K) * sizeof(T), s);
+            if (e == cudaSuccess && grad_bias) e = cudaMemsetAsync(grad_bias, 0, size_t(Nout) * sizeof(T), s);
+            if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+            return int(TD_OK);
+        }
+        if (grad_bias) {
+            A* sums = k16 ? reinterpret_cast<A*>(ws + w.bias) : static_cast<A*>(grad_bias);
+            unsigned* arr = k16 ? reinterpret_cast<unsigned*>(ws + w.bias_arrivals) : nullptr;
+            if (int rc = launch_column_sum<T>(static_cast<const T*>(grad_out), static_cast<T*>(grad_bias), sums, arr,
+                                              M, Nout, s, err, err_len))
+                return rc;
+        }
+        DeviceFacts f;
+        if (int rc = device_facts(&f, err, err_len)) return rc;
+        if constexpr (k16) {
+            if (grad_tc_eligible<T>({grad_out, input, grad_weight}, M, Nout, K)) {
+                GradGemmArgs<T> g{};
+                g.out = static_cast<T*>(grad_weight);
+                g.acc = reinterpret_cast<float*>(ws + w.acc);
+                g.arrivals = reinterpret_cast<unsigned*>(ws + w.arrivals);
+                g.rows = int(Nout);
+                g.cols = int(K);
+                g.m_tiles = int((Nout + 127) / 128);
+                g.n_tiles = int((K + 127) / 128);
+                int64_t per = 0;
+                g.k_blocks = int((M + 63) / 64);
+                g.splits = grad_splits(int64_t(g.m_tiles) * g.n_tiles, g.k_blocks, f.sm_count, 4, &per);
+                g.kb_per_split = int(per);
+                cudaError_t e = cudaMemsetAsync(g.acc, 0, size_t(Nout) * size_t(K) * 4, s);
+                if (e == cudaSuccess)
+                    e = cudaMemsetAsync(g.arrivals, 0, size_t(g.m_tiles) * size_t(g.n_tiles) * 4, s);
+                if (e != cudaSuccess)
+                    return fail(err, err_len, TD_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+                // A = grad_out [M, Nout] and B = input [M, K], both MN-major (the sum runs over their M rows)
+                return launch_grad_tc<T, true, 128, true>(grad_out, uint64_t(Nout), uint64_t(M), 64, input,
+                                                          uint64_t(K), uint64_t(M), g, s, err, err_len);
+            }
+        }
+        GradSimtArgs<T> p{};
+        p.a = static_cast<const T*>(grad_out);
+        p.b = static_cast<const T*>(input);
+        p.out = static_cast<T*>(grad_weight);
+        p.sam = 1; p.sak = Nout; p.sbk = K; p.sbn = 1;
+        p.rows = int(Nout); p.cols = int(K); p.K = M;
+        if constexpr (k16) {
+            // 16-bit shapes the tensor cores do not take: one pass over all rows per tile, no atomics
+            p.k_per_split = (M + 15) / 16 * 16;
+            return launch_grad_simt<T, false>(p, 1, s, err, err_len);
+        } else {
+            const int64_t tiles = ((Nout + 63) / 64) * ((K + 63) / 64);
+            int64_t per = 0;
+            const int splits = grad_splits(tiles, (M + 15) / 16, 2 * f.sm_count, 16, &per);
+            p.k_per_split = per * 16;
+            const cudaError_t e = cudaMemsetAsync(grad_weight, 0, size_t(Nout) * size_t(K) * sizeof(T), s);
+            if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+            return launch_grad_simt<T, true>(p, splits, s, err, err_len);
+        }
     });
 }
 

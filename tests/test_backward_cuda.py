@@ -191,3 +191,60 @@ def test_grad_value_finish(cuda):
             assert torch.allclose(bias.double(), want, atol=1e-3 * max(1.0, rows ** 0.5), rtol=1e-5), \
                 f'{rows}x{HD} {dtype}: bias'
     assert _native.grad_value_finish(torch.zeros(4, 6, device=cuda), torch.float16, True) is None
+
+
+LINEAR_GRAD_TOL = {torch.float16: 2e-3, torch.bfloat16: 1e-2, torch.float32: 2e-5, torch.float64: 1e-12}
+
+
+@pytest.mark.parametrize('dtype', [torch.float16, torch.bfloat16, torch.float32, torch.float64])
+def test_linear_gradients(policy, dtype):
+    """td_linear_grad_input and td_linear_grad_weight (+ the bias column sums) against float64 torch on the same
+    rounded inputs: the operator backward's shapes (c1h: 8400 tokens; c3: 67200 tokens, many K splits), output_proj
+    (300 x 256), and ragged shapes (Nout, K not multiples of the 128-wide tiles or the 64-deep K blocks, token counts
+    not multiples of 64), on tensor cores (16-bit types) and on CUDA cores."""
+    g = torch.Generator(device='cuda').manual_seed(17)
+    for M, Nout, K in ((8400, 256, 256), (67200, 256, 256), (300, 256, 256), (1000, 200, 136), (130, 48, 32),
+                       (37, 8, 24)):
+        if dtype == torch.float64 and M > 10000:
+            continue
+        go = torch.randn(M, Nout, generator=g, device='cuda').to(dtype)
+        x = torch.randn(M, K, generator=g, device='cuda').to(dtype)
+        w = (torch.randn(Nout, K, generator=g, device='cuda') / K ** 0.5).to(dtype)
+        with torch.inference_mode():
+            gi = _native.linear_grad_input(go, w)
+            gw, gb = _native.linear_grad_weight(go, x, with_bias=True)
+        want_i = go.double() @ w.double()
+        want_w = go.double().t() @ x.double()
+        want_b = go.double().sum(0)
+        tol = LINEAR_GRAD_TOL[dtype]
+        tag = f'{dtype} {policy} M{M} Nout{Nout} K{K}'
+        for got, want, what in ((gi, want_i, 'grad_input'), (gw, want_w, 'grad_weight'), (gb, want_b, 'grad_bias')):
+            assert got.dtype == dtype and got.shape == want.shape, f'{tag} {what}'
+            err = (got.double() - want).abs().max().item()
+            assert err <= tol * max(1.0, want.abs().max().item()), f'{tag} {what}: max |diff| {err:.3g}'
+    torch.cuda.synchronize()
+    assert _native.device_error(clear=True) == 0
+
+
+def test_backward_runs_only_library_kernels(cuda):
+    """One training step of the operator (project and fused order, with output_proj) through the profiler: every
+    GPU kernel of the backward is this library's (no cuBLAS / cuDNN GEMM), besides torch's own elementwise work."""
+    args = make(1, 300, 8, 32, 256, [(80, 80), (40, 40), (20, 20)], 4, dtype=torch.float16, seed=9)
+    x = [t.cuda().requires_grad_(True) if t is not None and t.is_floating_point() else
+         (t.cuda() if t is not None else None) for t in args]
+    wo = (torch.randn(256, 256, device='cuda') / 16).half().requires_grad_(True)
+    for mode in ('project', 'fused'):
+        out = ma_deform_attn(*x, mode=mode, output_weight=wo)
+        g = torch.randn_like(out)
+        with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+            out.backward(g)
+            torch.cuda.synchronize()
+        names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+        gemm_like = [n for n in names if any(k in n.lower() for k in ('gemm', 'cublas', 'cutlass', 'sm90_', 'sm100_',
+                                                                      'nvjet', 'xmma'))
+                     and 'grad_gemm' not in n]
+        assert not gemm_like, f'{mode}: library GEMMs in the backward: {sorted(set(gemm_like))}'
+        assert any('grad_gemm_tc_kernel' in n for n in names), f'{mode}: {sorted(set(names))}'
+        for t in x + [wo]:
+            if t is not None and t.grad is not None:
+                t.grad = None
