@@ -19,6 +19,7 @@
 #include "td_common.cuh"
 #include "td_fused_simt.cuh"
 #include "td_fused_tc.cuh"
+#include "td_fused_warp.cuh"
 #include "td_gemm_simt.cuh"
 #include "td_gemm_tc.cuh"
 #include "td_gemm_grad.cuh"
@@ -238,6 +239,31 @@ int launch_fused_tc(const T* memory, const T* weight, const T* bias, const int64
     return launch_fused_tc_cfg<T, 4>(map_w, a, f.sm_count, smem, stream, err, err_len);
 }
 
+// Fused order, one warp per row (td_fused_warp.cuh); *launched stays false when the shapes do not fit it: rows of
+// C * e = 512 or 1024 bytes (wider rows would spill the 96 registers a thread has at 20 warps per SM), D = 32 or 64,
+// 16-byte aligned memory and weights.
+template <typename T>
+int launch_fused_warp(const FusedWarpArgs<T>& a, int64_t C, int64_t D, cudaStream_t stream, char* err, size_t err_len,
+                      bool* launched) {
+    *launched = false;
+    const int64_t row_bytes = C * int64_t(sizeof(T));
+    if ((row_bytes != 512 && row_bytes != 1024) || (D != 32 && D != 64) || !aligned16(a.memory) ||
+        !aligned16(a.weight))
+        return TD_OK;
+    const int CV = int(row_bytes / 512);
+    const dim3 grid(unsigned((a.rows + kFwWarps - 1) / kFwWarps));
+    auto go = [&](auto kernel) {
+        *launched = true;
+        const cudaError_t e = launch_kernel(kernel, grid, dim3(kFwWarps * 32), 0, stream, true, a);
+        if (e != cudaSuccess)
+            return fail(err, err_len, TD_ERR_CUDA, "fused_warp_kernel launch: %s", cudaGetErrorString(e));
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+        return check_launch(err, err_len, "fused_warp_kernel");
+    };
+    if (D == 32) return CV == 1 ? go(fused_warp_kernel<T, 1, 1>) : go(fused_warp_kernel<T, 2, 1>);
+    return CV == 1 ? go(fused_warp_kernel<T, 1, 2>) : go(fused_warp_kernel<T, 2, 2>);
+}
+
 template <typename T>
 int launch_fused(const T* memory, const T* weight, const T* bias, const int64_t* shapes, const int64_t* starts,
                  const T* loc, const T* attn, T* out, int64_t B, int64_t Q, int64_t N, int64_t C, int64_t H,
@@ -246,6 +272,17 @@ int launch_fused(const T* memory, const T* weight, const T* bias, const int64_t*
     using A = typename Elem<T>::acc;
     DeviceFacts f;
     if (int rc = device_facts(&f, err, err_len)) return rc;
+    if constexpr (!std::is_same<T, double>::value) {
+        if (g_policy.load(std::memory_order_relaxed) == TD_POLICY_BEST) {
+            FusedWarpArgs<T> w;
+            w.memory = memory; w.weight = weight; w.bias = bias; w.loc = loc; w.attn = attn; w.out = out;
+            w.shapes = shapes; w.starts = starts; w.mask = mask; w.n_tok = N; w.rows = B * H * Q;
+            w.Q = int(Q); w.C = int(C); w.H = int(H); w.L = int(L); w.P = int(P);
+            bool launched = false;
+            const int rc = launch_fused_warp<T>(w, C, D, stream, err, err_len, &launched);
+            if (rc != TD_OK || launched) return rc;
+        }
+    }
     if constexpr (std::is_same<T, __half>::value || std::is_same<T, __nv_bfloat16>::value) {
         // tcgen05 path: N = D a multiple of 16, whole 64-wide K blocks, 16-byte aligned rows and outputs
         if (g_policy.load(std::memory_order_relaxed) == TD_POLICY_BEST && D % 16 == 0 && D <= 256 && C % 64 == 0 &&
