@@ -271,6 +271,17 @@ TD_API int td_linear_grad_weight(int dtype, const void* grad_out, const void* in
                                  size_t workspace_bytes, void* stream, char* err, size_t err_len);
 
 /*
+ * Test of the bounded waits (no counterpart in upstream): every wait of the tensor-core kernels on a TMA or MMA
+ * completion gives up after about a second, records a code in the device error word (td_device_error) and lets the
+ * kernel free its tensor memory and exit, so that a stuck pipeline ends in an error status rather than a hung GPU.
+ * This call makes the NEXT float16 / bfloat16 tensor-core launch of td_linear_grad_input / td_linear_grad_weight
+ * starve its own pipeline -- its TMA producers issue nothing, so no copy or MMA is ever in flight -- and give up
+ * each wait after spin_limit_cycles (1 .. 2e9) instead: its output is left unwritten, the error word holds the code
+ * of the first wait that ran out, and later launches are ordinary. Returns TD_ERR_ARG for a limit out of range.
+ */
+TD_API int td_test_starve_next_grad_gemm(long long spin_limit_cycles);
+
+/*
  * Measurement kernel (no counterpart in upstream): reads `visits` pseudo-random rows of row_bytes (a power of two,
  * 16..512; 32..512 with wide = 1, which uses 32-byte loads) from buf ([rows, row_bytes], 16- or 32-byte aligned)
  * with every SM, the way the sampler reads corner rows, and writes one 16-byte word per thread into sink

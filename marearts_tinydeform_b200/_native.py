@@ -55,6 +55,7 @@ SIGNATURES = {
     'td_linear_grad_workspace_bytes': (_sz, [_ip, _i64, _i64]),
     'td_linear_grad_input': (_ip, [_ip, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _cp, _sz]),
     'td_linear_grad_weight': (_ip, [_ip, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp, _cp, _sz]),
+    'td_test_starve_next_grad_gemm': (_ip, [ctypes.c_longlong]),
     'td_probe_row_gather': (_ip, [_vp, _i64, _ip, _ip, _i64, ctypes.c_uint, _vp, _sz, _ip, _vp, _cp, _sz]),
     'td_set_kernel_policy': (_ip, [_ip]),
     'td_device_error': (_ip, [_ip, ctypes.POINTER(ctypes.c_uint), _cp, _sz]),

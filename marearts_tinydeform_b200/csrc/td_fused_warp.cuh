@@ -22,6 +22,8 @@
 // 16 or 17 rows in one wave.
 #pragma once
 
+#include <type_traits>
+
 #include "td_common.cuh"
 #include "td_ptx.cuh"
 
@@ -45,6 +47,9 @@ struct FusedWarpArgs {
 
 constexpr int kFwWarps = 2;
 
+// What a corner outside the map reads: zeros, as many bytes as the widest row the kernel takes.
+__device__ __align__(16) const uint4 g_fw_zero_row[64] = {};
+
 // CV: 16-byte vectors per lane per corner row (C * sizeof(T) = 512 * CV, CV = 1 or 2). DW: outputs per lane
 // (D = 32 * DW). 96 registers a thread at 10 CTAs per SM, no spills.
 template <typename T, int CV, int DW>
@@ -52,7 +57,10 @@ __global__ void __launch_bounds__(kFwWarps * 32, 10) fused_warp_kernel(const Fus
     constexpr int V = Elem<T>::kVec;      // elements per 16-byte vector
     constexpr int D = 32 * DW;
     constexpr int kB = 16 / CV;           // corner rows in flight per lane
-    __shared__ int s_tok[kFwWarps][kMaxCorners];
+    constexpr int kRowBytes = 512 * CV;
+    // per corner: the address of its memory row (or of the zero row) and its weight; the list is padded with
+    // zero-weight entries on the zero row to a multiple of kB, so the gather loop needs no bounds test
+    __shared__ const unsigned char* s_ptr[kFwWarps][kMaxCorners];
     __shared__ float s_wt[kFwWarps][kMaxCorners];
 
     grid_dependency_wait();
@@ -64,48 +72,54 @@ __global__ void __launch_bounds__(kFwWarps * 32, 10) fused_warp_kernel(const Fus
     const long long bh = row / a.Q;
     const int h = int(bh % a.H);
     const long long b = bh / a.H;
-    const int LP = a.L * a.P, S = 4 * LP;
-    int* tok = s_tok[warp];
+    const int LP = a.L * a.P, S = 4 * LP, S_pad = (S + kB - 1) / kB * kB;
+    const unsigned char** ptr = s_ptr[warp];
     float* wt = s_wt[warp];
+    const unsigned char* zero = reinterpret_cast<const unsigned char*>(g_fw_zero_row);
 
     // 1. corners of the row's points (loc / attn are [B, Q, H, L, P])
     {
         const uint8_t* mask_b = a.mask != nullptr ? a.mask + b * a.n_tok : nullptr;
+        const unsigned char* mb = reinterpret_cast<const unsigned char*>(a.memory + b * a.n_tok * a.C);
         const long long base = ((b * a.Q + q) * a.H + h) * LP;
         for (int j = lane; j < LP; j += 32) {
             const Level lv = level_at(a.shapes, a.starts, j / a.P);
             const long long i = base + j;
-            corners4<float>(to_acc(a.loc[2 * i]), to_acc(a.loc[2 * i + 1]), to_acc(a.attn[i]), lv, a.n_tok,
-                            tok + 4 * j, wt + 4 * j, mask_b);
+            int tk[4];
+            float w4[4];
+            corners4<float>(to_acc(a.loc[2 * i]), to_acc(a.loc[2 * i + 1]), to_acc(a.attn[i]), lv, a.n_tok, tk, w4,
+                            mask_b);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                ptr[4 * j + k] = tk[k] >= 0 ? mb + (long long)tk[k] * kRowBytes : zero;
+                wt[4 * j + k] = w4[k];
+            }
+        }
+        for (int s = S + lane; s < S_pad; s += 32) {
+            ptr[s] = zero;
+            wt[s] = 0.f;
         }
     }
     __syncwarp();
 
     // 2. gather: lane holds channels [(lane + 32 v) * V, + V) of m_r, v < CV
-    const T* mb = a.memory + b * a.n_tok * a.C + lane * V;
     float acc[CV][V];
 #pragma unroll
     for (int v = 0; v < CV; ++v)
 #pragma unroll
         for (int i = 0; i < V; ++i) acc[v][i] = 0.f;
-    for (int s0 = 0; s0 < S; s0 += kB) {
+    for (int s0 = 0; s0 < S_pad; s0 += kB) {
         uint4 raw[kB][CV];
-        // every load of the batch is issued before the first is used; a corner outside the map (or past the
-        // row's last) loads nothing
+        // every load of the batch is issued before the first is used
 #pragma unroll
         for (int u = 0; u < kB; ++u) {
-            const int s = s0 + u;
-            const int t = s < S ? tok[s] : -1;
+            const uint4* src = reinterpret_cast<const uint4*>(ptr[s0 + u]) + lane;
 #pragma unroll
-            for (int v = 0; v < CV; ++v) {
-                raw[u][v] = make_uint4(0u, 0u, 0u, 0u);
-                if (t >= 0) raw[u][v] = __ldg(reinterpret_cast<const uint4*>(mb + (long long)t * a.C + 32 * v * V));
-            }
+            for (int v = 0; v < CV; ++v) raw[u][v] = __ldg(src + 32 * v);
         }
 #pragma unroll
         for (int u = 0; u < kB; ++u) {
-            const int s = s0 + u;
-            const float w = s < S ? wt[s] : 0.f;  // 0 for a corner outside the map
+            const float w = wt[s0 + u];
 #pragma unroll
             for (int v = 0; v < CV; ++v) {
                 float x[V];
@@ -124,50 +138,51 @@ __global__ void __launch_bounds__(kFwWarps * 32, 10) fused_warp_kernel(const Fus
         for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
     }
 
-    // 4. projection, eight outputs at a time: p[k] = sum over this lane's channels c of W[hD + d0 + k, c] * m_r[c];
-    // three halving steps (lanes 16, 8, 4 apart) leave each lane one output of the eight, d0 + (lane >> 2), summed
-    // over 8 lanes, and two butterfly steps finish the sum over all 32. Lane l keeps output (l & 3) * 8 + (l >> 2)
-    // of every 32 (chunk l & 3 of each group of four chunks).
-    const T* wh = a.weight + (long long)h * D * a.C + lane * V;
-    float mine[DW];
-#pragma unroll
-    for (int c8 = 0; c8 < D / 8; ++c8) {
-        float p[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) p[k] = 0.f;
-#pragma unroll
-        for (int v = 0; v < CV; ++v) {
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                float wv[V];
-                load16<T>(wh + (long long)(c8 * 8 + k) * a.C + 32 * v * V, wv);
-#pragma unroll
-                for (int i = 0; i < V; ++i) p[k] = fmaf(wv[i], acc[v][i], p[k]);
-            }
-        }
-#pragma unroll
-        for (int o = 16, n = 4; o >= 4; o >>= 1, n >>= 1) {
-            const bool upper = (lane & o) != 0;
-#pragma unroll
-            for (int i = 0; i < n; ++i) {
-                const float send = upper ? p[i] : p[i + n];
-                const float keep = upper ? p[i + n] : p[i];
-                p[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-            }
-        }
-        p[0] += __shfl_xor_sync(0xffffffffu, p[0], 2);
-        p[0] += __shfl_xor_sync(0xffffffffu, p[0], 1);
-        if ((c8 & 3) == (lane & 3)) mine[c8 >> 2] = p[0];
-    }
-
-    // 5. + bias * sum of weights, stored: out[b, q, h * D + d]
     T* orow = a.out + ((b * a.Q + q) * a.H + h) * D;
+    {
+        // 4. projection on CUDA cores, eight outputs at a time: p[k] = sum over this lane's channels c of
+        // W[hD + d0 + k, c] * m_r[c]; three halving steps (lanes 16, 8, 4 apart) leave each lane one output of the
+        // eight, d0 + (lane >> 2), summed over 8 lanes, and two butterfly steps finish the sum over all 32. Lane l
+        // keeps output (l & 3) * 8 + (l >> 2) of every 32 (chunk l & 3 of each group of four chunks).
+        const T* wh = a.weight + (long long)h * D * (kRowBytes / int(sizeof(T))) + lane * V;
+        float mine[DW];
 #pragma unroll
-    for (int k = 0; k < DW; ++k) {
-        const int d = 32 * k + (lane & 3) * 8 + (lane >> 2);
-        float v = mine[k];
-        if (a.bias != nullptr) v = fmaf(to_acc(a.bias[h * D + d]), wsum, v);
-        orow[d] = from_acc<T>(v);
+        for (int c8 = 0; c8 < D / 8; ++c8) {
+            float p[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) p[k] = 0.f;
+#pragma unroll
+            for (int v = 0; v < CV; ++v) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    float wv[V];
+                    load16<T>(wh + (c8 * 8 + k) * (kRowBytes / int(sizeof(T))) + 32 * v * V, wv);
+#pragma unroll
+                    for (int i = 0; i < V; ++i) p[k] = fmaf(wv[i], acc[v][i], p[k]);
+                }
+            }
+#pragma unroll
+            for (int o = 16, n = 4; o >= 4; o >>= 1, n >>= 1) {
+                const bool upper = (lane & o) != 0;
+#pragma unroll
+                for (int i = 0; i < n; ++i) {
+                    const float send = upper ? p[i] : p[i + n];
+                    const float keep = upper ? p[i + n] : p[i];
+                    p[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                }
+            }
+            p[0] += __shfl_xor_sync(0xffffffffu, p[0], 2);
+            p[0] += __shfl_xor_sync(0xffffffffu, p[0], 1);
+            if ((c8 & 3) == (lane & 3)) mine[c8 >> 2] = p[0];
+        }
+        // 5. + bias * sum of weights, stored: out[b, q, h * D + d]
+#pragma unroll
+        for (int k = 0; k < DW; ++k) {
+            const int d = 32 * k + (lane & 3) * 8 + (lane >> 2);
+            float v = mine[k];
+            if (a.bias != nullptr) v = fmaf(to_acc(a.bias[h * D + d]), wsum, v);
+            orow[d] = from_acc<T>(v);
+        }
     }
 }
 

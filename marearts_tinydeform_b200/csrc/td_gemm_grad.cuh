@@ -41,6 +41,10 @@ struct GradGemmArgs {
     int m_tiles, n_tiles, splits;
     int k_blocks;         // 64-deep K blocks in all
     int kb_per_split;     // K blocks per split (the last split takes what is left)
+    // Test of the bounded waits (td_test_starve_next_grad_gemm): starve = 1 makes the TMA producer issue nothing,
+    // so that every wait runs out after spin_limit cycles with nothing in flight; 0 in every ordinary launch.
+    int starve;
+    long long spin_limit;  // cycles a wait gives up after (kSpinLimitCycles in ordinary launches)
 };
 
 template <int BN>
@@ -49,8 +53,8 @@ struct GradTcLayout {
     static constexpr uint32_t kBBytes = BN * 128;
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
     static constexpr int kStages = BN == 256 ? 4 : 6;
-    static constexpr uint32_t kBarOffset = kStages * kStageBytes;  // full[S], empty[S], tfull
-    static constexpr uint32_t kSlotOffset = kBarOffset + (2 * kStages + 1) * 8;  // TMEM base, last-arrival flag
+    static constexpr uint32_t kBarOffset = kStages * kStageBytes;  // full[S], empty[S], tfull, drained
+    static constexpr uint32_t kSlotOffset = kBarOffset + (2 * kStages + 2) * 8;  // TMEM base, last-arrival flag
     static constexpr uint32_t kSmemBytes = kSlotOffset + 16 + 1024;  // + slack to align the base to 1024
     static constexpr int kThreads = 256;
     static_assert(BN == 128 || BN == 256, "tile width");
@@ -86,6 +90,7 @@ __global__ void __launch_bounds__(256) grad_gemm_tc_kernel(const __grid_constant
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lay::kBarOffset);
     uint64_t* empty = full + S;
     uint64_t* tfull = empty + S;
+    uint64_t* drained = tfull + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Lay::kSlotOffset);
     uint32_t* last_flag = tmem_slot + 1;
     auto slot_a = [&](int s) { return smem + s * Lay::kStageBytes; };
@@ -108,6 +113,7 @@ __global__ void __launch_bounds__(256) grad_gemm_tc_kernel(const __grid_constant
             mbar_init(&empty[s], 1);
         }
         mbar_init(tfull, 1);
+        mbar_init(drained, 1);
         mbar_fence_init();
         tma_prefetch_desc(&map_a);
         tma_prefetch_desc(&map_b);
@@ -123,12 +129,15 @@ __global__ void __launch_bounds__(256) grad_gemm_tc_kernel(const __grid_constant
     grid_dependency_wait();  // the operands were written by the kernels before this one
     launch_dependents();
 
+    const long long limit = a.spin_limit;
     if (warp == 0) {
         if (lane == 0) {
             const uint64_t pol = l2_evict_first();
-            for (int i = 0; i < nkb; ++i) {
+            const int issue = a.starve ? 0 : nkb;  // the blocks this producer loads
+            int issued = 0;
+            for (int i = 0; i < issue; ++i, ++issued) {
                 const int s = i % S;
-                if (!mbar_wait(&empty[s], uint32_t((i / S) & 1) ^ 1u, kErrSlotWait)) break;
+                if (!mbar_wait_limit(&empty[s], uint32_t((i / S) & 1) ^ 1u, kErrSlotWait, limit)) break;
                 const int k0 = (kb0 + i) * 64;
                 mbar_arrive_expect_tx(&full[s], Lay::kStageBytes);
                 if constexpr (A_MN) {
@@ -142,8 +151,8 @@ __global__ void __launch_bounds__(256) grad_gemm_tc_kernel(const __grid_constant
                     tma_load_2d(slot_b(s) + j * 8192, &map_b, &full[s], n0 + 64 * j, k0, pol);
             }
             // the MMA commit of each slot's last use arrives before the CTA exits
-            for (int i = nkb > S ? nkb - S : 0; i < nkb; ++i)
-                if (!mbar_wait(&empty[i % S], uint32_t((i / S) & 1), kErrSlotWait)) break;
+            for (int i = issued > S ? issued - S : 0; i < issued; ++i)
+                if (!mbar_wait_limit(&empty[i % S], uint32_t((i / S) & 1), kErrSlotWait, limit)) break;
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -153,7 +162,7 @@ __global__ void __launch_bounds__(256) grad_gemm_tc_kernel(const __grid_constant
             bool ok = true;
             for (int i = 0; i < nkb; ++i) {
                 const int s = i % S;
-                if (!mbar_wait(&full[s], uint32_t((i / S) & 1), kErrTmaWait)) {
+                if (!mbar_wait_limit(&full[s], uint32_t((i / S) & 1), kErrTmaWait, limit)) {
                     ok = false;
                     break;
                 }
@@ -166,13 +175,20 @@ __global__ void __launch_bounds__(256) grad_gemm_tc_kernel(const __grid_constant
                             (i | k) != 0);
                 mma_commit(&empty[s]);
             }
-            if (ok) mma_commit(tfull);
+            if (ok) {
+                mma_commit(tfull);
+            } else {
+                // a load never landed: no accumulator for the epilogue, and before the CTA frees TMEM and exits,
+                // every MMA this thread issued has completed
+                mma_commit(drained);
+                mbar_wait_limit(drained, 0u, kErrMmaWait, limit);
+            }
         }
     } else if (warp >= 4) {
         const int quarter = warp & 3;
         const int r = quarter * 32 + lane;  // tile row = TMEM lane
         const int row = m0 + r;
-        const bool ready = __all_sync(0xffffffffu, mbar_wait(tfull, 0u, kErrMmaWait));
+        const bool ready = __all_sync(0xffffffffu, mbar_wait_limit(tfull, 0u, kErrMmaWait, limit));
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < BN / 32 && ready; ++c) {

@@ -75,17 +75,23 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
     return done != 0;
 }
 
-// Wait for the phase with the given parity to complete; false (and the error word set) after ~1 s.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int err_code) {
+// Wait for the phase with the given parity to complete; false (and the error word set) after `limit` cycles.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, unsigned int err_code,
+                                                long long limit) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - t0 > kSpinLimitCycles) {
+        if (clock64() - t0 > limit) {
             record_error(err_code);
             return false;
         }
     }
     return true;
+}
+
+// Wait for the phase with the given parity to complete; false (and the error word set) after ~1 s.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int err_code) {
+    return mbar_wait_limit(bar, parity, err_code, kSpinLimitCycles);
 }
 
 // ---- L2 eviction priority ---------------------------------------------------------------------------------

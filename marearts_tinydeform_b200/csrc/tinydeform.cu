@@ -241,14 +241,14 @@ int launch_fused_tc(const T* memory, const T* weight, const T* bias, const int64
 
 // Fused order, one warp per row (td_fused_warp.cuh); *launched stays false when the shapes do not fit it: rows of
 // C * e = 512 or 1024 bytes (wider rows would spill the 96 registers a thread has at 20 warps per SM), D = 32 or 64,
-// 16-byte aligned memory and weights.
+// 16-byte aligned memory, weights and output.
 template <typename T>
 int launch_fused_warp(const FusedWarpArgs<T>& a, int64_t C, int64_t D, cudaStream_t stream, char* err, size_t err_len,
                       bool* launched) {
     *launched = false;
     const int64_t row_bytes = C * int64_t(sizeof(T));
     if ((row_bytes != 512 && row_bytes != 1024) || (D != 32 && D != 64) || !aligned16(a.memory) ||
-        !aligned16(a.weight))
+        !aligned16(a.weight) || !aligned16(a.out))
         return TD_OK;
     const int CV = int(row_bytes / 512);
     const dim3 grid(unsigned((a.rows + kFwWarps - 1) / kFwWarps));
@@ -738,11 +738,18 @@ bool grad_tc_eligible(std::initializer_list<const void*> ptrs, int64_t M, int64_
     }
 }
 
+// Test of the bounded waits: a positive value makes the next tensor-core gradient launch starve its own pipeline
+// (its producers issue nothing) and give up every wait after that many cycles (td_test_starve_next_grad_gemm).
+std::atomic<long long> g_starve_next{0};
+
 template <typename T, bool A_MN, int BN, bool SPLIT>
 int launch_grad_tc(const void* a_ptr, uint64_t a_cols, uint64_t a_rows, uint32_t a_box_rows, const void* b_ptr,
-                   uint64_t b_cols, uint64_t b_rows, const GradGemmArgs<T>& args, cudaStream_t stream, char* err,
+                   uint64_t b_cols, uint64_t b_rows, GradGemmArgs<T> args, cudaStream_t stream, char* err,
                    size_t err_len) {
     using Lay = GradTcLayout<BN>;
+    const long long starve = g_starve_next.exchange(0);
+    args.starve = starve > 0 ? 1 : 0;
+    args.spin_limit = starve > 0 ? starve : kSpinLimitCycles;
     static std::atomic<uint64_t> smem_done{0};
     CUtensorMap map_a, map_b;
     if (int rc = tensor_map_2d(&map_a, a_ptr, a_cols, a_rows, a_box_rows, err, err_len, 2)) return rc;
@@ -1593,6 +1600,12 @@ int td_probe_row_gather(const void* buf, int64_t rows, int row_bytes, int wide, 
         return fail(err, err_len, TD_ERR_CUDA, "row_gather_probe_kernel launch: %s", cudaGetErrorString(e));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return check_launch(err, err_len, "row_gather_probe_kernel");
+}
+
+int td_test_starve_next_grad_gemm(long long spin_limit_cycles) {
+    if (spin_limit_cycles <= 0 || spin_limit_cycles > kSpinLimitCycles) return TD_ERR_ARG;
+    g_starve_next.store(spin_limit_cycles);
+    return TD_OK;
 }
 
 int td_device_info(int device, int* sm_count, int* cc_major, int* cc_minor, char* err, size_t err_len) {

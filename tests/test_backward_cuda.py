@@ -248,3 +248,33 @@ def test_backward_runs_only_library_kernels(cuda):
         for t in x + [wo]:
             if t is not None and t.grad is not None:
                 t.grad = None
+
+
+def test_a_starved_pipeline_ends_in_an_error_status(cuda):
+    """The bounded waits of a tensor-core kernel, run out on purpose: with td_test_starve_next_grad_gemm the next
+    gradient GEMM's producers issue nothing (no copy, no MMA in flight), every wait gives up after ~1 ms, the kernel
+    records the wait's code, frees its tensor memory and exits. The context stays usable: the error word reads the
+    code, and the next launches of the same kernel and of the projection kernel (which allocate tensor memory on the
+    same SMs) are correct."""
+    lib = _native.load()
+    assert lib.td_test_starve_next_grad_gemm(0) == 1 and lib.td_test_starve_next_grad_gemm(-5) == 1
+    g = torch.Generator(device='cuda').manual_seed(23)
+    go = torch.randn(2048, 256, generator=g, device='cuda').half()
+    x = torch.randn(2048, 192, generator=g, device='cuda').half()
+    torch.cuda.synchronize()
+    assert _native.device_error(clear=True) == 0
+    assert lib.td_test_starve_next_grad_gemm(2_000_000) == 0
+    with torch.inference_mode():
+        _native.linear_grad_weight(go, x)  # starved: its output is not written
+    torch.cuda.synchronize()
+    code = _native.device_error(clear=True)
+    assert code in (1, 2), code  # a TMA wait (kErrTmaWait) or the accumulator wait (kErrMmaWait) ran out first
+    with torch.inference_mode():
+        gw, _ = _native.linear_grad_weight(go, x)
+        w = (torch.randn(256, 192, generator=g, device='cuda') / 16).half()
+        y = _native.linear(x, w, None)
+    torch.cuda.synchronize()
+    assert _native.device_error(clear=True) == 0
+    want = go.double().t() @ x.double()
+    assert (gw.double() - want).abs().max().item() <= 2e-3 * want.abs().max().item()
+    assert torch.allclose(y.double(), x.double() @ w.double().t(), atol=3e-3, rtol=3e-3)
