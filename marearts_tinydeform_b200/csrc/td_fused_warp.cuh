@@ -47,6 +47,16 @@ struct FusedWarpArgs {
 
 constexpr int kFwWarps = 2;
 
+// 16-byte read-only load without L1 allocation: the gathered rows are read about once per SM, while the weight rows
+// the projection reads next are read by every row of the head (c2: 6.15 -> 5.94 us per call, c1h 10.04 -> 9.93).
+__device__ __forceinline__ uint4 ld_nc_no_l1(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
 // What a corner outside the map reads: zeros, as many bytes as the widest row the kernel takes.
 __device__ __align__(16) const uint4 g_fw_zero_row[64] = {};
 
@@ -115,7 +125,7 @@ __global__ void __launch_bounds__(kFwWarps * 32, 10) fused_warp_kernel(const Fus
         for (int u = 0; u < kB; ++u) {
             const uint4* src = reinterpret_cast<const uint4*>(ptr[s0 + u]) + lane;
 #pragma unroll
-            for (int v = 0; v < CV; ++v) raw[u][v] = __ldg(src + 32 * v);
+            for (int v = 0; v < CV; ++v) raw[u][v] = ld_nc_no_l1(src + 32 * v);
         }
 #pragma unroll
         for (int u = 0; u < kB; ++u) {
