@@ -49,6 +49,8 @@ constexpr int kFwWarps = 2;
 
 // 16-byte read-only load without L1 allocation: the gathered rows are read about once per SM, while the weight rows
 // the projection reads next are read by every row of the head (c2: 6.15 -> 5.94 us per call, c1h 10.04 -> 9.93).
+// Used for 512-byte rows only: on 1024-byte rows (float32 C = 256, float16 C = 512) the L1-allocating load measured
+// faster (c5 float16 B1 Q50: 24.7 against 43.9 us).
 __device__ __forceinline__ uint4 ld_nc_no_l1(const void* p) {
     uint4 r;
     asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
@@ -125,7 +127,8 @@ __global__ void __launch_bounds__(kFwWarps * 32, 10) fused_warp_kernel(const Fus
         for (int u = 0; u < kB; ++u) {
             const uint4* src = reinterpret_cast<const uint4*>(ptr[s0 + u]) + lane;
 #pragma unroll
-            for (int v = 0; v < CV; ++v) raw[u][v] = ld_nc_no_l1(src + 32 * v);
+            for (int v = 0; v < CV; ++v)
+                raw[u][v] = CV == 1 ? ld_nc_no_l1(src + 32 * v) : __ldg(src + 32 * v);
         }
 #pragma unroll
         for (int u = 0; u < kB; ++u) {
