@@ -60,15 +60,15 @@ __device__ __forceinline__ uint4 ld_nc_no_l1(const void* p) {
 }
 
 // What a corner outside the map reads: zeros, as many bytes as the widest row the kernel takes.
-__device__ __align__(16) const uint4 g_fw_zero_row[64] = {};
+__device__ __align__(16) const uint4 g_fw_zero_row[128] = {};
 
-// CV: 16-byte vectors per lane per corner row (C * sizeof(T) = 512 * CV, CV = 1 or 2). DW: outputs per lane
+// CV: 16-byte vectors per lane per corner row (C * sizeof(T) = 512 * CV, CV = 1, 2 or 4). DW: outputs per lane
 // (D = 32 * DW). 96 registers a thread at 10 CTAs per SM, no spills.
 template <typename T, int CV, int DW>
 __global__ void __launch_bounds__(kFwWarps * 32, 10) fused_warp_kernel(const FusedWarpArgs<T> a) {
     constexpr int V = Elem<T>::kVec;      // elements per 16-byte vector
     constexpr int D = 32 * DW;
-    constexpr int kB = 16 / CV;           // corner rows in flight per lane
+    constexpr int kB = CV == 4 ? 2 : 16 / CV;  // corner rows in flight per lane
     constexpr int kRowBytes = 512 * CV;
     // per corner: the address of its memory row (or of the zero row) and its weight; the list is padded with
     // zero-weight entries on the zero row to a multiple of kB, so the gather loop needs no bounds test

@@ -240,14 +240,14 @@ int launch_fused_tc(const T* memory, const T* weight, const T* bias, const int64
 }
 
 // Fused order, one warp per row (td_fused_warp.cuh); *launched stays false when the shapes do not fit it: rows of
-// C * e = 512 or 1024 bytes (wider rows would spill the 96 registers a thread has at 20 warps per SM), D = 32 or 64,
-// 16-byte aligned memory, weights and output.
+// C * e = 512, 1024 or 2048 bytes (2048-byte rows keep two rows in flight per lane, to fit 96 registers a thread at
+// 20 warps per SM), D = 32 or 64, 16-byte aligned memory, weights and output.
 template <typename T>
 int launch_fused_warp(const FusedWarpArgs<T>& a, int64_t C, int64_t D, cudaStream_t stream, char* err, size_t err_len,
                       bool* launched) {
     *launched = false;
     const int64_t row_bytes = C * int64_t(sizeof(T));
-    if ((row_bytes != 512 && row_bytes != 1024) || (D != 32 && D != 64) || !aligned16(a.memory) ||
+    if ((row_bytes != 512 && row_bytes != 1024 && row_bytes != 2048) || (D != 32 && D != 64) || !aligned16(a.memory) ||
         !aligned16(a.weight) || !aligned16(a.out))
         return TD_OK;
     const int CV = int(row_bytes / 512);
@@ -260,8 +260,11 @@ int launch_fused_warp(const FusedWarpArgs<T>& a, int64_t C, int64_t D, cudaStrea
         g_launches.fetch_add(1, std::memory_order_relaxed);
         return check_launch(err, err_len, "fused_warp_kernel");
     };
-    if (D == 32) return CV == 1 ? go(fused_warp_kernel<T, 1, 1>) : go(fused_warp_kernel<T, 2, 1>);
-    return CV == 1 ? go(fused_warp_kernel<T, 1, 2>) : go(fused_warp_kernel<T, 2, 2>);
+    if (D == 32)
+        return CV == 1 ? go(fused_warp_kernel<T, 1, 1>)
+                       : (CV == 2 ? go(fused_warp_kernel<T, 2, 1>) : go(fused_warp_kernel<T, 4, 1>));
+    return CV == 1 ? go(fused_warp_kernel<T, 1, 2>)
+                   : (CV == 2 ? go(fused_warp_kernel<T, 2, 2>) : go(fused_warp_kernel<T, 4, 2>));
 }
 
 template <typename T>
