@@ -783,7 +783,11 @@ def main():
     ap.add_argument('--ref-dim', type=int, default=4, choices=(2, 4),
                     help='--layer: reference points (2) or reference boxes (4)')
     ap.add_argument('--dtype', nargs='+', default=['float16', 'bfloat16', 'float32'])
+    ap.add_argument('--as-dtype', choices=('float32', 'float16', 'bfloat16', 'float64'),
+                    help='run the config in this dtype instead of its own (profiling the other kernels)')
     args = ap.parse_args()
+    if args.as_dtype:
+        workloads.CONFIGS[args.config] = dict(workloads.CONFIGS[args.config], dtype=getattr(torch, args.as_dtype))
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == 'reference':

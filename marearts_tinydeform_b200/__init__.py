@@ -47,15 +47,15 @@ MODES = ('auto', 'fused', 'project')
 # 'project' ~ batch * tokens * C * H * D plus a fixed part that matters at batch 1.
 # FUSED_LIMIT and FUSED_LIMIT_SM75 are upstream's tables (RTX 4090 / RTX 2080 Super); FUSED_LIMIT_SM100 is fitted
 # to crossovers measured with this library on B200 (bench.py --sweep over upstream's query/batch grid, c4 and the
-# c5 grid: 114 cases, the pick within 10% of the faster order in all of them), used for compute capability 10.x.
-# On B200 the tensor-core projection (float32 too, as three TF32 products) makes 'project' cheap even at batch 1,
-# while 'fused' pays its per-call latency once for the whole batch, so 'fused' only wins at batch >= 4 with few
-# queries: b is negative (the limit grows with the batch). In float16 / bfloat16 the project order was the faster
-# one in all 76 cases of the sweep (closest: batch 8, 50 queries, 0.98x), so their limit lies below the sweep's
-# smallest ratio (0.0089) and 'fused' is left to batches of a few dozen queries.
+# c5 grid, 114 cases; profiles/auto_sweep_b200.md), used for compute capability 10.x. float32: the pick is within
+# 10 % of the faster order in all 38 cases -- the fused order (a warp per row) wins up to about 300 queries per image
+# at every batch, as the float32 projection runs three TF32 products per K step. float16 / bfloat16: 74 of 76; the
+# fused order wins at 50-100 queries at batch 1-8 (RT-DETR shapes) and at batch 64 with 50 queries (c5), the project
+# order above; no (a, b) also takes DINO batch 1 with 300 queries (fused 10.7 against 13.5 us), since the c5 shapes
+# at batch 4-8 need the limit below its ratio.
 FUSED_LIMIT = {torch.float32: (0.073, 0.032), torch.float16: (0.023, 0.031), torch.bfloat16: (0.023, 0.031)}
 FUSED_LIMIT_SM75 = {torch.float32: (0.068, 0.0), torch.float16: (0.020, 0.0), torch.bfloat16: (0.132, 0.0)}
-FUSED_LIMIT_SM100 = {torch.float32: (0.026, -0.05), torch.float16: (0.008, -0.008), torch.bfloat16: (0.008, -0.008)}
+FUSED_LIMIT_SM100 = {torch.float32: (0.0775, 0.028), torch.float16: (0.024, -0.006), torch.bfloat16: (0.024, -0.006)}
 
 
 @functools.lru_cache(maxsize=None)

@@ -118,9 +118,9 @@ def test_tensor_contract_rejects_cpu_tensors_in_the_native_path():
 
 
 def test_b200_table_picks_the_measured_faster_order(monkeypatch):
-    """The sm_100 table on the BASELINE shapes: 'project' for every BASELINE config (float32 included: its
-    projection runs on the tensor cores too), 'fused' only for float32 with few queries at batch >= 4-8 (in 16-bit
-    types the project order measured faster across the whole sweep, batch 8 with 50 queries included)."""
+    """The sm_100 table on the BASELINE shapes and the sweep's crossovers: 16-bit types take the fused order at 50-100
+    queries (c2: RT-DETR, batch 1, 100 queries) and the project order from 200 queries on (c1h, c3, c4); float32
+    takes the fused order up to 300 queries at every batch and the project order from 600."""
     from marearts_tinydeform_b200 import workloads
     monkeypatch.setattr(td, '_limits', lambda device_index: td.FUSED_LIMIT_SM100)
 
@@ -136,11 +136,16 @@ def test_b200_table_picks_the_measured_faster_order(monkeypatch):
         return choose_mode(FakeCuda(a[0]), a[1], a[5])
 
     assert pick('c1h') == 'project'
-    assert pick('c2') == 'project'
+    assert pick('c2') == 'fused'
     assert pick('c3') == 'project'
     assert pick('c4') == 'project'
-    assert pick('c1h', B=8, Q=50) == 'project'
-    assert pick('c3', Q=50) == 'project'
-    assert pick('c1', Q=300) == 'project'
+    assert pick('c1h', B=8, Q=50) == 'fused'
+    assert pick('c1h', Q=200) == 'project'
+    assert pick('c3', Q=50) == 'fused'
+    assert pick('c5', B=4, Q=50) == 'project'
+    assert pick('c5', B=64, Q=50) == 'fused'
+    assert pick('c1', Q=300) == 'fused'
+    assert pick('c1', Q=600) == 'project'
     assert pick('c1', B=8, Q=100) == 'fused'
-    assert pick('c1', B=4, Q=100) == 'project'
+    assert pick('c1', B=4, Q=300) == 'fused'
+    assert pick('c5', dtype=torch.float32, B=1, Q=300) == 'project'
