@@ -10,7 +10,7 @@
 //
 // 16-bit types run grad_gemm_tc_kernel on tcgen05 tensor cores, one CTA per (output tile of 128 rows x BN columns,
 // K slice):
-//   * warp 0, one lane: TMA producer into a ring of slots, each slot one 64-deep K block of A and of B with the
+//   * warp 0, one lane per box: TMA producers into a ring of slots, each slot one 64-deep K block of A and of B with the
 //     128-byte swizzle: a K-major A is one 64 x 128 box; an MN-major operand is a box of 64 rows of K by 64 columns
 //     of M (or N) per 64 columns -- the canonical MN-major layout, whose atom is 64 elements by 8 K rows (1 KB):
 //     stride byte offset 1024 (the next 8 K rows), leading byte offset 8192 (the next 64 columns, the next box);
@@ -85,6 +85,8 @@ __global__ void __launch_bounds__(256) grad_gemm_tc_kernel(const __grid_constant
                                                            const GradGemmArgs<T> a) {
     using Lay = GradTcLayout<BN>;
     constexpr int S = Lay::kStages;
+    constexpr int kABoxes = A_MN ? 2 : 1;  // MN-major: two 64-column boxes of 64 K rows; K-major: one 64 x 128 box
+    constexpr int kBoxes = kABoxes + BN / 64;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lay::kBarOffset);
@@ -109,7 +111,7 @@ __global__ void __launch_bounds__(256) grad_gemm_tc_kernel(const __grid_constant
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full[s], kBoxes);
             mbar_init(&empty[s], 1);
         }
         mbar_init(tfull, 1);
@@ -131,7 +133,9 @@ __global__ void __launch_bounds__(256) grad_gemm_tc_kernel(const __grid_constant
 
     const long long limit = a.spin_limit;
     if (warp == 0) {
-        if (lane == 0) {
+        // one issuing lane per box of a slot (kBoxes of them: the TMA copies of one thread are served one after
+        // another, those of different threads overlap); each arms the slot's full barrier for its own bytes
+        if (lane < kBoxes) {
             const uint64_t pol = l2_evict_first();
             const int issue = a.starve ? 0 : nkb;  // the blocks this producer loads
             int issued = 0;
@@ -139,20 +143,22 @@ __global__ void __launch_bounds__(256) grad_gemm_tc_kernel(const __grid_constant
                 const int s = i % S;
                 if (!mbar_wait_limit(&empty[s], uint32_t((i / S) & 1) ^ 1u, kErrSlotWait, limit)) break;
                 const int k0 = (kb0 + i) * 64;
-                mbar_arrive_expect_tx(&full[s], Lay::kStageBytes);
-                if constexpr (A_MN) {
-                    tma_load_2d(slot_a(s), &map_a, &full[s], m0, k0, pol);
-                    tma_load_2d(slot_a(s) + 8192, &map_a, &full[s], m0 + 64, k0, pol);
+                if (lane < kABoxes) {
+                    mbar_arrive_expect_tx(&full[s], Lay::kABytes / kABoxes);
+                    if constexpr (A_MN)
+                        tma_load_2d(slot_a(s) + lane * 8192, &map_a, &full[s], m0 + 64 * lane, k0, pol);
+                    else
+                        tma_load_2d(slot_a(s), &map_a, &full[s], k0, m0, pol);
                 } else {
-                    tma_load_2d(slot_a(s), &map_a, &full[s], k0, m0, pol);
-                }
-#pragma unroll
-                for (int j = 0; j < BN / 64; ++j)
+                    const int j = lane - kABoxes;
+                    mbar_arrive_expect_tx(&full[s], 8192u);
                     tma_load_2d(slot_b(s) + j * 8192, &map_b, &full[s], n0 + 64 * j, k0, pol);
+                }
             }
             // the MMA commit of each slot's last use arrives before the CTA exits
-            for (int i = issued > S ? issued - S : 0; i < issued; ++i)
-                if (!mbar_wait_limit(&empty[i % S], uint32_t((i / S) & 1), kErrSlotWait, limit)) break;
+            if (lane == 0)
+                for (int i = issued > S ? issued - S : 0; i < issued; ++i)
+                    if (!mbar_wait_limit(&empty[i % S], uint32_t((i / S) & 1), kErrSlotWait, limit)) break;
         }
     } else if (warp == 1) {
         if (lane == 0) {
