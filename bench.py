@@ -711,6 +711,81 @@ def run_backward(args):
     print(json.dumps(line), flush=True)
 
 
+def load_upstream(path):
+    """Upstream's package from an installed checkout (with its compiled CUDA extension), imported under the name
+    upstream_marearts_tinydeform so that it does not shadow this repository's alias package. (module, None) or
+    (None, why)."""
+    import importlib.util
+    pkg = os.path.join(path, 'marearts_tinydeform')
+    init = os.path.join(pkg, '__init__.py')
+    if not os.path.exists(init):
+        return None, f'no installed marearts_tinydeform package under {path}'
+    spec = importlib.util.spec_from_file_location('upstream_marearts_tinydeform', init,
+                                                  submodule_search_locations=[pkg])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = mod
+    try:
+        spec.loader.exec_module(mod)
+    except Exception as exc:  # an extension built for another torch or CUDA
+        return None, f'upstream package failed to import: {type(exc).__name__}: {exc}'
+    if getattr(mod, '_C', None) is None:
+        return None, 'upstream CUDA extension is not built in ' + pkg
+    return mod, None
+
+
+REFERENCE_CUDA_CASES = [  # (config, overrides)
+    ('c1h', {}), ('c1h', {'Q': 100}), ('c1h', {'B': 8}), ('c1', {}), ('c3', {}), ('c4', {})]
+
+
+def run_reference_cuda(args):
+    """Upstream's own CUDA operator (its fused_forward; its project order = F.linear + sample_forward) against this
+    library's ma_deform_attn (auto), same B200, same harness: a graph of K calls over inputs rotating through a pool
+    larger than 2x L2, median of replays, TF32 off. One JSON line per case; a line with 'unavailable' when upstream's
+    extension is not installed (python -m pip install --no-index --no-build-isolation --no-deps --target
+    baseline/_ref <upstream checkout>, built with TORCH_CUDA_ARCH_LIST=10.0)."""
+    mod, why = load_upstream(args.ref_path)
+    if mod is None:
+        print(json.dumps({'impl': 'reference-cuda', 'unavailable': why}), flush=True)
+        return
+    torch.cuda.set_device(0)
+    dev = torch.device('cuda', 0)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    _native.load()
+    for name, over in REFERENCE_CUDA_CASES:
+        cfg = dict(workloads.CONFIGS[name], **over)
+        saved = workloads.CONFIGS[name]
+        workloads.CONFIGS[name] = cfg
+        try:
+            base, pool = input_pool(name, cfg['B'], dev, 2 * L2_BYTES)
+        finally:
+            workloads.CONFIGS[name] = saved
+        W, bias, shapes, starts = base[1], base[2], base[3], base[4]
+        res = {}
+        with torch.inference_mode():
+            for label, fn, mode in (('upstream_fused', mod.ma_deform_attn, 'fused'),
+                                    ('upstream_project', mod.ma_deform_attn, 'project'),
+                                    ('ours_auto', ma_deform_attn, 'auto')):
+                def call(i, fn=fn, mode=mode):
+                    mem, loc, attn = pool[i % len(pool)]
+                    return fn(mem, W, bias, shapes, starts, loc, attn, mode=mode)
+                g, _ = graph_time_us(call, args.steps, args.warmup)
+                res[label] = round(time_graph(g, args.steps, reps=max(5, args.reps // 5)), 3)
+                del g
+            mem, loc, attn = pool[0]
+            ours = ma_deform_attn(mem, W, bias, shapes, starts, loc, attn).double()
+            theirs = mod.ma_deform_attn(mem, W, bias, shapes, starts, loc, attn, mode='project').double()
+            diff = (ours - theirs).abs().max().item()
+            picked = choose_mode(mem, W, loc)
+        best_ref = min(res['upstream_fused'], res['upstream_project'])
+        print(json.dumps({'impl': 'reference-cuda', 'case': f'{name} {over}' if over else name,
+                          'dtype': str(cfg['dtype']).replace('torch.', ''), 'B': cfg['B'], 'Q': cfg['Q'],
+                          'us_per_call': res, 'ours_mode': picked,
+                          'speedup_vs_upstream_faster': round(best_ref / res['ours_auto'], 3),
+                          'max_abs_diff_vs_upstream_project': diff, 'steps': args.steps,
+                          'l2': 'rotating inputs > 2x L2 between calls'}), flush=True)
+
+
 def run_l2_peak(args):
     """The L2 random-row gather rates (td_probe_row_gather) for every row size the gather kernels read; one line."""
     torch.cuda.set_device(0)
@@ -769,7 +844,11 @@ def main():
     ap.add_argument('--reps', type=int, default=50)
     ap.add_argument('--config', default='c1h', choices=sorted(workloads.CONFIGS))
     ap.add_argument('--mode', default='auto', choices=('auto', 'fused', 'project'))
-    ap.add_argument('--impl', default='ours', choices=('ours', 'reference'))
+    ap.add_argument('--impl', default='ours', choices=('ours', 'reference', 'reference-cuda'),
+                    help="reference: upstream's algorithm on the host CPU; reference-cuda: upstream's own CUDA "
+                         "operator from an installed checkout (--ref-path), timed beside this library")
+    ap.add_argument('--ref-path', default=os.path.join(ROOT, 'baseline', '_ref'),
+                    help='--impl reference-cuda: where upstream is installed (pip --target)')
     ap.add_argument('--no-cpu', action='store_true')
     ap.add_argument('--no-sharded', action='store_true', help='skip the batch-sharded c3 record')
     ap.add_argument('--l2-peak', action='store_true', help='print the L2 random-row gather rates and exit')
@@ -792,6 +871,8 @@ def main():
         args.warmup = 3
     if args.impl == 'reference':
         run_reference_arm(args)
+    elif args.impl == 'reference-cuda':
+        run_reference_cuda(args)
     elif args.l2_peak:
         run_l2_peak(args)
     elif args.sweep:

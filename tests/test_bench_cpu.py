@@ -34,3 +34,19 @@ def test_reference_arm_is_silent_on_other_ranks():
                   env_extra={'RANK': '1', 'WORLD_SIZE': '2', 'LOCAL_RANK': '1'})
     assert p.returncode == 0, p.stderr[-2000:]
     assert not [ln for ln in p.stdout.splitlines() if ln.startswith('{')]
+
+
+def test_reference_arm_config_names_the_gpu_arms_workload():
+    """The CPU arm's config is the GPU arm's: per-GPU batch, and 'auto' resolved with the B200 table."""
+    p = run_bench('--impl', 'reference', '--steps', '1', '--warmup', '3')
+    assert p.returncode == 0, p.stderr[-2000:]
+    line = json.loads([ln for ln in p.stdout.splitlines() if ln.startswith('{')][0])
+    assert 'per GPU' in line['config']['workload'] and line['config']['mode'] == 'project'
+
+
+def test_reference_cuda_without_an_installed_upstream_says_unavailable():
+    p = run_bench('--impl', 'reference-cuda', '--ref-path', os.path.join(ROOT, 'no_such_checkout'))
+    assert p.returncode == 0, p.stderr[-2000:]
+    lines = [json.loads(ln) for ln in p.stdout.splitlines() if ln.startswith('{')]
+    assert lines == [{'impl': 'reference-cuda', 'unavailable': lines[0]['unavailable']}]
+    assert 'no installed marearts_tinydeform' in lines[0]['unavailable']
