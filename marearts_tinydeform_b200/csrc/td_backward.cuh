@@ -134,6 +134,8 @@ __global__ void __launch_bounds__(kBackWarps * 32) sample_backward_vec_kernel(co
     int tok[4];
     CT wt[4];
     corners4<CT>(lx, ly, CT(1), lv, a.n_tok, tok, wt, mask_b);  // a dead group's point lies outside every map
+#pragma unroll
+    for (int c = 0; c < 4; ++c) TD_BOUNDS_TOKEN(tok[c], a.n_tok);
     const CT x = cmin(cmax(lx * CT(lv.w) - CT(0.5), CT(-2)), CT(lv.w) + CT(1));
     const CT y = cmin(cmax(ly * CT(lv.h) - CT(0.5), CT(-2)), CT(lv.h) + CT(1));
     const CT fx = x - cfloor(x), fy = y - cfloor(y);
@@ -206,7 +208,8 @@ __global__ void __launch_bounds__(kBackWarps * 32) sample_backward_generic_kerne
     const long long g_tok = (long long)a.H * a.D;
     const T* go = a.grad_out + row * a.D;
     for (int s = 0; s < S; ++s) {
-        const int t = s_tok[s];
+        int t = s_tok[s];
+        TD_BOUNDS_TOKEN(t, a.n_tok);
         A dp = A(0);
         if (t >= 0) {
             const CT coef = s_coef[s];

@@ -117,7 +117,8 @@ __global__ void __launch_bounds__(kFusedThreads) fused_simt_kernel(const FusedAr
                 for (int i = 0; i < V; ++i) acc[i] = A(0);
 #pragma unroll 8
                 for (int s = 0; s < S; ++s) {
-                    const int t = tk[s];
+                    int t = tk[s];
+                    TD_BOUNDS_TOKEN(t, a.n_tok);
                     if (t >= 0) {
                         A x[V];
                         load16<T>(mb + (long long)t * C + cv * V, x);
@@ -137,7 +138,8 @@ __global__ void __launch_bounds__(kFusedThreads) fused_simt_kernel(const FusedAr
             for (int c = lane; c < C; c += 32) {
                 A acc = A(0);
                 for (int s = 0; s < S; ++s) {
-                    const int t = tk[s];
+                    int t = tk[s];
+                    TD_BOUNDS_TOKEN(t, a.n_tok);
                     if (t >= 0) acc = fma(A(w[s]), to_acc(mb[(long long)t * C + c]), acc);
                 }
                 m[r * C + c] = acc;

@@ -222,7 +222,8 @@ __global__ void __launch_bounds__(kFtcThreads, 1)
 #pragma unroll
                     for (int u = 0; u < kB; ++u) {
                         const int s = s0 + u;
-                        const int t = s < s_hi ? tk[s] : -1;
+                        int t = s < s_hi ? tk[s] : -1;
+                        TD_BOUNDS_TOKEN(t, a.n_tok);
                         w[u] = s < s_hi ? wr[s] : 0.f;
 #pragma unroll
                         for (int v = 0; v < CV; ++v) {

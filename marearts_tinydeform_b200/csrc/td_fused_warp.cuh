@@ -102,6 +102,8 @@ __global__ void __launch_bounds__(kFwWarps * 32, 10) fused_warp_kernel(const Fus
             corners4<float>(to_acc(a.loc[2 * i]), to_acc(a.loc[2 * i + 1]), to_acc(a.attn[i]), lv, a.n_tok, tk, w4,
                             mask_b);
 #pragma unroll
+            for (int k = 0; k < 4; ++k) TD_BOUNDS_TOKEN(tk[k], a.n_tok);
+#pragma unroll
             for (int k = 0; k < 4; ++k) {
                 ptr[4 * j + k] = tk[k] >= 0 ? mb + (long long)tk[k] * kRowBytes : zero;
                 wt[4 * j + k] = w4[k];

@@ -22,6 +22,7 @@ enum DeviceError : unsigned int {
     kErrTmaWait = 1,      // a TMA load never completed its mbarrier
     kErrMmaWait = 2,      // an MMA commit never arrived
     kErrSlotWait = 3,     // a pipeline slot was never released
+    kErrBounds = 4,       // TD_DEBUG_BOUNDS builds: a corner token outside [0, N) reached a gather or scatter
 };
 
 constexpr long long kSpinLimitCycles = 2000000000LL;  // ~1 s at 1.9 GHz
@@ -31,6 +32,24 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
 }
 
 __device__ __forceinline__ void record_error(unsigned int code) { atomicCAS(&g_device_error, 0u, code); }
+
+// Checked builds (-DTD_DEBUG_BOUNDS, the library _tinydeform_debug.so): every corner token is tested against [0, n)
+// where a kernel is about to read or write the token's row; a token outside it is recorded (kErrBounds) and turned
+// into an outside corner (-1), so the access is skipped. The corner rule already keeps tokens inside [0, n); this
+// re-checks that promise at every use. Ordinary builds compile the test away.
+#ifdef TD_DEBUG_BOUNDS
+#define TD_BOUNDS_TOKEN(t, n)                                                       \
+    do {                                                                            \
+        if ((t) >= 0 && (long long)(t) >= (long long)(n)) {                         \
+            record_error(kErrBounds);                                               \
+            (t) = -1;                                                               \
+        }                                                                           \
+    } while (0)
+#else
+#define TD_BOUNDS_TOKEN(t, n) \
+    do {                      \
+    } while (0)
+#endif
 
 // ---- mbarrier -----------------------------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

@@ -139,7 +139,8 @@ __device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long l
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
             const int s = s0 + u * CG;
-            const int t = s < S ? s_tok[s] : -1;
+            int t = s < S ? s_tok[s] : -1;
+            TD_BOUNDS_TOKEN(t, a.n_tok);
             w[u] = t < 0 ? A(0) : A(s_wt[s]);
             const void* src = t < 0 ? static_cast<const void*>(g_zero32)
                                     : static_cast<const void*>(vb + (long long)t * a.s_tok + v * kWords * V);
@@ -241,7 +242,8 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_generic_kernel(const
     for (int d = lane; d < a.D; d += 32) {
         A acc = A(0);
         for (int s = 0; s < S; ++s) {
-            const int t = s_tok[warp][s];
+            int t = s_tok[warp][s];
+            TD_BOUNDS_TOKEN(t, a.n_tok);
             if (t >= 0) acc = fma(A(s_wt[warp][s]), to_acc(vb[(long long)t * a.s_tok + d]), acc);
         }
         a.out[row * a.D + d] = from_acc<T>(acc);
