@@ -481,7 +481,8 @@ def run_ours(args):
             'data': 'synthetic (seeded, BASELINE config shapes)',
             'config': dict(config_dict(args.config, world, mode),
                            **({'value_padding_mask': args.padding_mask} if mask is not None else {}),
-                           **({'output_proj': [C, H * D]} if wo is not None else {})),
+                           **({'output_proj': [C, H * D], 'outproj_plan': args.outproj_plan}
+                              if wo is not None else {})),
             'mode': mode, 'queries_per_s': round(B * Q * world / (t_call * 1e-6), 1),
             'replays': {'n': len(replays), 'steps_each': args.steps, 'median_us': round(t_call, 3),
                         'min_us': round(t_min, 3), 'value_is': 'median over replays (max over ranks)'},
@@ -854,6 +855,8 @@ def main():
     ap.add_argument('--l2-peak', action='store_true', help='print the L2 random-row gather rates and exit')
     ap.add_argument('--output-proj', action='store_true',
                     help='chain the decoder output_proj ([C, H*D] nn.Linear) behind the attention')
+    ap.add_argument('--outproj-plan', default='auto', choices=('auto', 'chained', 'cluster'),
+                    help="--output-proj / --layer: output_proj in the sampler's cluster kernel or chained as a GEMM")
     ap.add_argument('--padding-mask', type=float, default=0.0,
                     help='fraction of tokens padded by a random value padding mask (0: no mask)')
     ap.add_argument('--sweep', action='store_true')
@@ -865,6 +868,9 @@ def main():
     ap.add_argument('--as-dtype', choices=('float32', 'float16', 'bfloat16', 'float64'),
                     help='run the config in this dtype instead of its own (profiling the other kernels)')
     args = ap.parse_args()
+    if args.outproj_plan != 'auto':
+        _native.set_output_proj_plan({'chained': _native.OUTPROJ_CHAINED, 'cluster': _native.OUTPROJ_CLUSTER}[
+            args.outproj_plan])
     if args.as_dtype:
         workloads.CONFIGS[args.config] = dict(workloads.CONFIGS[args.config], dtype=getattr(torch, args.as_dtype))
     if args.warmup < 3:

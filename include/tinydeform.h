@@ -109,6 +109,20 @@ TD_API int td_sampling_producer(int dtype, const void* proj, const void* referen
                                 size_t err_len);
 
 /*
+ * Backward of td_sampling_producer: from grad_locations [B, Q, H, L, P, 2] and grad_weights [B, Q, H, L, P] (either
+ * may be NULL, meaning zero) and the forward's inputs, writes grad_proj [B, Q, 3 * H * L * P] (same layout as proj:
+ * offset gradients, then logit gradients through the softmax) and, unless grad_reference_points is NULL,
+ * grad_reference_points [B, Q, L, ref_dim] (summed over heads and points, in a fixed order: no atomics). One warp
+ * per (batch, query). Launched with programmatic dependent launch. No counterpart in upstream (no producer, no
+ * backward); the definition followed is the producer's own (Deformable-DETR's MSDeformAttn forward).
+ */
+TD_API int td_sampling_producer_backward(int dtype, const void* proj, const void* reference_points, int ref_dim,
+                                         const int64_t* spatial_shapes, const void* grad_locations,
+                                         const void* grad_weights, void* grad_proj, void* grad_reference_points,
+                                         int64_t B, int64_t Q, int64_t H, int64_t L, int64_t P, void* stream,
+                                         char* err, size_t err_len);
+
+/*
  * td_project_forward_masked followed by the decoder's output_proj in the same call: out [B, Q, C_out] =
  * attention @ output_weight^T + output_bias, output_weight [C_out, HD] (nn.Linear), output_bias [C_out] or NULL;
  * the output GEMM (the projection kernel, as td_linear) is queued right behind the sampler with programmatic
@@ -299,6 +313,20 @@ TD_API int td_probe_row_gather(const void* buf, int64_t rows, int row_bytes, int
  */
 enum td_policy { TD_POLICY_BEST = 0, TD_POLICY_CUDA_CORES = 1 };
 TD_API int td_set_kernel_policy(int policy);
+
+/*
+ * How calls that apply output_proj in the project order (td_project_forward_ex, td_layer_forward) run it, for
+ * every later call in this process. TD_OUTPROJ_AUTO (default): in the sampler's own kernel (thread-block clusters
+ * of 8 CTAs share the attention rows over distributed shared memory and split Wo's columns) while that kernel's grid
+ * is one wave (B * Q * H / 8 <= 3 CTAs per SM: 444 queries at 8 heads on B200), chained as a separate GEMM above
+ * that. TD_OUTPROJ_CHAINED: always chained.
+ * TD_OUTPROJ_CLUSTER: in the sampler's kernel wherever its conditions hold (H dividing 8, H * D * element size of
+ * 512 bytes, C_out <= 256, 16-byte aligned Wo and value rows of 16 * 2^k bytes up to 512), else chained.
+ * Results agree within the dtype's rounding either way. No counterpart in upstream, which has no output_proj
+ * (its README lists fusing it as future work, README.md:11). Returns the previous plan, or -1 for an unknown plan.
+ */
+enum td_outproj_plan { TD_OUTPROJ_AUTO = 0, TD_OUTPROJ_CHAINED = 1, TD_OUTPROJ_CLUSTER = 2 };
+TD_API int td_set_output_proj_plan(int plan);
 
 /*
  * Reads the library's device error word on the current device (0 = no error), and clears it when `clear` is set.

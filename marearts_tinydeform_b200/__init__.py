@@ -33,7 +33,7 @@ import functools
 import torch
 
 from . import _native
-from .autograd import linear_train, ma_deform_attn_train
+from .autograd import linear_train, ma_deform_attn_train, producer_train
 from .reference import deform_attn_layer_reference, ma_deform_attn_reference, sampling_producer_reference
 
 __all__ = ['ma_deform_attn', 'ma_deform_attn_reference', 'choose_mode', 'deform_attn_layer', 'sampling_producer',
@@ -157,13 +157,14 @@ def sampling_producer(query, reference_points, spatial_shapes, n_heads, n_points
         return sampling_producer_reference(query, reference_points, spatial_shapes, n_heads, n_points,
                                            sampling_weight, sampling_bias)
     _native.load()
-    if _wants_grad(query, reference_points, sampling_weight, sampling_bias):
-        # training: torch's operators (two GEMMs, softmax, arithmetic), differentiable as they are
-        return sampling_producer_reference(query, reference_points, spatial_shapes, n_heads, n_points,
-                                           sampling_weight, sampling_bias)
     L = spatial_shapes.shape[0]
     if sampling_weight.dim() != 2 or sampling_weight.shape[0] != 3 * n_heads * L * n_points:
         raise RuntimeError('sampling_weight must be [3 * H * L * P, Cq]: the offset rows, then the attention rows')
+    if _wants_grad(query, reference_points, sampling_weight, sampling_bias):
+        # training: the same kernels behind autograd Functions whose backward runs this library's kernels (the
+        # producer's backward, then the query projection's gradient GEMMs)
+        return producer_train(query, reference_points, spatial_shapes, n_heads, n_points, sampling_weight,
+                              sampling_bias)
     proj = _native.linear(query, sampling_weight, sampling_bias)
     return _native.sampling_producer(proj, reference_points, spatial_shapes, n_heads, n_points)
 
@@ -196,9 +197,9 @@ def deform_attn_layer(query, reference_points, memory, spatial_shapes, level_sta
         mode = _pick(memory, value_weight, query.shape[1], n_heads, spatial_shapes.shape[0], n_points)
     if _wants_grad(query, reference_points, memory, sampling_weight, sampling_bias, value_weight, value_bias,
                    output_weight, output_bias):
-        # training: the producer in torch's operators, the attention through the differentiable CUDA operator
-        loc, attn = sampling_producer_reference(query, reference_points, spatial_shapes, n_heads, n_points,
-                                                sampling_weight, sampling_bias)
+        # training: the producer and the attention behind autograd Functions on this library's kernels
+        loc, attn = sampling_producer(query, reference_points, spatial_shapes, n_heads, n_points, sampling_weight,
+                                      sampling_bias)
         return ma_deform_attn(memory, value_weight, value_bias, spatial_shapes, level_start_index, loc, attn,
                               mode=mode, value_padding_mask=value_padding_mask, output_weight=output_weight,
                               output_bias=output_bias)

@@ -37,6 +37,8 @@ SIGNATURES = {
     'td_linear': (_ip, [_ip, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _cp, _sz]),
     'td_sampling_producer': (_ip, [_ip, _vp, _vp, ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp,
                                    _cp, _sz]),
+    'td_sampling_producer_backward': (_ip, [_ip, _vp, _vp, ctypes.c_int, _vp, _vp, _vp, _vp, _vp, _i64, _i64,
+                                            _i64, _i64, _i64, _vp, _cp, _sz]),
     'td_sample_backward': (_ip, [_ip, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                  _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _cp, _sz]),
     'td_project_ex_workspace_bytes': (_sz, [_ip, _i64, _i64, _i64, _i64, _ip]),
@@ -58,6 +60,7 @@ SIGNATURES = {
     'td_test_starve_next_grad_gemm': (_ip, [ctypes.c_longlong]),
     'td_probe_row_gather': (_ip, [_vp, _i64, _ip, _ip, _i64, ctypes.c_uint, _vp, _sz, _ip, _vp, _cp, _sz]),
     'td_set_kernel_policy': (_ip, [_ip]),
+    'td_set_output_proj_plan': (_ip, [_ip]),
     'td_device_error': (_ip, [_ip, ctypes.POINTER(ctypes.c_uint), _cp, _sz]),
     'td_device_info': (_ip, [_ip, ctypes.POINTER(_ip), ctypes.POINTER(_ip), ctypes.POINTER(_ip), _cp, _sz]),
     'td_launch_count': (ctypes.c_uint64, []),
@@ -339,6 +342,27 @@ def sampling_producer(proj, reference_points, spatial_shapes, heads, points):
     return loc, attn
 
 
+def sampling_producer_backward(proj, reference_points, spatial_shapes, heads, points, grad_loc, grad_attn,
+                               want_ref=True):
+    """(grad_proj [B, Q, 3 * H * L * P], grad_reference_points or None) of the producer through
+    td_sampling_producer_backward; grad_loc / grad_attn may be None (zero)."""
+    lib = load()
+    B, Q = reference_points.shape[:2]
+    L = spatial_shapes.size(0)
+    pr, ref, shp = _dense(proj, reference_points, spatial_shapes)
+    gl = None if grad_loc is None else _dense(grad_loc.to(proj.dtype))[0]
+    ga = None if grad_attn is None else _dense(grad_attn.to(proj.dtype))[0]
+    grad_proj = torch.empty_like(pr)
+    grad_ref = torch.empty_like(ref) if want_ref else None
+    if B * Q == 0:
+        return grad_proj, None if grad_ref is None else grad_ref.zero_()
+    with torch.cuda.device(proj.device):
+        _call(lib.td_sampling_producer_backward, DTYPE_CODE[proj.dtype], _ptr(pr), _ptr(ref), ref.size(3),
+              _ptr(shp), None if gl is None else _ptr(gl), None if ga is None else _ptr(ga), _ptr(grad_proj),
+              None if grad_ref is None else _ptr(grad_ref), B, Q, heads, L, points, _stream(proj.device))
+    return grad_proj, grad_ref
+
+
 ORDER_CODE = {'project': 0, 'fused': 1}
 
 
@@ -537,6 +561,19 @@ def set_kernel_policy(policy):
     prev = load().td_set_kernel_policy(policy)
     if prev < 0:
         raise ValueError(f'unknown kernel policy {policy}')
+    return prev
+
+
+OUTPROJ_AUTO, OUTPROJ_CHAINED, OUTPROJ_CLUSTER = 0, 1, 2
+
+
+def set_output_proj_plan(plan):
+    """How the project order applies output_proj: OUTPROJ_AUTO (in the sampler's cluster kernel while its grid is one
+    wave, B * Q * H / 8 <= 3 CTAs per SM; the default), OUTPROJ_CHAINED (a separate GEMM) or OUTPROJ_CLUSTER (the cluster
+    kernel wherever its shape conditions hold); returns the previous plan."""
+    prev = load().td_set_output_proj_plan(plan)
+    if prev < 0:
+        raise ValueError(f'unknown output_proj plan {plan}')
     return prev
 
 

@@ -18,7 +18,10 @@ half-precision backward keeps its gradients in half precision; float32 / float64
 value padding mask blocks the gradient of padded tokens exactly as masked_fill does in the reference.
 
 LinearFunction is output_proj (y = x @ W^T + b) on the same kernels: td_linear forward, td_linear_grad_input and
-td_linear_grad_weight (with the bias gradient's column sums) backward.
+td_linear_grad_weight (with the bias gradient's column sums) backward. It is also the query projection of the
+sampling producer, whose own step (softmax over each row's L * P logits, offsets moving the reference points) is
+ProducerFunction: td_sampling_producer forward, td_sampling_producer_backward backward (gradients of the query
+projection's output and of the reference points).
 """
 
 import torch
@@ -113,3 +116,31 @@ class LinearFunction(torch.autograd.Function):
 def linear_train(x, weight, bias):
     """The differentiable output_proj on CUDA."""
     return LinearFunction.apply(x, weight, bias)
+
+
+class ProducerFunction(torch.autograd.Function):
+    """(sampling_locations, attention_weights) from the query projection proj [B, Q, 3 * H * L * P] and the reference
+    points, on this library's producer kernels, differentiable in proj and the reference points."""
+
+    @staticmethod
+    def forward(ctx, proj, reference_points, spatial_shapes, heads, points):
+        ctx.save_for_backward(proj, reference_points, spatial_shapes)
+        ctx.heads, ctx.points = heads, points
+        loc, attn = _native.sampling_producer(proj, reference_points, spatial_shapes, heads, points)
+        return loc, attn
+
+    @staticmethod
+    def backward(ctx, grad_loc, grad_attn):
+        proj, ref, shapes = ctx.saved_tensors
+        need = ctx.needs_input_grad
+        if not (need[0] or need[1]):
+            return None, None, None, None, None
+        grad_proj, grad_ref = _native.sampling_producer_backward(proj, ref, shapes, ctx.heads, ctx.points, grad_loc,
+                                                                 grad_attn, want_ref=need[1])
+        return grad_proj if need[0] else None, grad_ref, None, None, None
+
+
+def producer_train(query, reference_points, spatial_shapes, heads, points, sampling_weight, sampling_bias):
+    """The differentiable sampling producer on CUDA: the query projection (LinearFunction), then ProducerFunction."""
+    proj = LinearFunction.apply(query, sampling_weight, sampling_bias)
+    return ProducerFunction.apply(proj, reference_points, spatial_shapes, heads, points)

@@ -132,4 +132,136 @@ __global__ void __launch_bounds__(kProducerWarps * 32) sampling_producer_kernel(
     }
 }
 
+// ---- backward ------------------------------------------------------------------------------------------------
+// Gradients of the producer, given those of its two outputs (either may be absent: zero):
+//   logits:  g_x[j] = w[j] * (g_w[j] - sum_k w[k] g_w[k])                       (softmax over the row's L * P points)
+//   offsets: 2-d reference points: g_off = g_loc / (w_l, h_l);  4-d boxes: g_off = g_loc * wh / P * 0.5
+//   reference points (summed over the query's heads and each level's points):
+//            g_ref.xy += g_loc;  4-d boxes also g_ref.wh += g_loc * off / P * 0.5
+// One warp per (batch, query): the H heads one after another, lanes over the L * P points (two per lane, as the
+// forward), so the reference-point gradient of each level is a sum inside the warp (no atomics, fixed order).
+template <typename T>
+struct ProducerBwdArgs {
+    const T* proj;            // [B * Q, 3 * H * L * P]: offsets (head, level, point, xy), then logits (head, L * P)
+    const T* ref;             // [B, Q, L, ref_dim]
+    const int64_t* shapes;    // [L, 2] (height, width)
+    const T* g_loc;           // [B, Q, H, L, P, 2] or null
+    const T* g_attn;          // [B, Q, H, L, P] or null
+    T* g_proj;                // [B * Q, 3 * H * L * P]
+    T* g_ref;                 // [B, Q, L, ref_dim] or null
+    long long bq;             // B * Q
+    int ref_dim, H, L, P;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kProducerWarps * 32) sampling_producer_backward_kernel(const ProducerBwdArgs<T> a) {
+    using A = typename Elem<T>::acc;
+    // per warp and point: the point's reference-gradient terms summed over the heads (x, y, w, h)
+    __shared__ A s_sum[kProducerWarps][kMaxLevelPoints][4];
+    grid_dependency_wait();
+    launch_dependents();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long bq = (long long)blockIdx.x * kProducerWarps + warp;
+    if (bq >= a.bq) return;  // warp-uniform
+    const int LP = a.L * a.P;
+    const long long row_len = 3LL * a.H * LP;
+    const T* __restrict__ base = a.proj + bq * row_len;
+    T* __restrict__ gbase = a.g_proj + bq * row_len;
+    const A inv_p_half = A(0.5) / A(a.P);
+    A sx[2], sy[2], acc[2][4];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int j = lane + 32 * k;
+        const bool on = j < LP;
+        const int l = on ? j / a.P : 0;
+        if (a.ref_dim == 2) {  // the offset normaliser (w_l, h_l)
+            sx[k] = on ? A(a.shapes[2 * l + 1]) : A(1);
+            sy[k] = on ? A(a.shapes[2 * l]) : A(1);
+        } else {               // the box's width and height
+            const T* r = a.ref + (bq * a.L + l) * 4;
+            sx[k] = on ? to_acc(r[2]) : A(0);
+            sy[k] = on ? to_acc(r[3]) : A(0);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[k][c] = A(0);
+    }
+    for (int h = 0; h < a.H; ++h) {
+        const T* __restrict__ off = base + (long long)h * LP * 2;
+        const T* __restrict__ logit = base + 2LL * a.H * LP + (long long)h * LP;
+        const long long pt0 = (bq * a.H + h) * LP;  // this head's first point in loc / attn
+        A x[2], ox[2], oy[2], gx[2], gy[2], gw[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int j = lane + 32 * k;
+            const bool on = j < LP;
+            x[k] = on ? to_acc(logit[j]) : A(-INFINITY);
+            ox[k] = on ? to_acc(off[2 * j]) : A(0);
+            oy[k] = on ? to_acc(off[2 * j + 1]) : A(0);
+            gx[k] = on && a.g_loc != nullptr ? to_acc(a.g_loc[2 * (pt0 + j)]) : A(0);
+            gy[k] = on && a.g_loc != nullptr ? to_acc(a.g_loc[2 * (pt0 + j) + 1]) : A(0);
+            gw[k] = on && a.g_attn != nullptr ? to_acc(a.g_attn[pt0 + j]) : A(0);
+        }
+        // the forward's softmax again
+        A m = x[0] > x[1] ? x[0] : x[1];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const A y = __shfl_xor_sync(0xffffffffu, m, o);
+            m = y > m ? y : m;
+        }
+        A e[2], sum = A(0);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            e[k] = lane + 32 * k < LP ? exp(x[k] - m) : A(0);
+            sum += e[k];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        A w[2], dot = A(0);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            w[k] = e[k] / sum;
+            dot += w[k] * gw[k];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        T* __restrict__ g_off = gbase + (long long)h * LP * 2;
+        T* __restrict__ g_logit = gbase + 2LL * a.H * LP + (long long)h * LP;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int j = lane + 32 * k;
+            if (j >= LP) continue;
+            g_logit[j] = from_acc<T>(w[k] * (gw[k] - dot));
+            if (a.ref_dim == 2) {
+                g_off[2 * j] = from_acc<T>(gx[k] / sx[k]);
+                g_off[2 * j + 1] = from_acc<T>(gy[k] / sy[k]);
+            } else {
+                g_off[2 * j] = from_acc<T>(gx[k] * sx[k] * inv_p_half);
+                g_off[2 * j + 1] = from_acc<T>(gy[k] * sy[k] * inv_p_half);
+                acc[k][2] += gx[k] * ox[k] * inv_p_half;
+                acc[k][3] += gy[k] * oy[k] * inv_p_half;
+            }
+            acc[k][0] += gx[k];
+            acc[k][1] += gy[k];
+        }
+    }
+    if (a.g_ref == nullptr) return;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int j = lane + 32 * k;
+        if (j < LP) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) s_sum[warp][j][c] = acc[k][c];
+        }
+    }
+    __syncwarp();
+    // output i (lanes over L * ref_dim): level i / ref_dim, coordinate i % ref_dim, summed over the level's points in
+    // order
+    for (int i = lane; i < a.L * a.ref_dim; i += 32) {
+        const int l = i / a.ref_dim, c = i - l * a.ref_dim;
+        A v = A(0);
+        for (int p = 0; p < a.P; ++p) v += s_sum[warp][l * a.P + p][c];
+        a.g_ref[(bq * a.L + l) * a.ref_dim + c] = from_acc<T>(v);
+    }
+}
+
 }  // namespace td

@@ -198,6 +198,38 @@ __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepco
 // Allow the next kernel in the stream, if launched with programmatic serialization, to start its prologue now.
 __device__ __forceinline__ void launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// ---- thread-block clusters and distributed shared memory -----------------------------------------------------
+// Rank of this CTA in its cluster (0 .. cluster size - 1).
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// The shared::cluster address of the variable at shared::cta address `saddr` in the CTA of cluster rank `rank`.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+// 16 bytes from the shared memory of a CTA of the cluster (16-byte aligned shared::cluster address).
+__device__ __forceinline__ uint4 ld_cluster_v4(uint32_t caddr) {
+    uint4 v;
+    asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(caddr)
+                 : "memory");
+    return v;
+}
+// Cluster-wide barrier in two halves (every thread of every CTA of the cluster executes both, in order): arrive
+// releases this thread's earlier shared-memory writes to the cluster, wait returns once every thread has arrived
+// and acquires theirs. A hardware barrier, not a spin: the cluster's CTAs are co-scheduled by construction.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// Arrive without ordering this thread's earlier memory accesses (for a barrier that only marks that they are done).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+
 // ---- tcgen05: tensor memory ---------------------------------------------------------------------------------
 // Executed by one whole warp. Writes the TMEM base address to *slot.
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {

@@ -104,13 +104,15 @@ __device__ __forceinline__ void sample_row_corners(const SampleArgs<T>& a, long 
     }
 }
 
-// out[row] = sum over the row's corners of weight * value[token] (head slice): G lanes per corner row, each loading
+// The sum over the row's corners of weight * value[token] (head slice): G lanes per corner row, each loading
 // 16 bytes of it (kWide: 32 bytes, for rows of 128 bytes and more -- half the load instructions, which measured 16 %
 // faster on the stress shape's 128-byte rows and made no difference on 64-byte rows), kBatch corner rows in flight
-// per lane, the lanes' groups summed with an xor butterfly.
+// per lane, the lanes' groups summed with an xor butterfly. On return every lane holds the finished sum of its
+// slice: head channels [(v * kWords + k) * V, + V) in acc[k * V ..], v = lane % G.
 template <typename T, bool kWide, bool kNoAlloc>
-__device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long long row, int lane, const int* s_tok,
-                                                  const typename Coord<T>::type* s_wt) {
+__device__ __forceinline__ void sample_row_sum(const SampleArgs<T>& a, long long row, int lane, const int* s_tok,
+                                               const typename Coord<T>::type* s_wt,
+                                               typename Elem<T>::acc (&acc)[(kWide ? 2 : 1) * Elem<T>::kVec]) {
     using A = typename Elem<T>::acc;
     constexpr int V = Elem<T>::kVec;         // elements per 16-byte word
     constexpr int kWords = kWide ? 2 : 1;    // 16-byte words per lane and corner row
@@ -128,7 +130,6 @@ __device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long l
     }
     const T* vb = a.value + b * a.s_img + (long long)h * a.s_head;
     const int G = a.G, CG = 32 / G, cg = lane / G, v = lane - cg * G;
-    A acc[kWords * V];
 #pragma unroll
     for (int i = 0; i < kWords * V; ++i) acc[i] = A(0);
     for (int s0 = cg; s0 < S; s0 += kBatch * CG) {
@@ -161,9 +162,20 @@ __device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long l
 #pragma unroll
         for (int i = 0; i < kWords * V; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
     }
-    if (cg == 0) {
+}
+
+// out[row] = sample_row_sum, stored by the first corner group's lanes.
+template <typename T, bool kWide, bool kNoAlloc>
+__device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long long row, int lane, const int* s_tok,
+                                                  const typename Coord<T>::type* s_wt) {
+    using A = typename Elem<T>::acc;
+    constexpr int V = Elem<T>::kVec;
+    constexpr int kWords = kWide ? 2 : 1;
+    A acc[kWords * V];
+    sample_row_sum<T, kWide, kNoAlloc>(a, row, lane, s_tok, s_wt, acc);
+    if (lane < a.G) {
 #pragma unroll
-        for (int k = 0; k < kWords; ++k) store16<T>(a.out + row * a.D + (v * kWords + k) * V, acc + k * V);
+        for (int k = 0; k < kWords; ++k) store16<T>(a.out + row * a.D + (lane * kWords + k) * V, acc + k * V);
     }
 }
 

@@ -26,6 +26,7 @@
 #include "td_producer.cuh"
 #include "td_backward.cuh"
 #include "td_sampler.cuh"
+#include "td_sample_outproj.cuh"
 #include "td_probe.cuh"
 
 namespace td {
@@ -33,6 +34,7 @@ namespace {
 
 std::atomic<uint64_t> g_launches{0};
 std::atomic<int> g_policy{TD_POLICY_BEST};
+std::atomic<int> g_outproj_plan{TD_OUTPROJ_AUTO};
 
 int fail(char* err, size_t err_len, int code, const char* fmt, ...) {
     if (err != nullptr && err_len > 0) {
@@ -171,6 +173,81 @@ int launch_sampler(const T* value, long long s_img, long long s_tok, long long s
     if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "sampler launch: %s", cudaGetErrorString(e));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return check_launch(err, err_len, vec ? "sample_vec_kernel" : "sample_generic_kernel");
+}
+
+// The sampler with output_proj in the same kernel (sample_outproj_kernel, clusters of 4 or 8 CTAs): y [B * Q,
+// C_out] = Wo . attention + bo, the attention never written to global memory. Returns TD_OK having launched it, or
+// kNotApplicable (nothing launched) when the shapes, the alignment or the plan rule it out -- the caller then chains
+// the sampler and the output GEMM. Under TD_OUTPROJ_AUTO it is taken while the kernel's grid is at most
+// kOpAutoCtasPerSm CTAs per SM (one wave). There the chained GEMM is a second grid of a few CTAs behind a kernel
+// boundary, which the cluster epilogue saves; in several waves each CTA's longer life (weight loads, cluster
+// barriers, the product) is paid once per wave and the chained GEMM wins. Measured on B200, float16, RT-DETR levels,
+// C_out = 256, graphs of 100 calls: B x Q = 1 x 50: 8.3 against 10.7 us chained; 1 x 100: 8.7 / 10.9;
+// 1 x 300: 11.0 / 12.2; 2 x 300: 17.6 / 15.9; 8 x 300 (bfloat16): 46.6 / 38.1.
+constexpr int kNotApplicable = -1000;
+constexpr long long kOpAutoCtasPerSm = 3;
+
+template <typename T>
+int launch_sample_outproj(const T* value, long long s_img, long long s_tok, long long s_head, const int64_t* shapes,
+                          const int64_t* starts, const T* loc, const T* attn, const T* out_w, const T* out_b, T* y,
+                          int64_t C_out, int64_t B, int64_t Q, int64_t N, int64_t H, int64_t D, int64_t L, int64_t P,
+                          cudaStream_t stream, char* err, size_t err_len, bool after_producer,
+                          const uint8_t* mask = nullptr, ProducerIn<T> prod = {}) {
+    const int plan = g_outproj_plan.load(std::memory_order_relaxed);
+    if (plan == TD_OUTPROJ_CHAINED) return kNotApplicable;
+    if (plan == TD_OUTPROJ_AUTO) {
+        DeviceFacts f;
+        if (int rc = device_facts(&f, err, err_len)) return rc;
+        if ((B * Q * H + kSampleWarps - 1) / kSampleWarps > kOpAutoCtasPerSm * f.sm_count) return kNotApplicable;
+    }
+    const long long HD = H * D;
+    const long long row_bytes = D * (long long)sizeof(T);
+    const long long G = row_bytes / 16;
+    const bool ok = kSampleWarps % H == 0 && HD * (long long)sizeof(T) == 512 &&
+                    C_out <= 256 && row_bytes % 16 == 0 && row_bytes <= 512 &&
+                    (G & (G - 1)) == 0 && aligned16(value) && aligned16(out_w) &&
+                    (s_img * (long long)sizeof(T)) % 16 == 0 && (s_tok * (long long)sizeof(T)) % 16 == 0 &&
+                    (s_head * (long long)sizeof(T)) % 16 == 0 && B * Q > 0;
+    if (!ok) return kNotApplicable;
+    SampleArgs<T> a;
+    a.value = value; a.loc = loc; a.attn = attn; a.out = nullptr; a.shapes = shapes; a.starts = starts; a.prod = prod;
+    a.rows = B * Q * H; a.s_img = s_img; a.s_tok = s_tok; a.s_head = s_head; a.n_tok = N; a.mask = mask;
+    a.Q = int(Q); a.H = int(H); a.D = int(D); a.L = int(L); a.P = int(P); a.G = int(G);
+    const bool wide = row_bytes % 32 == 0 && row_bytes >= 128 && aligned32(value) &&
+                      (s_img * (long long)sizeof(T)) % 32 == 0 && (s_tok * (long long)sizeof(T)) % 32 == 0 &&
+                      (s_head * (long long)sizeof(T)) % 32 == 0;
+    if (wide) a.G = int(row_bytes / 32);
+    const bool no_alloc = B * H * N * D * (long long)sizeof(T) > (64LL << 20);
+    OutProjArgs<T> o;
+    o.weight = out_w; o.bias = out_b; o.out = y; o.queries = B * Q; o.C_out = int(C_out); o.HD = int(HD);
+    // cluster size: 8 CTAs (each computes C_out / 8 output columns; clusters of 4 measured slower: twice the weight
+    // loads per CTA)
+    constexpr int CS = sizeof(T) == 2 ? kOpClusterMma : kOpCluster;
+    o.cols = int((C_out + CS - 1) / CS);
+    const long long ctas = (B * Q * H + kSampleWarps - 1) / kSampleWarps;
+    const unsigned grid = unsigned((ctas + CS - 1) / CS * CS);
+    const size_t smem = sample_outproj_smem<T>(int(L), int(P), int(H), int(HD), CS);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kSampleWarps * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CS;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = after_producer ? 2 : 1;
+    const cudaError_t e = wide       ? cudaLaunchKernelEx(&cfg, sample_outproj_kernel<T, true, true, CS>, a, o)
+                          : no_alloc ? cudaLaunchKernelEx(&cfg, sample_outproj_kernel<T, false, true, CS>, a, o)
+                                     : cudaLaunchKernelEx(&cfg, sample_outproj_kernel<T, false, false, CS>, a, o);
+    if (e != cudaSuccess)
+        return fail(err, err_len, TD_ERR_CUDA, "sample_outproj_kernel launch: %s", cudaGetErrorString(e));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return check_launch(err, err_len, "sample_outproj_kernel");
 }
 
 int tensor_map_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows, char* err,
@@ -860,6 +937,17 @@ int launch_producer(const T* proj, const T* ref, int ref_dim, const int64_t* sha
     return check_launch(err, err_len, "sampling_producer_kernel");
 }
 
+template <typename T>
+int launch_producer_backward(const ProducerBwdArgs<T>& a, cudaStream_t stream, char* err, size_t err_len) {
+    const unsigned grid = unsigned((a.bq + kProducerWarps - 1) / kProducerWarps);
+    const cudaError_t e = launch_kernel(sampling_producer_backward_kernel<T>, dim3(grid), dim3(kProducerWarps * 32),
+                                        0, stream, true, a);
+    if (e != cudaSuccess)
+        return fail(err, err_len, TD_ERR_CUDA, "sampling_producer_backward_kernel launch: %s", cudaGetErrorString(e));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return check_launch(err, err_len, "sampling_producer_backward_kernel");
+}
+
 // Backward of the sampling half (td_backward.cuh): zeroes grad_value, then one warp per (b, q, h) row.
 template <typename T>
 int launch_sample_backward(const T* value, long long s_img, long long s_tok, long long s_head, const int64_t* shapes,
@@ -1052,6 +1140,35 @@ int td_sampling_producer(int dtype, const void* proj, const void* reference_poin
         return launch_producer<T>(static_cast<const T*>(proj), static_cast<const T*>(reference_points), ref_dim,
                                   spatial_shapes, static_cast<T*>(sampling_locations),
                                   static_cast<T*>(attention_weights), B, Q, H, L, P, s, err, err_len);
+    });
+}
+
+int td_sampling_producer_backward(int dtype, const void* proj, const void* reference_points, int ref_dim,
+                                  const int64_t* spatial_shapes, const void* grad_locations,
+                                  const void* grad_weights, void* grad_proj, void* grad_reference_points, int64_t B,
+                                  int64_t Q, int64_t H, int64_t L, int64_t P, void* stream, char* err,
+                                  size_t err_len) {
+    if (dtype_size(dtype) == 0) return fail(err, err_len, TD_ERR_ARG, "unsupported dtype code %d", dtype);
+    if (B < 0 || Q < 0 || H <= 0 || L <= 0 || P <= 0)
+        return fail(err, err_len, TD_ERR_ARG, "producer needs B, Q >= 0 and H, L, P > 0");
+    if (L * P > TD_MAX_LEVEL_POINTS)
+        return fail(err, err_len, TD_ERR_ARG, "levels x points must be <= %d", TD_MAX_LEVEL_POINTS);
+    if (ref_dim != 2 && ref_dim != 4)
+        return fail(err, err_len, TD_ERR_ARG, "reference points must have 2 (x, y) or 4 (cx, cy, w, h) coordinates");
+    if (B * Q * H > INT32_MAX) return fail(err, err_len, TD_ERR_ARG, "too many (batch, query, head) rows");
+    if (B * Q == 0) return TD_OK;
+    if (!proj || !reference_points || !spatial_shapes || !grad_proj)
+        return fail(err, err_len, TD_ERR_ARG, "null tensor pointer");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return dispatch(dtype, [&](auto tag) {
+        using T = decltype(tag);
+        ProducerBwdArgs<T> a;
+        a.proj = static_cast<const T*>(proj); a.ref = static_cast<const T*>(reference_points);
+        a.shapes = spatial_shapes; a.g_loc = static_cast<const T*>(grad_locations);
+        a.g_attn = static_cast<const T*>(grad_weights); a.g_proj = static_cast<T*>(grad_proj);
+        a.g_ref = static_cast<T*>(grad_reference_points); a.bq = B * Q; a.ref_dim = ref_dim; a.H = int(H);
+        a.L = int(L); a.P = int(P);
+        return launch_producer_backward<T>(a, s, err, err_len);
     });
 }
 
@@ -1403,6 +1520,14 @@ int td_layer_forward(int dtype, int order, const void* query, int64_t Cq, const 
             }
             ProducerIn<T> prod;
             prod.proj = proj; prod.ref = ref; prod.ref_dim = ref_dim; prod.wait_first = paired ? 1 : 0;
+            if (output_weight != nullptr) {
+                // output_proj in the sampler's own kernel, where the plan and the shapes allow it
+                const int rc = launch_sample_outproj<T>(
+                    value, H * N * D, D, N * D, spatial_shapes, level_start_index, nullptr, nullptr,
+                    static_cast<const T*>(output_weight), static_cast<const T*>(output_bias), static_cast<T*>(out),
+                    C_out, B, Q, N, H, D, L, P, s, err, err_len, N > 0, value_padding_mask, prod);
+                if (rc != kNotApplicable) return rc;
+            }
             // with no value projection in between, the sampler follows the query projection in plain stream order
             if (int rc = launch_sampler<T>(value, H * N * D, D, N * D, spatial_shapes, level_start_index, nullptr,
                                            nullptr, target, B, Q, N, H, D, L, P, s, err, err_len, N > 0,
@@ -1477,6 +1602,15 @@ int td_project_forward_ex(int dtype, const void* memory, const void* value_weigh
                                         static_cast<const T*>(value_bias), v, B, N, C, H, HD, 1, s, err, err_len,
                                         true))
                 return rc;
+        }
+        {
+            // output_proj in the sampler's own kernel, where the plan and the shapes allow it
+            const int rc = launch_sample_outproj<T>(
+                v, H * N * D, D, N * D, spatial_shapes, level_start_index, static_cast<const T*>(sampling_locations),
+                static_cast<const T*>(attention_weights), static_cast<const T*>(output_weight),
+                static_cast<const T*>(output_bias), static_cast<T*>(out), C_out, B, Q, N, H, D, L, P, s, err,
+                err_len, N > 0, value_padding_mask);
+            if (rc != kNotApplicable) return rc;
         }
         if (int rc = launch_sampler<T>(v, H * N * D, D, N * D, spatial_shapes, level_start_index,
                                        static_cast<const T*>(sampling_locations),
@@ -1622,6 +1756,11 @@ int td_device_info(int device, int* sm_count, int* cc_major, int* cc_minor, char
 int td_set_kernel_policy(int policy) {
     if (policy != TD_POLICY_BEST && policy != TD_POLICY_CUDA_CORES) return -1;
     return g_policy.exchange(policy);
+}
+
+int td_set_output_proj_plan(int plan) {
+    if (plan != TD_OUTPROJ_AUTO && plan != TD_OUTPROJ_CHAINED && plan != TD_OUTPROJ_CLUSTER) return -1;
+    return g_outproj_plan.exchange(plan);
 }
 
 int td_device_error(int clear, unsigned int* code, char* err, size_t err_len) {
