@@ -18,7 +18,11 @@ nn.Linear, softmax, location arithmetic; then this library's ma_deform_attn) and
 --backward times training steps instead: forward + backward of ma_deform_attn (gradients of memory, value_weight,
 value_bias, sampling_locations and attention_weights), beside the same through the torch reference (nn.Linear +
 grid_sample, autograd) on the GPU, both captured in CUDA graphs on rotating inputs; plus the backward kernel alone
-with its roofline.
+with its roofline. --layer --backward times a training step of the whole layer (every gradient, this library's
+kernels only) beside the all-torch layer under autograd.
+
+--output-proj adds the decoder's output_proj to every call; --outproj-plan chooses whether it runs in the sampler's
+cluster epilogue or as a chained GEMM (default: the library's automatic plan).
 
 --impl reference times the CPU implementation of the same call: upstream's algorithm (nn.Linear + grid_sample, the
 oracle's torch_port on torch's CPU operators) with all host threads, on rank 0 only.
@@ -632,6 +636,86 @@ def run_layer(args):
     print(json.dumps(line), flush=True)
 
 
+def run_layer_backward(args):
+    """A training step of the whole layer per step (--layer --backward): forward (producer, attention, output_proj)
+    and the gradients of every float input -- query, reference points, memory and the four projections' weights and
+    biases -- on this library's kernels, beside the same step in torch operators (grid_sample, F.linear, autograd) on
+    the GPU; prints one JSON line."""
+    torch.cuda.set_device(0)
+    dev = torch.device('cuda', 0)
+    _native.load()
+    cfg = workloads.CONFIGS[args.config]
+    B, Q, C, H, D, P, dtype = cfg['B'], cfg['Q'], cfg['C'], cfg['H'], cfg['D'], cfg['P'], cfg['dtype']
+    L = len(cfg['levels'])
+    base, pool = input_pool(args.config, B, dev, 2 * L2_BYTES)
+    shapes, starts = base[3], base[4]
+    shapes_host, starts_host = shapes.cpu(), starts.cpu()
+    g = torch.Generator(device=dev).manual_seed(92)
+    LP = H * L * P
+    params = [torch.cat([torch.randn(2 * LP, C, generator=g, device=dev) * (2.0 / C ** 0.5),
+                         torch.randn(LP, C, generator=g, device=dev) / C ** 0.5]).to(dtype),
+              (torch.randn(3 * LP, generator=g, device=dev) * 0.5).to(dtype),
+              base[1].detach().clone(), base[2].detach().clone(),
+              ((torch.rand(C, H * D, generator=g, device=dev) * 2 - 1) * (6 / (C + H * D)) ** 0.5).to(dtype),
+              torch.zeros(C, dtype=dtype, device=dev)]
+    params = [t.requires_grad_(True) for t in params]
+    sets = []
+    for mem, _, _ in pool:
+        q = torch.randn(B, Q, C, generator=g, device=dev).to(dtype)
+        ref = torch.rand(B, Q, L, args.ref_dim, generator=g, device=dev)
+        if args.ref_dim == 4:
+            ref[..., 2:] = 0.05 + 0.45 * ref[..., 2:]
+        sets.append(tuple(t.requires_grad_(True) for t in (q, ref.to(dtype), mem.detach().clone())))
+    gouts = [torch.randn(B, Q, C, generator=g, device=dev).to(dtype) for _ in range(4)]
+    mode = args.mode if args.mode != 'auto' else choose_mode(base[0], base[1], base[5])
+
+    def ours(i):
+        q, ref, mem = sets[i % len(sets)]
+        sw, sb, W, bias, wo, bo = params
+        out = deform_attn_layer(q, ref, mem, shapes, starts, H, P, sw, sb, W, bias, output_weight=wo,
+                                output_bias=bo, mode=args.mode)
+        return torch.autograd.grad(out, (q, ref, mem, *params), gouts[i % len(gouts)])
+
+    def all_torch(i):
+        q, ref, mem = sets[i % len(sets)]
+        sw, sb, W, bias, wo, bo = params
+        loc, attn = sampling_producer_reference(q, ref, shapes, H, P, sw, sb)
+        out = torch.nn.functional.linear(ma_deform_attn_reference(mem, W, bias, shapes_host, starts_host, loc, attn),
+                                         wo, bo)
+        return torch.autograd.grad(out, (q, ref, mem, *params), gouts[i % len(gouts)])
+
+    times = {}
+    gr, launches = graph_time_us(ours, args.steps, args.warmup)
+    torch.cuda.synchronize()
+    with ClockSampler(0) as clocks:
+        time.sleep(0.25)
+        times['ours'] = time_graph(gr, args.steps, reps=max(1, args.reps))
+    del gr
+    gr, _ = graph_time_us(all_torch, args.steps, args.warmup)
+    times['all_torch'] = time_graph(gr, args.steps, reps=max(1, args.reps))
+    del gr
+    # gradients of ours against the all-torch step in float32 on the first input set (upcast inputs; the half-precision
+    # torch step is itself too coarse to judge by): the largest |diff| over max |grad|, per tensor
+    q0, r0, m0 = sets[0]
+    up = [t.detach().float().requires_grad_(True) for t in (q0, r0, m0, *params)]
+    loc32, attn32 = sampling_producer_reference(up[0], up[1], shapes, H, P, up[3], up[4])
+    out32 = torch.nn.functional.linear(ma_deform_attn_reference(up[2], up[5], up[6], shapes_host, starts_host, loc32,
+                                                                attn32), up[7], up[8])
+    want = torch.autograd.grad(out32, up, gouts[0].float())
+    rel = max(float((a.float() - b).abs().max()) / max(float(b.abs().max()), 1e-30) for a, b in zip(ours(0), want))
+    line = {
+        'metric': 'µs per training step of the deformable attention layer (forward + every gradient, device-timed)',
+        'value': round(times['ours'], 3), 'unit': 'us', 'n_gpus': 1, 'steps': args.steps, 'warmup': args.warmup,
+        'higher_is_better': False, 'dtype': str(dtype).replace('torch.', ''),
+        'data': 'synthetic (seeded, BASELINE config shapes)',
+        'config': dict(config_dict(args.config, 1, mode), query_dim=C, reference_points=args.ref_dim,
+                       output_proj=[C, H * D]),
+        'all_torch_us': round(times['all_torch'], 3), 'max_rel_grad_diff_vs_float32_torch': rel,
+        'gpu_launches': launches, 'clocks': clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_backward(args):
     """Forward + backward per step (see the module docstring); prints one JSON line."""
     torch.cuda.set_device(0)
@@ -861,7 +945,8 @@ def main():
                     help='fraction of tokens padded by a random value padding mask (0: no mask)')
     ap.add_argument('--sweep', action='store_true')
     ap.add_argument('--layer', action='store_true', help='time the whole deformable attention layer')
-    ap.add_argument('--backward', action='store_true', help='time forward + backward (training)')
+    ap.add_argument('--backward', action='store_true',
+                    help='time forward + backward (training); with --layer, the whole layer\'s training step')
     ap.add_argument('--ref-dim', type=int, default=4, choices=(2, 4),
                     help='--layer: reference points (2) or reference boxes (4)')
     ap.add_argument('--dtype', nargs='+', default=['float16', 'bfloat16', 'float32'])
@@ -883,6 +968,8 @@ def main():
         run_l2_peak(args)
     elif args.sweep:
         run_sweep(args)
+    elif args.layer and args.backward:
+        run_layer_backward(args)
     elif args.layer:
         run_layer(args)
     elif args.backward:

@@ -112,8 +112,8 @@ TD_API int td_sampling_producer(int dtype, const void* proj, const void* referen
  * Backward of td_sampling_producer: from grad_locations [B, Q, H, L, P, 2] and grad_weights [B, Q, H, L, P] (either
  * may be NULL, meaning zero) and the forward's inputs, writes grad_proj [B, Q, 3 * H * L * P] (same layout as proj:
  * offset gradients, then logit gradients through the softmax) and, unless grad_reference_points is NULL,
- * grad_reference_points [B, Q, L, ref_dim] (summed over heads and points, in a fixed order: no atomics). One warp
- * per (batch, query). Launched with programmatic dependent launch. No counterpart in upstream (no producer, no
+ * grad_reference_points [B, Q, L, ref_dim] (summed over heads and points, in a fixed order: no atomics). One CTA
+ * per (batch, query), a warp per head. Launched with programmatic dependent launch. No counterpart in upstream (no producer, no
  * backward); the definition followed is the producer's own (Deformable-DETR's MSDeformAttn forward).
  */
 TD_API int td_sampling_producer_backward(int dtype, const void* proj, const void* reference_points, int ref_dim,

@@ -138,8 +138,9 @@ __global__ void __launch_bounds__(kProducerWarps * 32) sampling_producer_kernel(
 //   offsets: 2-d reference points: g_off = g_loc / (w_l, h_l);  4-d boxes: g_off = g_loc * wh / P * 0.5
 //   reference points (summed over the query's heads and each level's points):
 //            g_ref.xy += g_loc;  4-d boxes also g_ref.wh += g_loc * off / P * 0.5
-// One warp per (batch, query): the H heads one after another, lanes over the L * P points (two per lane, as the
-// forward), so the reference-point gradient of each level is a sum inside the warp (no atomics, fixed order).
+// One CTA per (batch, query), warp w taking heads w, w + kProducerWarps, ... with lanes over the L * P points (two
+// per lane, as the forward); the reference-point gradient is then summed over the warps and each level's points
+// through shared memory, in a fixed order (no atomics: bitwise reproducible).
 template <typename T>
 struct ProducerBwdArgs {
     const T* proj;            // [B * Q, 3 * H * L * P]: offsets (head, level, point, xy), then logits (head, L * P)
@@ -156,13 +157,12 @@ struct ProducerBwdArgs {
 template <typename T>
 __global__ void __launch_bounds__(kProducerWarps * 32) sampling_producer_backward_kernel(const ProducerBwdArgs<T> a) {
     using A = typename Elem<T>::acc;
-    // per warp and point: the point's reference-gradient terms summed over the heads (x, y, w, h)
+    // per warp and point: the point's reference-gradient terms summed over the warp's heads (x, y, w, h)
     __shared__ A s_sum[kProducerWarps][kMaxLevelPoints][4];
     grid_dependency_wait();
     launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long bq = (long long)blockIdx.x * kProducerWarps + warp;
-    if (bq >= a.bq) return;  // warp-uniform
+    const long long bq = blockIdx.x;
     const int LP = a.L * a.P;
     const long long row_len = 3LL * a.H * LP;
     const T* __restrict__ base = a.proj + bq * row_len;
@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(kProducerWarps * 32) sampling_producer_backwar
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[k][c] = A(0);
     }
-    for (int h = 0; h < a.H; ++h) {
+    for (int h = warp; h < a.H; h += kProducerWarps) {
         const T* __restrict__ off = base + (long long)h * LP * 2;
         const T* __restrict__ logit = base + 2LL * a.H * LP + (long long)h * LP;
         const long long pt0 = (bq * a.H + h) * LP;  // this head's first point in loc / attn
@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(kProducerWarps * 32) sampling_producer_backwar
             acc[k][1] += gy[k];
         }
     }
-    if (a.g_ref == nullptr) return;
+    if (a.g_ref == nullptr) return;  // uniform over the CTA
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
         const int j = lane + 32 * k;
@@ -253,13 +253,15 @@ __global__ void __launch_bounds__(kProducerWarps * 32) sampling_producer_backwar
             for (int c = 0; c < 4; ++c) s_sum[warp][j][c] = acc[k][c];
         }
     }
-    __syncwarp();
-    // output i (lanes over L * ref_dim): level i / ref_dim, coordinate i % ref_dim, summed over the level's points in
-    // order
-    for (int i = lane; i < a.L * a.ref_dim; i += 32) {
+    __syncthreads();
+    // output i (threads over L * ref_dim): level i / ref_dim, coordinate i % ref_dim, summed over the warps that held
+    // heads, then the level's points, in order
+    const int warps = a.H < kProducerWarps ? a.H : kProducerWarps;
+    for (int i = threadIdx.x; i < a.L * a.ref_dim; i += kProducerWarps * 32) {
         const int l = i / a.ref_dim, c = i - l * a.ref_dim;
         A v = A(0);
-        for (int p = 0; p < a.P; ++p) v += s_sum[warp][l * a.P + p][c];
+        for (int ww = 0; ww < warps; ++ww)
+            for (int p = 0; p < a.P; ++p) v += s_sum[ww][l * a.P + p][c];
         a.g_ref[(bq * a.L + l) * a.ref_dim + c] = from_acc<T>(v);
     }
 }

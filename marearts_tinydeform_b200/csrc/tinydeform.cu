@@ -939,7 +939,7 @@ int launch_producer(const T* proj, const T* ref, int ref_dim, const int64_t* sha
 
 template <typename T>
 int launch_producer_backward(const ProducerBwdArgs<T>& a, cudaStream_t stream, char* err, size_t err_len) {
-    const unsigned grid = unsigned((a.bq + kProducerWarps - 1) / kProducerWarps);
+    const unsigned grid = unsigned(a.bq);  // one CTA per (batch, query)
     const cudaError_t e = launch_kernel(sampling_producer_backward_kernel<T>, dim3(grid), dim3(kProducerWarps * 32),
                                         0, stream, true, a);
     if (e != cudaSuccess)
