@@ -538,6 +538,25 @@ def sharded_record(args, world, dev, cfg_name='c3'):
             times[name] = barrier_max(time_graph(g, args.steps, reps=max(5, args.reps // 5)), world)
             del g
         out = step(0, gather)
+        # the all-gather fused into the sampler (rows stored into every rank's output over NVLink): PeerGather
+        peer = None
+        if world > 1:
+            from marearts_tinydeform_b200.shard import PeerGather
+            pg = PeerGather(Bg, cfg['Q'], cfg['H'], cfg['D'], cfg['dtype'])
+            try:
+                dist.barrier()
+                g, _ = graph_time_us(lambda i: pg(*pool[i % len(pool)][:1], W, bias, shapes, starts,
+                                                  *pool[i % len(pool)][1:]), args.steps, args.warmup)
+                dist.barrier()
+                times['peer'] = barrier_max(time_graph(g, args.steps, reps=max(5, args.reps // 5)), world)
+                del g
+                torch.cuda.synchronize()
+                peer = torch.equal(pg(*pool[0][:1], W, bias, shapes, starts, *pool[0][1:]).clone(), out)
+                torch.cuda.synchronize()
+                if _native.device_error(clear=True) != 0:
+                    peer = False
+            finally:
+                pg.close()
     N, C, H, D, L, P, Q = base[0].shape[1], cfg['C'], cfg['H'], cfg['D'], len(cfg['levels']), cfg['P'], cfg['Q']
     e = base[0].element_size()
     hbm, _ = peaks()
@@ -551,6 +570,9 @@ def sharded_record(args, world, dev, cfg_name='c3'):
             'queries_per_s': round(Bg * Q / (t * 1e-6), 1), 'gathered_shape': list(out.shape),
             'gathered_bytes_per_rank': out.numel() * out.element_size() if gather else 0,
             'per_gpu_roofline_frac': round(alg / (times['no_gather'] * 1e-6) / 1e9 / hbm, 4),
+            **({'us_per_step_peer_gather': round(times['peer'], 3), 'peer_gather_equals_nccl': peer,
+                'peer_gather': 'rows stored into every rank\'s output over NVLink by the sampler (PeerGather)'}
+               if 'peer' in times else {}),
             'timing': 'CUDA graph of K steps (NCCL all-gather captured), median of replays, max over ranks'}
 
 

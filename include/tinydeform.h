@@ -307,6 +307,43 @@ TD_API int td_probe_row_gather(const void* buf, int64_t rows, int row_bytes, int
                                void* sink, size_t sink_bytes, int grid, void* stream, char* err, size_t err_len);
 
 /*
+ * Batch sharding with the output all-gather fused into the sampler (no upstream counterpart: upstream has no
+ * distributed code; this replaces the project order's separate all-gather collective). One process per GPU; every
+ * rank holds a gathered output buffer [B_global, Q, H * D] and a control block, allocated here and mapped into every
+ * other rank through CUDA IPC (the handles travel over the caller's own host collective):
+ *   td_peer_buffer_alloc  cudaMalloc'd, zeroed buffer and its IPC handle (TD_IPC_HANDLE_BYTES bytes);
+ *   td_peer_buffer_open   a peer's buffer from its handle (peer access enabled lazily); closed by
+ *   td_peer_buffer_close  (opened = 1 for a peer's mapping, 0 for this process's own allocation).
+ * td_project_forward_peer computes this rank's B images (global images first_image .. first_image + B - 1) in the
+ * project order and stores every output row into all `world` buffers (outputs[r] = rank r's buffer as mapped in
+ * this process, controls[r] likewise its control block of TD_PEER_CTRL_BYTES bytes, zeroed at allocation); a one-warp
+ * kernel behind it signals every peer once the rows are stored and waits (bounded, about one second; a peer that
+ * never signals sets code TD_DEVERR_PEER_WAIT in td_device_error) until every peer has signalled this call. After it,
+ * the buffer holds every rank's rows. Every rank must make the same sequence of calls (a rank with no images passes
+ * B = 0 and still signals). Epochs are kept in the control blocks on the device, so a captured CUDA graph replays
+ * correctly. A peer may write the next call's rows as soon as this rank's wait has finished: consume the buffer
+ * before the next call, or alternate two buffer sets. Shapes: D * element size of 16 * 2^k bytes up to 512; 1-8
+ * ranks; workspace td_project_workspace_bytes(dtype, B, N, HD).
+ */
+#define TD_IPC_HANDLE_BYTES 64
+#define TD_PEER_CTRL_BYTES 64
+#define TD_DEVERR_PEER_WAIT 5
+TD_API int td_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle, char* err, size_t err_len);
+TD_API int td_peer_buffer_open(const void* ipc_handle, void** ptr, char* err, size_t err_len);
+TD_API int td_peer_buffer_close(void* ptr, int opened, char* err, size_t err_len);
+TD_API int td_project_forward_peer(int dtype, const void* memory, const void* value_weight, const void* value_bias,
+                                   const int64_t* spatial_shapes, const int64_t* level_start_index,
+                                   const void* sampling_locations, const void* attention_weights,
+                                   const uint8_t* value_padding_mask, int64_t B, int64_t Q, int64_t N, int64_t C,
+                                   int64_t H, int64_t HD, int64_t L, int64_t P, int64_t first_image, int world,
+                                   int rank, void* const* outputs, void* const* controls, void* workspace,
+                                   size_t workspace_bytes, void* stream, char* err, size_t err_len);
+/* Test only: the peer wait alone on one control block, with a wait limit of limit_cycles clock cycles (a test makes
+ * it run out on one GPU by naming a peer that never signals). */
+TD_API int td_test_peer_wait(void* control, int world, int rank, long long limit_cycles, void* stream, char* err,
+                             size_t err_len);
+
+/*
  * Kernel policy for every later call in this process: TD_POLICY_BEST (default) uses the tcgen05 tensor-core
  * kernels wherever the shapes allow; TD_POLICY_CUDA_CORES keeps every call on the CUDA-core kernels (parity tests
  * run both). No counterpart in upstream, which has only CUDA-core kernels. Returns the previous policy.

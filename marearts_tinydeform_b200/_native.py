@@ -32,6 +32,14 @@ SIGNATURES = {
                                 _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _cp, _sz]),
     'td_value_proj': (_ip, [_ip, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _ip, _vp, _cp, _sz]),
     'td_project_workspace_bytes': (_sz, [_ip, _i64, _i64, _i64]),
+    'td_peer_buffer_alloc': (_ip, [_sz, ctypes.POINTER(ctypes.c_void_p), _vp, _cp, _sz]),
+    'td_peer_buffer_open': (_ip, [_vp, ctypes.POINTER(ctypes.c_void_p), _cp, _sz]),
+    'td_peer_buffer_close': (_ip, [_vp, ctypes.c_int, _cp, _sz]),
+    'td_project_forward_peer': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
+                                      _i64, _i64, _i64, _i64, ctypes.c_int, ctypes.c_int,
+                                      ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p), _vp, _sz,
+                                      _vp, _cp, _sz]),
+    'td_test_peer_wait': (_ip, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_longlong, _vp, _cp, _sz]),
     'td_project_forward': (_ip, [_ip, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                  _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp, _cp, _sz]),
     'td_linear': (_ip, [_ip, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _cp, _sz]),
@@ -281,6 +289,59 @@ def project_forward(memory, value_weight, value_bias, spatial_shapes, level_star
     e = memory.element_size()
     value = ws[skip:skip + B * N * HD * e].view(memory.dtype).view(B, H, N, HD // H)
     return out, value
+
+
+IPC_HANDLE_BYTES, PEER_CTRL_BYTES, DEVERR_PEER_WAIT = 64, 64, 5
+
+
+def peer_buffer_alloc(nbytes):
+    """(device pointer, IPC handle bytes) of a new zeroed device buffer that other processes can map."""
+    ptr = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    _call(load().td_peer_buffer_alloc, nbytes, ctypes.byref(ptr), ctypes.cast(handle, ctypes.c_void_p))
+    return ptr.value, handle.raw
+
+
+def peer_buffer_open(handle):
+    """Device pointer of another process's buffer, mapped into this one from its IPC handle."""
+    ptr = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(bytes(handle), IPC_HANDLE_BYTES)
+    _call(load().td_peer_buffer_open, ctypes.cast(buf, ctypes.c_void_p), ctypes.byref(ptr))
+    return ptr.value
+
+
+def peer_buffer_close(ptr, opened):
+    _call(load().td_peer_buffer_close, ctypes.c_void_p(ptr), 1 if opened else 0)
+
+
+def project_forward_peer(memory, value_weight, value_bias, spatial_shapes, level_start_index, sampling_locations,
+                         attention_weights, first_image, rank, outputs, controls, value_padding_mask=None):
+    """This rank's images in the project order, every output row stored into every rank's gathered buffer
+    (outputs / controls: device pointers in rank order, as mapped in this process), through td_project_forward_peer;
+    returns nothing (the rows land in the buffers)."""
+    lib = load()
+    B, Q, H, L, P = check_geometry(memory, spatial_shapes, level_start_index, sampling_locations, attention_weights)
+    HD = check_projection(memory, value_weight, value_bias, H)
+    mask = check_mask(value_padding_mask, memory)
+    N, C = memory.size(1), memory.size(2)
+    mem, w, b, shp, st, loc, att = _dense(memory, value_weight, value_bias, spatial_shapes, level_start_index,
+                                          sampling_locations, attention_weights)
+    code = DTYPE_CODE[memory.dtype]
+    ws_bytes = lib.td_project_workspace_bytes(code, B, N, HD)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=memory.device)
+    world = len(outputs)
+    outs = (ctypes.c_void_p * world)(*outputs)
+    ctrls = (ctypes.c_void_p * world)(*controls)
+    with torch.cuda.device(memory.device):
+        _call(lib.td_project_forward_peer, code, _ptr(mem), _ptr(w), _ptr(b), _ptr(shp), _ptr(st), _ptr(loc),
+              _ptr(att), _ptr(mask), B, Q, N, C, H, HD, L, P, first_image, world, rank, outs, ctrls, _ptr(ws),
+              ws_bytes, _stream(memory.device))
+
+
+def test_peer_wait(control_ptr, world, rank, limit_cycles, device):
+    """Test hook: the peer wait alone on one control block with a short limit (td_test_peer_wait)."""
+    with torch.cuda.device(device):
+        _call(load().td_test_peer_wait, ctypes.c_void_p(control_ptr), world, rank, limit_cycles, _stream(device))
 
 
 def linear(x, weight, bias):

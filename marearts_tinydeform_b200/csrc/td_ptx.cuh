@@ -23,6 +23,7 @@ enum DeviceError : unsigned int {
     kErrMmaWait = 2,      // an MMA commit never arrived
     kErrSlotWait = 3,     // a pipeline slot was never released
     kErrBounds = 4,       // TD_DEBUG_BOUNDS builds: a corner token outside [0, N) reached a gather or scatter
+    kErrPeerWait = 5,     // the peer-gather wait: a peer rank never signalled its rows within the limit
 };
 
 constexpr long long kSpinLimitCycles = 2000000000LL;  // ~1 s at 1.9 GHz

@@ -12,6 +12,7 @@
 #include <initializer_list>
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <type_traits>
 
@@ -27,6 +28,7 @@
 #include "td_backward.cuh"
 #include "td_sampler.cuh"
 #include "td_sample_outproj.cuh"
+#include "td_peer_gather.cuh"
 #include "td_probe.cuh"
 
 namespace td {
@@ -1438,6 +1440,150 @@ int td_project_forward_masked(int dtype, const void* memory, const void* value_w
                                  static_cast<T*>(out), B, Q, N, H, D, L, P, s, err, err_len, true,
                                  value_padding_mask);
     });
+}
+
+static_assert(td::kErrPeerWait == TD_DEVERR_PEER_WAIT, "peer wait error code");
+static_assert(td::kPeerCtrlWords * 4 == TD_PEER_CTRL_BYTES, "peer control block size");
+
+int td_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle, char* err, size_t err_len) {
+    if (ptr == nullptr || ipc_handle == nullptr || bytes == 0)
+        return fail(err, err_len, TD_ERR_ARG, "peer buffer needs bytes > 0 and output pointers");
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        if (p != nullptr) cudaFree(p);
+        cudaGetLastError();
+        return fail(err, err_len, TD_ERR_CUDA, "peer buffer of %zu bytes: %s", bytes, cudaGetErrorString(e));
+    }
+    static_assert(sizeof(h) == TD_IPC_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(ipc_handle, &h, sizeof(h));
+    *ptr = p;
+    return TD_OK;
+}
+
+int td_peer_buffer_open(const void* ipc_handle, void** ptr, char* err, size_t err_len) {
+    if (ptr == nullptr || ipc_handle == nullptr) return fail(err, err_len, TD_ERR_ARG, "null pointer");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, ipc_handle, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(err, err_len, TD_ERR_CUDA, "opening a peer's buffer: %s", cudaGetErrorString(e));
+    }
+    return TD_OK;
+}
+
+int td_peer_buffer_close(void* ptr, int opened, char* err, size_t err_len) {
+    if (ptr == nullptr) return TD_OK;
+    const cudaError_t e = opened ? cudaIpcCloseMemHandle(ptr) : cudaFree(ptr);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(err, err_len, TD_ERR_CUDA, "closing a peer buffer: %s", cudaGetErrorString(e));
+    }
+    return TD_OK;
+}
+
+int td_project_forward_peer(int dtype, const void* memory, const void* value_weight, const void* value_bias,
+                            const int64_t* spatial_shapes, const int64_t* level_start_index,
+                            const void* sampling_locations, const void* attention_weights,
+                            const uint8_t* value_padding_mask, int64_t B, int64_t Q, int64_t N, int64_t C,
+                            int64_t H, int64_t HD, int64_t L, int64_t P, int64_t first_image, int world, int rank,
+                            void* const* outputs, void* const* controls, void* workspace, size_t workspace_bytes,
+                            void* stream, char* err, size_t err_len) {
+    if (dtype_size(dtype) == 0) return fail(err, err_len, TD_ERR_ARG, "unsupported dtype code %d", dtype);
+    if (int rc = check_geometry(B, Q, N, H, L, P, err, err_len)) return rc;
+    if (C <= 0 || HD <= 0) return fail(err, err_len, TD_ERR_ARG, "channels and value_weight rows must be positive");
+    if (HD % H != 0) return fail(err, err_len, TD_ERR_ARG, "value_weight rows must be a multiple of the head count");
+    if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world)
+        return fail(err, err_len, TD_ERR_ARG, "the peer gather takes 1 to %d ranks (rank %d of %d)", kMaxPeers, rank,
+                    world);
+    if (first_image < 0) return fail(err, err_len, TD_ERR_ARG, "first_image must be >= 0");
+    if (outputs == nullptr || controls == nullptr) return fail(err, err_len, TD_ERR_ARG, "null peer pointer table");
+    for (int r = 0; r < world; ++r)
+        if (outputs[r] == nullptr || controls[r] == nullptr) return fail(err, err_len, TD_ERR_ARG, "null peer pointer");
+    if (B * Q > 0 && (!memory || !value_weight || !sampling_locations || !attention_weights ||
+                      (L * P > 0 && (!spatial_shapes || !level_start_index))))
+        return fail(err, err_len, TD_ERR_ARG, "null tensor pointer");
+    const int64_t D = HD / H;
+    const size_t e = dtype_size(dtype);
+    const long long row_bytes = D * (long long)e;
+    const long long G = row_bytes / 16;
+    // the vector sampler's conditions (the value is this call's own head-major projection)
+    if (row_bytes % 16 != 0 || row_bytes > 512 || (G & (G - 1)) != 0)
+        return fail(err, err_len, TD_ERR_ARG, "the peer gather needs D * element size = 16, 32, ... 512 bytes");
+    for (int r = 0; r < world; ++r)
+        if (!aligned16(outputs[r])) return fail(err, err_len, TD_ERR_ARG, "peer outputs must be 16-byte aligned");
+    const size_t need = td_project_workspace_bytes(dtype, B, N, HD);
+    if (B * Q > 0 && (workspace == nullptr || workspace_bytes < need))
+        return fail(err, err_len, TD_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need,
+                    workspace_bytes);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    void* value = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+    return dispatch(dtype, [&](auto tag) -> int {
+        using T = decltype(tag);
+        T* v = static_cast<T*>(value);
+        const bool project = B * Q > 0 && N > 0;
+        if (project) {
+            if (int rc = launch_proj<T>(static_cast<const T*>(memory), static_cast<const T*>(value_weight),
+                                        static_cast<const T*>(value_bias), v, B, N, C, H, HD, 1, s, err, err_len,
+                                        true))
+                return rc;
+        }
+        SampleArgs<T> a;
+        a.value = v; a.loc = static_cast<const T*>(sampling_locations); a.attn = static_cast<const T*>(attention_weights);
+        a.out = nullptr; a.shapes = spatial_shapes; a.starts = level_start_index; a.prod = ProducerIn<T>{};
+        a.rows = B * Q * H; a.s_img = H * N * D; a.s_tok = D; a.s_head = N * D; a.n_tok = N; a.mask = value_padding_mask;
+        a.Q = int(Q); a.H = int(H); a.D = int(D); a.L = int(L); a.P = int(P); a.G = int(G);
+        const bool wide = row_bytes % 32 == 0 && row_bytes >= 128;
+        if (wide) a.G = int(row_bytes / 32);
+        const bool no_alloc = B * H * N * D * (long long)e > (64LL << 20);
+        PeerOut<T> po;
+        PeerCtrl pc;
+        for (int r = 0; r < kMaxPeers; ++r) {
+            po.out[r] = r < world ? static_cast<T*>(outputs[r]) : nullptr;
+            pc.p[r] = r < world ? static_cast<unsigned*>(controls[r]) : nullptr;
+        }
+        po.row0 = first_image * Q * H; po.world = world; po.rank = rank;
+        if (a.rows > 0) {
+            const unsigned grid = unsigned((a.rows + kSampleWarps - 1) / kSampleWarps);
+            const size_t smem = sample_vec_smem<T>(int(L), int(P));
+            const cudaError_t ce = wide ? launch_kernel(sample_peer_kernel<T, true, true>, dim3(grid),
+                                                        dim3(kSampleWarps * 32), smem, s, project, a, po)
+                                   : no_alloc ? launch_kernel(sample_peer_kernel<T, false, true>, dim3(grid),
+                                                              dim3(kSampleWarps * 32), smem, s, project, a, po)
+                                              : launch_kernel(sample_peer_kernel<T, false, false>, dim3(grid),
+                                                              dim3(kSampleWarps * 32), smem, s, project, a, po);
+            if (ce != cudaSuccess)
+                return fail(err, err_len, TD_ERR_CUDA, "sample_peer_kernel launch: %s", cudaGetErrorString(ce));
+            g_launches.fetch_add(1, std::memory_order_relaxed);
+            if (int rc = check_launch(err, err_len, "sample_peer_kernel")) return rc;
+        }
+        if (world == 1) return int(TD_OK);
+        // a rank with an empty shard still signals its peers and waits for theirs
+        const cudaError_t ce = launch_kernel(peer_signal_wait_kernel, dim3(1), dim3(32), 0, s, true, pc, world, rank,
+                                             1, kSpinLimitCycles);
+        if (ce != cudaSuccess)
+            return fail(err, err_len, TD_ERR_CUDA, "peer_signal_wait_kernel launch: %s", cudaGetErrorString(ce));
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+        return check_launch(err, err_len, "peer_signal_wait_kernel");
+    });
+}
+
+int td_test_peer_wait(void* control, int world, int rank, long long limit_cycles, void* stream, char* err,
+                      size_t err_len) {
+    if (control == nullptr || world < 2 || world > kMaxPeers || rank < 0 || rank >= world || limit_cycles <= 0)
+        return fail(err, err_len, TD_ERR_ARG, "bad peer wait arguments");
+    PeerCtrl pc;
+    for (int r = 0; r < kMaxPeers; ++r) pc.p[r] = r == rank ? static_cast<unsigned*>(control) : nullptr;
+    const cudaError_t ce = launch_kernel(peer_signal_wait_kernel, dim3(1), dim3(32), 0,
+                                         static_cast<cudaStream_t>(stream), false, pc, world, rank, 0, limit_cycles);
+    if (ce != cudaSuccess)
+        return fail(err, err_len, TD_ERR_CUDA, "peer_signal_wait_kernel launch: %s", cudaGetErrorString(ce));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return check_launch(err, err_len, "peer_signal_wait_kernel");
 }
 
 size_t td_layer_workspace_bytes(int dtype, int order, int64_t B, int64_t Q, int64_t N, int64_t H, int64_t HD,
