@@ -724,7 +724,10 @@ def run_layer_backward(args):
     out32 = torch.nn.functional.linear(ma_deform_attn_reference(up[2], up[5], up[6], shapes_host, starts_host, loc32,
                                                                 attn32), up[7], up[8])
     want = torch.autograd.grad(out32, up, gouts[0].float())
-    rel = max(float((a.float() - b).abs().max()) / max(float(b.abs().max()), 1e-30) for a, b in zip(ours(0), want))
+    names = ('query', 'reference_points', 'memory', 'sampling_weight', 'sampling_bias', 'value_weight', 'value_bias',
+             'output_weight', 'output_bias')
+    rel = {n: round(float((a.float() - b).abs().max()) / max(float(b.abs().max()), 1e-30), 5)
+           for n, a, b in zip(names, ours(0), want)}
     line = {
         'metric': 'µs per training step of the deformable attention layer (forward + every gradient, device-timed)',
         'value': round(times['ours'], 3), 'unit': 'us', 'n_gpus': 1, 'steps': args.steps, 'warmup': args.warmup,
@@ -732,7 +735,8 @@ def run_layer_backward(args):
         'data': 'synthetic (seeded, BASELINE config shapes)',
         'config': dict(config_dict(args.config, 1, mode), query_dim=C, reference_points=args.ref_dim,
                        output_proj=[C, H * D]),
-        'all_torch_us': round(times['all_torch'], 3), 'max_rel_grad_diff_vs_float32_torch': rel,
+        'all_torch_us': round(times['all_torch'], 3),
+        'grad_max_rel_diff_vs_float32_torch': rel,  # per input: max |diff| / max |grad|
         'gpu_launches': launches, 'clocks': clocks.summary(),
     }
     print(json.dumps(line), flush=True)

@@ -17,9 +17,10 @@
 //   * warp 1, one lane: MMA issuer (tcgen05.mma kind::f16, M = 128, N = BN, four K steps of 16 a block; a K step
 //     advances a K-major descriptor by 32 bytes and an MN-major one by 2048 bytes), float32 accumulator in TMEM;
 //   * warps 4-7: epilogue, TMEM lane = tile row. Input gradient: narrowed to the input type and stored. Weight
-//     gradient (K split over CTAs so that the grid fills the SMs): added into a float32 accumulator with 16-byte
-//     vector reductions (red.global.add.v4.f32); the CTA whose arrival on the tile's counter comes last converts the
-//     tile to the output type. No CTA waits for another.
+//     gradient (K split over CTAs so that the grid fills the SMs): each CTA stores its float32 partial tile into its
+//     split's slice of a workspace, and grad_split_reduce_kernel then sums the slices in split order and converts
+//     (deterministic; it replaced float32 vector reductions into one accumulator with a last-arriving CTA
+//     converting, whose 33-way contention per address at c1h made the GEMM 24.8 us). No CTA waits for another.
 // float32 and float64 run grad_gemm_simt_kernel: 64 x 64 tiles on CUDA cores, K split the same way, float32 /
 // float64 atomic adds straight into the (zeroed) output for the weight gradient.
 // Every mbarrier wait is bounded (td_ptx.cuh).
@@ -35,8 +36,7 @@ namespace td {
 template <typename T>
 struct GradGemmArgs {
     T* out;               // [rows, cols] row-major
-    float* acc;           // weight gradient of 16-bit types: float32 [rows, cols], zero before the launch
-    unsigned* arrivals;   // weight gradient of 16-bit types: one counter per output tile, zero before the launch
+    float* acc;           // weight gradient of 16-bit types: float32 partial sums [splits, rows, cols]
     int rows, cols;       // output size (M x N of the GEMM)
     int m_tiles, n_tiles, splits;
     int k_blocks;         // 64-deep K blocks in all
@@ -71,14 +71,9 @@ __device__ __forceinline__ uint64_t sdesc_sw128_mn(uint32_t saddr) {
     return d;
 }
 
-// 16-byte vector reduction into global float32 memory (sm_90+); p 16-byte aligned.
-__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
-    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
-                 : "memory");
-}
-
-// A_MN: A is MN-major (weight gradient); otherwise K-major (input gradient). SPLIT: float32 reductions + last-CTA
-// conversion (weight gradient); otherwise direct stores.
+// A_MN: A is MN-major (weight gradient); otherwise K-major (input gradient). SPLIT: each CTA stores its float32
+// partial tile into its split's slice of `acc` (weight gradient; grad_split_reduce_kernel sums the slices in split
+// order and converts); otherwise direct stores.
 template <typename T, bool A_MN, int BN, bool SPLIT>
 __global__ void __launch_bounds__(256) grad_gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a,
                                                            const __grid_constant__ CUtensorMap map_b,
@@ -94,7 +89,6 @@ __global__ void __launch_bounds__(256) grad_gemm_tc_kernel(const __grid_constant
     uint64_t* tfull = empty + S;
     uint64_t* drained = tfull + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Lay::kSlotOffset);
-    uint32_t* last_flag = tmem_slot + 1;
     auto slot_a = [&](int s) { return smem + s * Lay::kStageBytes; };
     auto slot_b = [&](int s) { return smem + s * Lay::kStageBytes + Lay::kABytes; };
 
@@ -103,7 +97,6 @@ __global__ void __launch_bounds__(256) grad_gemm_tc_kernel(const __grid_constant
     const int split = t % a.splits;
     t /= a.splits;
     const int nt = t % a.n_tiles, mt = t / a.n_tiles;
-    const int tile = t;
     const int m0 = mt * 128, n0 = nt * BN;
     const int kb0 = split * a.kb_per_split;
     const int kb1 = min(kb0 + a.kb_per_split, a.k_blocks);
@@ -210,27 +203,10 @@ __global__ void __launch_bounds__(256) grad_gemm_tc_kernel(const __grid_constant
                 const float f0 = __uint_as_float(v[4 * g]), f1 = __uint_as_float(v[4 * g + 1]);
                 const float f2 = __uint_as_float(v[4 * g + 2]), f3 = __uint_as_float(v[4 * g + 3]);
                 if constexpr (SPLIT) {
-                    red_add_v4(a.acc + (long long)row * a.cols + col, f0, f1, f2, f3);
+                    *reinterpret_cast<float4*>(a.acc + ((long long)split * a.rows + row) * a.cols + col) =
+                        make_float4(f0, f1, f2, f3);
                 } else {
                     const T q[4] = {from_acc<T>(f0), from_acc<T>(f1), from_acc<T>(f2), from_acc<T>(f3)};
-                    *reinterpret_cast<uint2*>(a.out + (long long)row * a.cols + col) =
-                        *reinterpret_cast<const uint2*>(q);
-                }
-            }
-        }
-        if constexpr (SPLIT) {
-            // the CTA whose arrival completes the tile converts it: every earlier CTA fenced its reductions before
-            // arriving, and this one fences before reading them back from L2
-            __threadfence();
-            named_barrier(1, 128);
-            if (threadIdx.x == 128)
-                *last_flag = (atomicAdd(a.arrivals + tile, 1u) == unsigned(a.splits - 1)) ? 1u : 0u;
-            named_barrier(1, 128);
-            if (*last_flag != 0u && ready && row < a.rows) {
-                __threadfence();
-                for (int col = n0; col < n0 + BN && col < a.cols; col += 4) {
-                    const float4 x = __ldcg(reinterpret_cast<const float4*>(a.acc + (long long)row * a.cols + col));
-                    const T q[4] = {from_acc<T>(x.x), from_acc<T>(x.y), from_acc<T>(x.z), from_acc<T>(x.w)};
                     *reinterpret_cast<uint2*>(a.out + (long long)row * a.cols + col) =
                         *reinterpret_cast<const uint2*>(q);
                 }
@@ -243,6 +219,24 @@ __global__ void __launch_bounds__(256) grad_gemm_tc_kernel(const __grid_constant
         tc_fence_after();
         tmem_dealloc(tmem, BN);
     }
+}
+
+// The weight gradient's second stage: out[i] = sum over s < splits, in order, of partial[s][i] (float32), converted
+// to T; four elements a thread (elems is a multiple of 4: cols is a multiple of 8).
+template <typename T>
+__global__ void __launch_bounds__(256) grad_split_reduce_kernel(const float* __restrict__ partial, T* __restrict__ out,
+                                                                int splits, long long elems) {
+    grid_dependency_wait();
+    launch_dependents();
+    const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (i >= elems) return;
+    float4 acc = __ldcg(reinterpret_cast<const float4*>(partial + i));
+    for (int sp = 1; sp < splits; ++sp) {
+        const float4 x = __ldcg(reinterpret_cast<const float4*>(partial + (long long)sp * elems + i));
+        acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+    }
+    const T q[4] = {from_acc<T>(acc.x), from_acc<T>(acc.y), from_acc<T>(acc.z), from_acc<T>(acc.w)};
+    *reinterpret_cast<uint2*>(out + i) = *reinterpret_cast<const uint2*>(q);
 }
 
 // CUDA-core form (float32, float64, and 16-bit shapes the tensor-core kernel does not take): out[m, n] =

@@ -867,20 +867,24 @@ inline int grad_splits(int64_t tiles, int64_t k_blocks, int sm_count, int64_t mi
     return int(std::max<int64_t>(splits, 1));
 }
 
-// Workspace of td_linear_grad_weight, laid out as: float32 accumulator [Nout, K] | arrival counters | float32 bias
-// sums [Nout] | bias arrival counters; every region 256-byte aligned (16-bit types only; float32 / float64
-// accumulate in the outputs themselves).
+// The weight gradient's K splits are capped so that tiles x splits <= kGradMaxCtas (at least the SM count of any
+// part this runs on): its float32 partials then take at most kGradMaxCtas x 64 KB of workspace.
+constexpr int64_t kGradMaxCtas = 256;
+inline int64_t grad_split_cap(int64_t tiles) { return std::max<int64_t>(1, kGradMaxCtas / std::max<int64_t>(tiles, 1)); }
+
+// Workspace of td_linear_grad_weight, laid out as: float32 partial sums [splits, Nout, K] | float32 bias sums [Nout] |
+// bias arrival counters; every region 256-byte aligned (16-bit types only; float32 / float64 accumulate in the
+// outputs themselves).
 struct GradWeightWs {
-    size_t acc = 0, arrivals = 0, bias = 0, bias_arrivals = 0, total = 0;
+    size_t acc = 0, bias = 0, bias_arrivals = 0, total = 0;
 };
 inline GradWeightWs grad_weight_ws(int dtype, int64_t Nout, int64_t K) {
     GradWeightWs w;
     if (dtype != TD_F16 && dtype != TD_BF16) return w;
     auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
-    const size_t tiles = size_t((Nout + 127) / 128) * size_t((K + 127) / 128);
+    const int64_t tiles = ((Nout + 127) / 128) * ((K + 127) / 128);
     w.acc = 0;
-    w.arrivals = up(size_t(Nout) * size_t(K) * 4);
-    w.bias = w.arrivals + up(tiles * 4);
+    w.bias = up(size_t(grad_split_cap(tiles)) * size_t(Nout) * size_t(K) * 4);
     w.bias_arrivals = w.bias + up(size_t(Nout) * 4);
     w.total = w.bias_arrivals + up(size_t((Nout + 255) / 256) * 4) + 256;  // + 256: alignment of the base
     return w;
@@ -1261,23 +1265,30 @@ int td_linear_grad_weight(int dtype, const void* grad_out, const void* input, vo
                 GradGemmArgs<T> g{};
                 g.out = static_cast<T*>(grad_weight);
                 g.acc = reinterpret_cast<float*>(ws + w.acc);
-                g.arrivals = reinterpret_cast<unsigned*>(ws + w.arrivals);
                 g.rows = int(Nout);
                 g.cols = int(K);
                 g.m_tiles = int((Nout + 127) / 128);
                 g.n_tiles = int((K + 127) / 128);
+                const int64_t tiles = int64_t(g.m_tiles) * g.n_tiles;
                 int64_t per = 0;
                 g.k_blocks = int((M + 63) / 64);
-                g.splits = grad_splits(int64_t(g.m_tiles) * g.n_tiles, g.k_blocks, f.sm_count, 4, &per);
+                g.splits = grad_splits(tiles, g.k_blocks, int(std::min<int64_t>(f.sm_count, kGradMaxCtas)), 4, &per);
                 g.kb_per_split = int(per);
-                cudaError_t e = cudaMemsetAsync(g.acc, 0, size_t(Nout) * size_t(K) * 4, s);
-                if (e == cudaSuccess)
-                    e = cudaMemsetAsync(g.arrivals, 0, size_t(g.m_tiles) * size_t(g.n_tiles) * 4, s);
+                // A = grad_out [M, Nout] and B = input [M, K], both MN-major (the sum runs over their M rows); every
+                // CTA writes its whole partial tile, so the partials need no clearing
+                if (int rc = launch_grad_tc<T, true, 128, true>(grad_out, uint64_t(Nout), uint64_t(M), 64, input,
+                                                                uint64_t(K), uint64_t(M), g, s, err, err_len))
+                    return rc;
+                const long long elems = (long long)Nout * K;
+                const unsigned grid = unsigned((elems / 4 + 255) / 256);
+                const cudaError_t e = launch_kernel(grad_split_reduce_kernel<T>, dim3(grid), dim3(256), 0, s, true,
+                                                    static_cast<const float*>(g.acc), static_cast<T*>(grad_weight),
+                                                    g.splits, elems);
                 if (e != cudaSuccess)
-                    return fail(err, err_len, TD_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
-                // A = grad_out [M, Nout] and B = input [M, K], both MN-major (the sum runs over their M rows)
-                return launch_grad_tc<T, true, 128, true>(grad_out, uint64_t(Nout), uint64_t(M), 64, input,
-                                                          uint64_t(K), uint64_t(M), g, s, err, err_len);
+                    return fail(err, err_len, TD_ERR_CUDA, "grad_split_reduce_kernel launch: %s",
+                                cudaGetErrorString(e));
+                g_launches.fetch_add(1, std::memory_order_relaxed);
+                return check_launch(err, err_len, "grad_split_reduce_kernel");
             }
         }
         GradSimtArgs<T> p{};
