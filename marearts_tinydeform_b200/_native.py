@@ -630,8 +630,8 @@ OUTPROJ_AUTO, OUTPROJ_CHAINED, OUTPROJ_CLUSTER = 0, 1, 2
 
 def set_output_proj_plan(plan):
     """How the project order applies output_proj: OUTPROJ_AUTO (in the sampler's cluster kernel while its grid is one
-    wave, B * Q * H / 8 <= 3 CTAs per SM; the default), OUTPROJ_CHAINED (a separate GEMM) or OUTPROJ_CLUSTER (the cluster
-    kernel wherever its shape conditions hold); returns the previous plan."""
+    wave, B * Q * H / 8 <= 3 CTAs per SM; the default), OUTPROJ_CHAINED (a separate GEMM) or OUTPROJ_CLUSTER (the
+    cluster kernel wherever its shape conditions hold); returns the previous plan."""
     prev = load().td_set_output_proj_plan(plan)
     if prev < 0:
         raise ValueError(f'unknown output_proj plan {plan}')

@@ -222,18 +222,28 @@ __global__ void __launch_bounds__(256) grad_gemm_tc_kernel(const __grid_constant
 }
 
 // The weight gradient's second stage: out[i] = sum over s < splits, in order, of partial[s][i] (float32), converted
-// to T; four elements a thread (elems is a multiple of 4: cols is a multiple of 8).
+// to T; four elements a thread (elems is a multiple of 4: cols is a multiple of 8), the partials read eight splits
+// at a time so that eight L2 round trips are in flight (the sum is still taken in split order).
+constexpr int kReduceThreads = 128;
 template <typename T>
-__global__ void __launch_bounds__(256) grad_split_reduce_kernel(const float* __restrict__ partial, T* __restrict__ out,
-                                                                int splits, long long elems) {
+__global__ void __launch_bounds__(kReduceThreads) grad_split_reduce_kernel(const float* __restrict__ partial,
+                                                                           T* __restrict__ out, int splits,
+                                                                           long long elems) {
     grid_dependency_wait();
     launch_dependents();
     const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
     if (i >= elems) return;
-    float4 acc = __ldcg(reinterpret_cast<const float4*>(partial + i));
-    for (int sp = 1; sp < splits; ++sp) {
-        const float4 x = __ldcg(reinterpret_cast<const float4*>(partial + (long long)sp * elems + i));
-        acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < splits; s0 += 8) {
+        float4 x[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            x[u] = s0 + u < splits ? __ldcg(reinterpret_cast<const float4*>(partial + (long long)(s0 + u) * elems + i))
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            acc.x += x[u].x; acc.y += x[u].y; acc.z += x[u].z; acc.w += x[u].w;
+        }
     }
     const T q[4] = {from_acc<T>(acc.x), from_acc<T>(acc.y), from_acc<T>(acc.z), from_acc<T>(acc.w)};
     *reinterpret_cast<uint2*>(out + i) = *reinterpret_cast<const uint2*>(q);

@@ -224,7 +224,9 @@ __device__ __forceinline__ uint4 ld_cluster_v4(uint32_t caddr) {
 // Cluster-wide barrier in two halves (every thread of every CTA of the cluster executes both, in order): arrive
 // releases this thread's earlier shared-memory writes to the cluster, wait returns once every thread has arrived
 // and acquires theirs. A hardware barrier, not a spin: the cluster's CTAs are co-scheduled by construction.
-__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 // Arrive without ordering this thread's earlier memory accesses (for a barrier that only marks that they are done).
 __device__ __forceinline__ void cluster_arrive_relaxed() {

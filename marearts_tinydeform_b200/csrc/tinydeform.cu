@@ -870,7 +870,9 @@ inline int grad_splits(int64_t tiles, int64_t k_blocks, int sm_count, int64_t mi
 // The weight gradient's K splits are capped so that tiles x splits <= kGradMaxCtas (at least the SM count of any
 // part this runs on): its float32 partials then take at most kGradMaxCtas x 64 KB of workspace.
 constexpr int64_t kGradMaxCtas = 256;
-inline int64_t grad_split_cap(int64_t tiles) { return std::max<int64_t>(1, kGradMaxCtas / std::max<int64_t>(tiles, 1)); }
+inline int64_t grad_split_cap(int64_t tiles) {
+    return std::max<int64_t>(1, kGradMaxCtas / std::max<int64_t>(tiles, 1));
+}
 
 // Workspace of td_linear_grad_weight, laid out as: float32 partial sums [splits, Nout, K] | float32 bias sums [Nout] |
 // bias arrival counters; every region 256-byte aligned (16-bit types only; float32 / float64 accumulate in the
@@ -1280,10 +1282,10 @@ int td_linear_grad_weight(int dtype, const void* grad_out, const void* input, vo
                                                                 uint64_t(K), uint64_t(M), g, s, err, err_len))
                     return rc;
                 const long long elems = (long long)Nout * K;
-                const unsigned grid = unsigned((elems / 4 + 255) / 256);
-                const cudaError_t e = launch_kernel(grad_split_reduce_kernel<T>, dim3(grid), dim3(256), 0, s, true,
-                                                    static_cast<const float*>(g.acc), static_cast<T*>(grad_weight),
-                                                    g.splits, elems);
+                const unsigned grid = unsigned((elems / 4 + kReduceThreads - 1) / kReduceThreads);
+                const cudaError_t e = launch_kernel(grad_split_reduce_kernel<T>, dim3(grid), dim3(kReduceThreads), 0,
+                                                    s, true, static_cast<const float*>(g.acc),
+                                                    static_cast<T*>(grad_weight), g.splits, elems);
                 if (e != cudaSuccess)
                     return fail(err, err_len, TD_ERR_CUDA, "grad_split_reduce_kernel launch: %s",
                                 cudaGetErrorString(e));
@@ -1544,9 +1546,11 @@ int td_project_forward_peer(int dtype, const void* memory, const void* value_wei
                 return rc;
         }
         SampleArgs<T> a;
-        a.value = v; a.loc = static_cast<const T*>(sampling_locations); a.attn = static_cast<const T*>(attention_weights);
+        a.value = v; a.loc = static_cast<const T*>(sampling_locations);
+        a.attn = static_cast<const T*>(attention_weights);
         a.out = nullptr; a.shapes = spatial_shapes; a.starts = level_start_index; a.prod = ProducerIn<T>{};
-        a.rows = B * Q * H; a.s_img = H * N * D; a.s_tok = D; a.s_head = N * D; a.n_tok = N; a.mask = value_padding_mask;
+        a.rows = B * Q * H; a.s_img = H * N * D; a.s_tok = D; a.s_head = N * D; a.n_tok = N;
+        a.mask = value_padding_mask;
         a.Q = int(Q); a.H = int(H); a.D = int(D); a.L = int(L); a.P = int(P); a.G = int(G);
         const bool wide = row_bytes % 32 == 0 && row_bytes >= 128;
         if (wide) a.G = int(row_bytes / 32);
