@@ -44,6 +44,7 @@ sys.path.insert(0, ROOT)
 
 from marearts_tinydeform_b200 import (_native, choose_mode, deform_attn_layer, ma_deform_attn,  # noqa: E402
                                       ma_deform_attn_reference, sampling_producer_reference, workloads)
+from marearts_tinydeform_b200 import _pick_with_outproj  # noqa: E402
 
 L2_BYTES = 126 * 2 ** 20
 METRIC = 'µs per ma_deform_attn call (device-timed) and achieved HBM GB/s vs peak'
@@ -371,6 +372,8 @@ def run_ours(args):
         go = torch.Generator(device=dev).manual_seed(78)
         wo = ((torch.rand(C, H * D, generator=go, device=dev) * 2 - 1) * (6 / (C + H * D)) ** 0.5).to(W.dtype)
         bo = torch.zeros(C, dtype=W.dtype, device=dev)
+        if args.mode == 'auto':  # the order auto takes with output_proj
+            mode = _pick_with_outproj(base[0], W, Q, H, L, P, wo)
 
     def call(i):
         mem, loc, attn = pool[i % len(pool)]
@@ -600,7 +603,7 @@ def run_layer(args):
         if args.ref_dim == 4:
             ref[..., 2:] = 0.05 + 0.45 * ref[..., 2:]
         sets.append((q, ref.to(dtype), mem))
-    mode = args.mode if args.mode != 'auto' else choose_mode(base[0], W, base[5])
+    mode = args.mode if args.mode != 'auto' else _pick_with_outproj(base[0], W, Q, H, L, P, wo)
     kw = dict(output_weight=wo, output_bias=bo)
 
     def ours(i):
@@ -689,7 +692,7 @@ def run_layer_backward(args):
             ref[..., 2:] = 0.05 + 0.45 * ref[..., 2:]
         sets.append(tuple(t.requires_grad_(True) for t in (q, ref.to(dtype), mem.detach().clone())))
     gouts = [torch.randn(B, Q, C, generator=g, device=dev).to(dtype) for _ in range(4)]
-    mode = args.mode if args.mode != 'auto' else choose_mode(base[0], base[1], base[5])
+    mode = args.mode if args.mode != 'auto' else _pick_with_outproj(base[0], base[1], Q, H, L, P, params[4])
 
     def ours(i):
         q, ref, mem = sets[i % len(sets)]

@@ -82,6 +82,34 @@ def _pick(memory, value_weight, n_qry, n_head, n_lvl, n_pt, limits=None):
     return 'fused' if ratio < a + b / max(n_img, 1) else 'project'
 
 
+def _outproj_in_epilogue(memory, value_weight, n_qry, n_head, output_weight):
+    """Whether the project order would run output_proj in the sampler's cluster epilogue (td_set_output_proj_plan's
+    automatic plan; the conditions of sample_outproj_kernel's 16-bit form)."""
+    if output_weight is None or not memory.is_cuda or memory.dtype not in (torch.float16, torch.bfloat16):
+        return False
+    if _native.output_proj_plan() == _native.OUTPROJ_CHAINED:
+        return False
+    e = memory.element_size()
+    hd = value_weight.shape[0]
+    row = hd // n_head * e
+    if hd * e != 512 or 8 % n_head or output_weight.shape[0] > 256:
+        return False
+    if row % 16 or row > 512 or (row // 16) & (row // 16 - 1):
+        return False
+    sms = torch.cuda.get_device_properties(memory.device).multi_processor_count
+    return -(-memory.shape[0] * n_qry * n_head // 8) <= 3 * sms
+
+
+def _pick_with_outproj(memory, value_weight, n_qry, n_head, n_lvl, n_pt, output_weight):
+    """auto with output_proj: at batch 1, when the project order would fold output_proj into the sampler's
+    epilogue, the project order (measured on B200, float16, C_out = 256: 1 x 20 queries 8.2 against 8.9 us fused
+    + chained GEMM, 1 x 50 8.4 / 9.1, 1 x 100 8.7 / 9.5; at batch 2 and more the fused order with the chained GEMM
+    is faster, 2 x 100 11.1 / 12.7); otherwise the operator's own pick."""
+    if memory.shape[0] == 1 and _outproj_in_epilogue(memory, value_weight, n_qry, n_head, output_weight):
+        return 'project'
+    return _pick(memory, value_weight, n_qry, n_head, n_lvl, n_pt)
+
+
 def ma_deform_attn(memory, value_weight, value_bias, spatial_shapes, level_start_index,
                    sampling_locations, attention_weights, mode='auto', value_padding_mask=None,
                    output_weight=None, output_bias=None):
@@ -109,7 +137,8 @@ def ma_deform_attn(memory, value_weight, value_bias, spatial_shapes, level_start
         return out if output_weight is None else torch.nn.functional.linear(out, output_weight, output_bias)
     _native.load()  # raises RuntimeError when the native library is missing: there is no fallback
     if mode == 'auto':
-        mode = choose_mode(memory, value_weight, sampling_locations)
+        _, n_qry, n_head, n_lvl, n_pt, _ = sampling_locations.shape
+        mode = _pick_with_outproj(memory, value_weight, n_qry, n_head, n_lvl, n_pt, output_weight)
     if _wants_grad(memory, value_weight, value_bias, sampling_locations, attention_weights, output_weight,
                    output_bias):
         # training: the same forward kernels behind autograd Functions whose backward runs this library's
@@ -194,7 +223,8 @@ def deform_attn_layer(query, reference_points, memory, spatial_shapes, level_sta
                                            value_bias, output_weight, output_bias, value_padding_mask)
     _native.load()
     if mode == 'auto':
-        mode = _pick(memory, value_weight, query.shape[1], n_heads, spatial_shapes.shape[0], n_points)
+        mode = _pick_with_outproj(memory, value_weight, query.shape[1], n_heads, spatial_shapes.shape[0], n_points,
+                                  output_weight)
     if _wants_grad(query, reference_points, memory, sampling_weight, sampling_bias, value_weight, value_bias,
                    output_weight, output_bias):
         # training: the producer and the attention behind autograd Functions on this library's kernels

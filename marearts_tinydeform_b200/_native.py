@@ -628,13 +628,22 @@ def set_kernel_policy(policy):
 OUTPROJ_AUTO, OUTPROJ_CHAINED, OUTPROJ_CLUSTER = 0, 1, 2
 
 
+_outproj_plan = 0  # the plan last set through set_output_proj_plan (the library's default is automatic)
+
+
+def output_proj_plan():
+    return _outproj_plan
+
+
 def set_output_proj_plan(plan):
     """How the project order applies output_proj: OUTPROJ_AUTO (in the sampler's cluster kernel while its grid is one
     wave, B * Q * H / 8 <= 3 CTAs per SM; the default), OUTPROJ_CHAINED (a separate GEMM) or OUTPROJ_CLUSTER (the
     cluster kernel wherever its shape conditions hold); returns the previous plan."""
+    global _outproj_plan
     prev = load().td_set_output_proj_plan(plan)
     if prev < 0:
         raise ValueError(f'unknown output_proj plan {plan}')
+    _outproj_plan = plan
     return prev
 
 

@@ -156,3 +156,17 @@ def test_output_proj_plan_rejects_unknown_codes(cuda):
     with pytest.raises(ValueError):
         _native.set_output_proj_plan(7)
     assert _native.set_output_proj_plan(_native.OUTPROJ_AUTO) in (0, 1, 2)
+
+
+def test_auto_with_output_proj_prefers_the_epilogue_at_batch_one(cuda):
+    """'auto' with output_proj: at batch 1, where the project order folds output_proj into the sampler's epilogue,
+    it runs the project order (bit for bit); at batch 2 it keeps the operator's own pick."""
+    from marearts_tinydeform_b200 import choose_mode
+    for B, expect_project in ((1, True), (2, False)):
+        dev = to(make(B, 100, 8, 32, 256, [(20, 20), (10, 10)], 4, dtype=torch.float16, seed=70 + B), 'cuda')
+        wo, bo = [t.cuda() for t in _weights(256, 256, torch.float16, 71)]
+        with torch.inference_mode():
+            auto = ma_deform_attn(*dev, mode='auto', output_weight=wo, output_bias=bo)
+            want_mode = 'project' if expect_project else choose_mode(dev[0], dev[1], dev[5])
+            want = ma_deform_attn(*dev, mode=want_mode, output_weight=wo, output_bias=bo)
+        assert torch.equal(auto, want), f'B={B}: auto is not {want_mode}'
