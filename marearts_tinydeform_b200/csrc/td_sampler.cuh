@@ -104,19 +104,33 @@ __device__ __forceinline__ void sample_row_corners(const SampleArgs<T>& a, long 
     }
 }
 
+// Corner rows in flight per lane: 8 (kWide: 4), or 6 (3) with kShort -- the host takes whichever leaves fewer empty
+// slots for the row's S corners (48 corners over 8 lane groups fill 6 exactly: c1h 8.1 -> 7.8 us per call, c3 34.4 ->
+// 33.0; 64 corners fill 8).
+template <bool kWide, bool kShort>
+constexpr int sample_batch() { return kWide ? (kShort ? 3 : 4) : (kShort ? 6 : 8); }
+
+// Whether the shorter batch leaves fewer empty slots for S corners over 32 / G lane groups (host side).
+inline bool sample_short_batch(int S, int G, bool wide) {
+    const int cg = 32 / G;
+    const int lo = wide ? 3 : 6, hi = wide ? 4 : 8;
+    auto slots = [&](int b) { return (S + b * cg - 1) / (b * cg) * b * cg; };
+    return slots(lo) < slots(hi);
+}
+
 // The sum over the row's corners of weight * value[token] (head slice): G lanes per corner row, each loading
 // 16 bytes of it (kWide: 32 bytes, for rows of 128 bytes and more -- half the load instructions, which measured 16 %
 // faster on the stress shape's 128-byte rows and made no difference on 64-byte rows), kBatch corner rows in flight
 // per lane, the lanes' groups summed with an xor butterfly. On return every lane holds the finished sum of its
 // slice: head channels [(v * kWords + k) * V, + V) in acc[k * V ..], v = lane % G.
-template <typename T, bool kWide, bool kNoAlloc>
+template <typename T, bool kWide, bool kNoAlloc, bool kShort>
 __device__ __forceinline__ void sample_row_sum(const SampleArgs<T>& a, long long row, int lane, const int* s_tok,
                                                const typename Coord<T>::type* s_wt,
                                                typename Elem<T>::acc (&acc)[(kWide ? 2 : 1) * Elem<T>::kVec]) {
     using A = typename Elem<T>::acc;
     constexpr int V = Elem<T>::kVec;         // elements per 16-byte word
     constexpr int kWords = kWide ? 2 : 1;    // 16-byte words per lane and corner row
-    constexpr int kBatch = kWide ? 4 : 8;    // corner rows in flight per lane
+    constexpr int kBatch = sample_batch<kWide, kShort>();  // corner rows in flight per lane
     const int S = 4 * a.L * a.P;
     int h;
     long long b;
@@ -165,14 +179,14 @@ __device__ __forceinline__ void sample_row_sum(const SampleArgs<T>& a, long long
 }
 
 // out[row] = sample_row_sum, stored by the first corner group's lanes.
-template <typename T, bool kWide, bool kNoAlloc>
+template <typename T, bool kWide, bool kNoAlloc, bool kShort>
 __device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long long row, int lane, const int* s_tok,
                                                   const typename Coord<T>::type* s_wt) {
     using A = typename Elem<T>::acc;
     constexpr int V = Elem<T>::kVec;
     constexpr int kWords = kWide ? 2 : 1;
     A acc[kWords * V];
-    sample_row_sum<T, kWide, kNoAlloc>(a, row, lane, s_tok, s_wt, acc);
+    sample_row_sum<T, kWide, kNoAlloc, kShort>(a, row, lane, s_tok, s_wt, acc);
     if (lane < a.G) {
 #pragma unroll
         for (int k = 0; k < kWords; ++k) store16<T>(a.out + row * a.D + (lane * kWords + k) * V, acc + k * V);
@@ -191,7 +205,7 @@ __device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long l
 // all issued together) -> corners -> (every corner row of the lane's group issued together) -> butterfly -> store.
 // When launched with programmatic serialization right after the projection kernel, everything before
 // grid_dependency_wait() overlaps that kernel; value is only read after it.
-template <typename T, bool kWide, bool kNoAlloc>
+template <typename T, bool kWide, bool kNoAlloc, bool kShort>
 __global__ void __launch_bounds__(kSampleWarps * 32) sample_vec_kernel(const SampleArgs<T> a) {
     using CT = typename Coord<T>::type;
     // per warp: S corner tokens, then S corner weights (dynamic, sample_vec_smem bytes, so that the CTAs stay small
@@ -210,7 +224,7 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_vec_kernel(const Sam
     __syncwarp();
     grid_dependency_wait();
     if (!live) return;
-    sample_row_gather<T, kWide, kNoAlloc>(a, row, lane, s_tok, s_wt);
+    sample_row_gather<T, kWide, kNoAlloc, kShort>(a, row, lane, s_tok, s_wt);
 }
 
 // Generic kernel: lanes over the head's D channels, scalar loads.

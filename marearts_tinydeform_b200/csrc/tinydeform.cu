@@ -164,12 +164,18 @@ int launch_sampler(const T* value, long long s_img, long long s_tok, long long s
     const size_t smem = sample_vec_smem<T>(int(L), int(P));
     // corner loads without L1 allocation when the value is large against L2 (more than 64 MB)
     const bool no_alloc = vec && B * H * N * D * (long long)sizeof(T) > (64LL << 20);
-    cudaError_t e = wide       ? launch_kernel(sample_vec_kernel<T, true, true>, dim3(grid), dim3(kSampleWarps * 32),
-                                               smem, stream, after_producer, a)
-                    : no_alloc ? launch_kernel(sample_vec_kernel<T, false, true>, dim3(grid),
-                                               dim3(kSampleWarps * 32), smem, stream, after_producer, a)
-                    : vec      ? launch_kernel(sample_vec_kernel<T, false, false>, dim3(grid),
-                                               dim3(kSampleWarps * 32), smem, stream, after_producer, a)
+    // corner rows in flight per lane: the batch depth that leaves fewer empty slots for this row's corners
+    const bool sh = vec && sample_short_batch(int(4 * L * P), a.G, wide);
+    auto vec_launch = [&](auto k_long, auto k_short) {
+        return sh ? launch_kernel(k_short, dim3(grid), dim3(kSampleWarps * 32), smem, stream, after_producer, a)
+                  : launch_kernel(k_long, dim3(grid), dim3(kSampleWarps * 32), smem, stream, after_producer, a);
+    };
+    cudaError_t e = wide       ? vec_launch(sample_vec_kernel<T, true, true, false>,
+                                            sample_vec_kernel<T, true, true, true>)
+                    : no_alloc ? vec_launch(sample_vec_kernel<T, false, true, false>,
+                                            sample_vec_kernel<T, false, true, true>)
+                    : vec      ? vec_launch(sample_vec_kernel<T, false, false, false>,
+                                            sample_vec_kernel<T, false, false, true>)
                           : launch_kernel(sample_generic_kernel<T>, dim3(grid), dim3(kSampleWarps * 32), 0, stream,
                                           after_producer, a);
     if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "sampler launch: %s", cudaGetErrorString(e));
@@ -243,9 +249,16 @@ int launch_sample_outproj(const T* value, long long s_img, long long s_tok, long
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = after_producer ? 2 : 1;
-    const cudaError_t e = wide       ? cudaLaunchKernelEx(&cfg, sample_outproj_kernel<T, true, true, CS>, a, o)
-                          : no_alloc ? cudaLaunchKernelEx(&cfg, sample_outproj_kernel<T, false, true, CS>, a, o)
-                                     : cudaLaunchKernelEx(&cfg, sample_outproj_kernel<T, false, false, CS>, a, o);
+    const bool sh = sample_short_batch(int(4 * L * P), a.G, wide);
+    auto op_launch = [&](auto k_long, auto k_short) {
+        return sh ? cudaLaunchKernelEx(&cfg, k_short, a, o) : cudaLaunchKernelEx(&cfg, k_long, a, o);
+    };
+    const cudaError_t e = wide ? op_launch(sample_outproj_kernel<T, true, true, CS, false>,
+                                           sample_outproj_kernel<T, true, true, CS, true>)
+                          : no_alloc ? op_launch(sample_outproj_kernel<T, false, true, CS, false>,
+                                                 sample_outproj_kernel<T, false, true, CS, true>)
+                                     : op_launch(sample_outproj_kernel<T, false, false, CS, false>,
+                                                 sample_outproj_kernel<T, false, false, CS, true>);
     if (e != cudaSuccess)
         return fail(err, err_len, TD_ERR_CUDA, "sample_outproj_kernel launch: %s", cudaGetErrorString(e));
     g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -1565,12 +1578,17 @@ int td_project_forward_peer(int dtype, const void* memory, const void* value_wei
         if (a.rows > 0) {
             const unsigned grid = unsigned((a.rows + kSampleWarps - 1) / kSampleWarps);
             const size_t smem = sample_vec_smem<T>(int(L), int(P));
-            const cudaError_t ce = wide ? launch_kernel(sample_peer_kernel<T, true, true>, dim3(grid),
-                                                        dim3(kSampleWarps * 32), smem, s, project, a, po)
-                                   : no_alloc ? launch_kernel(sample_peer_kernel<T, false, true>, dim3(grid),
-                                                              dim3(kSampleWarps * 32), smem, s, project, a, po)
-                                              : launch_kernel(sample_peer_kernel<T, false, false>, dim3(grid),
-                                                              dim3(kSampleWarps * 32), smem, s, project, a, po);
+            const bool sh = sample_short_batch(int(4 * L * P), a.G, wide);
+            auto peer_launch = [&](auto k_long, auto k_short) {
+                return sh ? launch_kernel(k_short, dim3(grid), dim3(kSampleWarps * 32), smem, s, project, a, po)
+                          : launch_kernel(k_long, dim3(grid), dim3(kSampleWarps * 32), smem, s, project, a, po);
+            };
+            const cudaError_t ce = wide ? peer_launch(sample_peer_kernel<T, true, true, false>,
+                                                      sample_peer_kernel<T, true, true, true>)
+                                   : no_alloc ? peer_launch(sample_peer_kernel<T, false, true, false>,
+                                                            sample_peer_kernel<T, false, true, true>)
+                                              : peer_launch(sample_peer_kernel<T, false, false, false>,
+                                                            sample_peer_kernel<T, false, false, true>);
             if (ce != cudaSuccess)
                 return fail(err, err_len, TD_ERR_CUDA, "sample_peer_kernel launch: %s", cudaGetErrorString(ce));
             g_launches.fetch_add(1, std::memory_order_relaxed);
