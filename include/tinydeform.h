@@ -272,10 +272,12 @@ TD_API int td_project_forward_noalloc(int dtype, const void* memory, const void*
  *                          column sums of grad_out) when grad_bias is not NULL. Outputs in the input dtype.
  * In the operator's backward x is memory, weight value_weight and grad_out the gradient of the projected value.
  * float16 / bfloat16 run on tcgen05 tensor cores (float32 accumulation) when every row is 16-byte aligned
- * (Nout, K multiples of 8); float32 / float64 and other shapes on CUDA cores. The weight gradient splits the M rows
- * over CTAs and adds float32 partial sums atomically, so its last bits may vary between runs.
- * td_linear_grad_weight needs td_linear_grad_workspace_bytes(dtype, Nout, K) bytes of workspace (0 for float32 and
- * float64, whose sums accumulate in the outputs themselves).
+ * (Nout, K multiples of 8); float32 / float64 and other shapes on CUDA cores. On the tensor cores the weight
+ * gradient splits the M rows over CTAs, each storing its float32 partial tile, and a second kernel sums the partials
+ * in a fixed order (bitwise reproducible); the bias gradient's column sums and the CUDA-core weight gradient add
+ * partial sums atomically, so their last bits may vary between runs.
+ * td_linear_grad_weight needs td_linear_grad_workspace_bytes(dtype, Nout, K) bytes of workspace (the split partials,
+ * at most 256 x 64 KB; 0 for float32 and float64, whose sums accumulate in the outputs themselves).
  */
 TD_API size_t td_linear_grad_workspace_bytes(int dtype, int64_t Nout, int64_t K);
 TD_API int td_linear_grad_input(int dtype, const void* grad_out, const void* weight, void* grad_input, int64_t M,

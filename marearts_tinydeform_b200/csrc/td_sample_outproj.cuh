@@ -3,21 +3,21 @@
 //
 // The attention half is sample_vec_kernel's (one warp per (batch, query, head) row, corners before the grid
 // dependency wait, one L2 round trip for the row's corner rows). What a chained output_proj costs at batch 1 is a
-// kernel boundary and a second grid, not arithmetic (300 x 256 x 256 at the RT-DETR shape). A CTA here holds
-// whole queries (kSampleWarps rows = kSampleWarps / H queries), and its cluster of kOpCluster CTAs splits the output
-// columns: after the gather every CTA writes its queries' attention rows (rounded to T, as the operator returns them)
-// into its shared memory, the cluster synchronises, and each CTA reads all the cluster's rows over distributed
-// shared memory and computes its C_out / kOpCluster columns for every query of the cluster. Each CTA thus reads
-// 1 / kOpCluster of Wo (16 KB at C_out = HD = 256, float16), where a CTA computing every column of its own queries
-// would read all 128 KB of it -- the cost that sank a per-CTA epilogue (39 MB of L2 reads at c1h).
-// The product per CTA is kOpCluster queries x 32 columns x HD: 256 multiply-adds per thread (a lane owns one
-// 16-byte chunk of K), in passes of 16 partial sums per lane that a reduce-scatter over the warp (16 shuffles) turns
-// into finished outputs. At 8 queries per cluster no tensor-core tile would be filled (tcgen05 tiles are 64 or 128
-// rows), so the product is on CUDA cores. The kernel keeps to 64 registers (four CTAs per SM, two of them beside a
-// running projection CTA, as sample_vec_kernel).
+// kernel boundary and a second grid, not arithmetic (300 x 256 x 256 at the RT-DETR shape). A CTA here holds whole
+// queries (kSampleWarps rows = kSampleWarps / H queries), and its cluster of CS = 8 CTAs splits the output columns:
+// after the gather every CTA writes its queries' attention rows (rounded to T, as the operator returns them) into
+// its shared memory, the cluster synchronises, each CTA copies the cluster's rows of one query slot out of its peers'
+// shared memory (distributed shared memory, one 16-byte load per lane: each row crosses the cluster once) and
+// computes its C_out / CS output columns for the slot's CS queries. Each CTA thus reads 1 / CS of Wo (16 KB at
+// C_out = HD = 256 in 16-bit types), where a CTA computing every column of its own queries would read all 128 KB of
+// it -- the cost that sank a per-CTA epilogue (39 MB of L2 reads at c1h).
+// The product: 16-bit types as warp-level tensor-core tiles (mma.sync m16n8k16, float32 accumulation; the slot's
+// queries are A's rows, a warp takes an 8-column tile); float32 / float64 on CUDA cores (a lane per 16-byte chunk of
+// K, a reduce-scatter over the warp). At 8 queries per cluster a 64- or 128-row tcgen05 tile would be mostly padding.
+// The kernel keeps to 64 registers, so two of its CTAs still become resident beside a running projection CTA.
 // Requirements (the host checks them, else output_proj is chained): kSampleWarps % H == 0; HD * sizeof(T) = 512
-// (one 16-byte vector of K per lane: H * D = 256 in 16-bit types, 128 in float32); C_out <= kOpCluster *
-// kSampleWarps * kOpColsPerWarp = 256; the sampler's vector-kernel conditions; Wo 16-byte aligned.
+// (one 16-byte vector of K per lane: H * D = 256 in 16-bit types, 128 in float32); C_out <= 256; the sampler's
+// vector-kernel conditions; Wo 16-byte aligned.
 #pragma once
 
 #include <type_traits>
@@ -26,9 +26,8 @@
 
 namespace td {
 
-constexpr int kOpCluster = 8;      // CTAs per cluster on the CUDA-core path (the portable maximum)
-constexpr int kOpClusterMma = 8;   // CTAs per cluster on the tensor-core path (16-bit types)
-constexpr int kOpColsPerWarp = 4;  // output columns per warp and query pass: 4 x 8 queries = 32 partials per lane
+constexpr int kOpCluster = 8;      // CTAs per cluster (the portable maximum; clusters of 4 and 16 measured slower)
+constexpr int kOpColsPerWarp = 4;  // CUDA-core path: output columns per warp and query pass
 
 template <typename T>
 struct OutProjArgs {

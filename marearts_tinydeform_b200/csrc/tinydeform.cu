@@ -228,9 +228,9 @@ int launch_sample_outproj(const T* value, long long s_img, long long s_tok, long
     const bool no_alloc = B * H * N * D * (long long)sizeof(T) > (64LL << 20);
     OutProjArgs<T> o;
     o.weight = out_w; o.bias = out_b; o.out = y; o.queries = B * Q; o.C_out = int(C_out); o.HD = int(HD);
-    // cluster size: 8 CTAs (each computes C_out / 8 output columns; clusters of 4 measured slower: twice the weight
-    // loads per CTA)
-    constexpr int CS = sizeof(T) == 2 ? kOpClusterMma : kOpCluster;
+    // clusters of 8 CTAs, each computing C_out / 8 output columns (clusters of 4 measured slower: twice the weight
+    // loads per CTA; of 16, slower from two images on)
+    constexpr int CS = kOpCluster;
     o.cols = int((C_out + CS - 1) / CS);
     const long long ctas = (B * Q * H + kSampleWarps - 1) / kSampleWarps;
     const unsigned grid = unsigned((ctas + CS - 1) / CS * CS);
