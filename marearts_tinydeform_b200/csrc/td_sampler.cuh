@@ -205,8 +205,12 @@ __device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long l
 // all issued together) -> corners -> (every corner row of the lane's group issued together) -> butterfly -> store.
 // When launched with programmatic serialization right after the projection kernel, everything before
 // grid_dependency_wait() overlaps that kernel; value is only read after it.
+// Registers: the 6-deep 16-byte form of the 16- and 32-bit types is held to 48 (five CTAs an SM: c3 33.0 -> 31.5 us
+// per call, c1h unchanged, no spills), the other 16- and 32-bit forms to 64 (four CTAs an SM; held to 48 the 8-deep
+// form spills, c4 92.5 -> 120 us, and so do the 32-byte forms), float64 to 85 (three CTAs an SM, no spills).
 template <typename T, bool kWide, bool kNoAlloc, bool kShort>
-__global__ void __launch_bounds__(kSampleWarps * 32) sample_vec_kernel(const SampleArgs<T> a) {
+__global__ void __launch_bounds__(kSampleWarps * 32, (kShort && !kWide && sizeof(T) < 8) ? 5 : (sizeof(T) == 8 ? 3 : 4))
+    sample_vec_kernel(const SampleArgs<T> a) {
     using CT = typename Coord<T>::type;
     // per warp: S corner tokens, then S corner weights (dynamic, sample_vec_smem bytes, so that the CTAs stay small
     // enough to become resident beside a running projection kernel)
