@@ -42,7 +42,7 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 }
 
 // sample_vec_kernel's rows, each stored into all `world` copies of the gathered output.
-template <typename T, bool kWide, bool kNoAlloc, bool kShort>
+template <typename T, bool kWide, bool kNoAlloc, int kBatch>
 __global__ void __launch_bounds__(kSampleWarps * 32) sample_peer_kernel(const SampleArgs<T> a, const PeerOut<T> p) {
     using A = typename Elem<T>::acc;
     using CT = typename Coord<T>::type;
@@ -63,7 +63,7 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_peer_kernel(const Sa
     grid_dependency_wait();
     if (!live) return;
     A acc[kWords * V];
-    sample_row_sum<T, kWide, kNoAlloc, kShort>(a, row, lane, s_tok, s_wt, acc);
+    sample_row_sum<T, kWide, kNoAlloc, kBatch>(a, row, lane, s_tok, s_wt, acc);
     if (lane < a.G) {
         const long long at = (p.row0 + row) * a.D + (lane * kWords) * V;
         for (int r = 0; r < p.world; ++r) {

@@ -71,7 +71,7 @@ __device__ __forceinline__ void mma_m16n8k16(float (&d)[4], uint32_t a0, uint32_
     }
 }
 
-template <typename T, bool kWide, bool kNoAlloc, int CS, bool kShort>
+template <typename T, bool kWide, bool kNoAlloc, int CS, int kBatch>
 __global__ void __launch_bounds__(kSampleWarps * 32) sample_outproj_kernel(const SampleArgs<T> a,
                                                                            const OutProjArgs<T> o) {
     using A = typename Elem<T>::acc;
@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_outproj_kernel(const
     {
         A acc[kWords * V];
         if (live) {
-            sample_row_sum<T, kWide, kNoAlloc, kShort>(a, row, lane, s_tok, s_wt, acc);
+            sample_row_sum<T, kWide, kNoAlloc, kBatch>(a, row, lane, s_tok, s_wt, acc);
         } else {
 #pragma unroll
             for (int i = 0; i < kWords * V; ++i) acc[i] = A(0);

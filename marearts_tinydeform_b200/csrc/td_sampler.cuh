@@ -104,18 +104,27 @@ __device__ __forceinline__ void sample_row_corners(const SampleArgs<T>& a, long 
     }
 }
 
-// Corner rows in flight per lane: 8 (kWide: 4), or 6 (3) with kShort -- the host takes whichever leaves fewer empty
-// slots for the row's S corners (48 corners over 8 lane groups fill 6 exactly: c1h 8.1 -> 7.8 us per call, c3 34.4 ->
-// 33.0; 64 corners fill 8).
-template <bool kWide, bool kShort>
-constexpr int sample_batch() { return kWide ? (kShort ? 3 : 4) : (kShort ? 6 : 8); }
-
-// Whether the shorter batch leaves fewer empty slots for S corners over 32 / G lane groups (host side).
-inline bool sample_short_batch(int S, int G, bool wide) {
-    const int cg = 32 / G;
-    const int lo = wide ? 3 : 6, hi = wide ? 4 : 8;
-    auto slots = [&](int b) { return (S + b * cg - 1) / (b * cg) * b * cg; };
-    return slots(lo) < slots(hi);
+// Corner rows in flight per lane (kBatch): a row's S = 4 L P corners are split over 32 / G lane groups, each lane
+// loading kBatch of its group's corners at once, in ceil(S / (kBatch * groups)) passes. In one wave of CTAs (every
+// row resident at once, latency-bound) the fewest passes win: 48 corners over 8 groups in one pass of 6 (c1h 8.40 ->
+// 7.99 us per call, against 8 slots of which a quarter fetched a zero row); 64 corners in two passes of 4 (as fast as
+// one pass of 8 at DINO batch 1, 14.3 us). Over several waves (throughput-bound) the fewest empty slots at the
+// smallest depth win, as smaller batches need fewer registers and so more resident CTAs: 48 corners in two passes of
+// 3 (c3 31.5 -> 30.5 us), 64 in two of 4 (c4 93.4 -> 84.2 us, against one pass of 8 at 64 registers). The 32-byte
+// forms (rows of 128 bytes and more) take 3 or 4, whichever leaves fewer empty slots.
+inline int sample_batch_depth(int S, int G, bool wide, long long rows, int sm_count) {
+    const int groups = 32 / G;
+    auto passes = [&](int b) { return (S + b * groups - 1) / (b * groups); };
+    auto slots = [&](int b) { return passes(b) * b * groups; };
+    if (wide) return slots(3) < slots(4) ? 3 : 4;
+    const long long wave_rows = (long long)sm_count * 5 * 8;  // five CTAs of eight rows on every SM
+    if (rows <= wave_rows) {
+        int best = 6;
+        for (int b : {4, 3})
+            if (passes(b) < passes(best) || (passes(b) == passes(best) && slots(b) < slots(best))) best = b;
+        return best;
+    }
+    return slots(3) < slots(4) ? 3 : 4;
 }
 
 // The sum over the row's corners of weight * value[token] (head slice): G lanes per corner row, each loading
@@ -123,14 +132,13 @@ inline bool sample_short_batch(int S, int G, bool wide) {
 // faster on the stress shape's 128-byte rows and made no difference on 64-byte rows), kBatch corner rows in flight
 // per lane, the lanes' groups summed with an xor butterfly. On return every lane holds the finished sum of its
 // slice: head channels [(v * kWords + k) * V, + V) in acc[k * V ..], v = lane % G.
-template <typename T, bool kWide, bool kNoAlloc, bool kShort>
+template <typename T, bool kWide, bool kNoAlloc, int kBatch>
 __device__ __forceinline__ void sample_row_sum(const SampleArgs<T>& a, long long row, int lane, const int* s_tok,
                                                const typename Coord<T>::type* s_wt,
                                                typename Elem<T>::acc (&acc)[(kWide ? 2 : 1) * Elem<T>::kVec]) {
     using A = typename Elem<T>::acc;
     constexpr int V = Elem<T>::kVec;         // elements per 16-byte word
     constexpr int kWords = kWide ? 2 : 1;    // 16-byte words per lane and corner row
-    constexpr int kBatch = sample_batch<kWide, kShort>();  // corner rows in flight per lane
     const int S = 4 * a.L * a.P;
     int h;
     long long b;
@@ -179,14 +187,14 @@ __device__ __forceinline__ void sample_row_sum(const SampleArgs<T>& a, long long
 }
 
 // out[row] = sample_row_sum, stored by the first corner group's lanes.
-template <typename T, bool kWide, bool kNoAlloc, bool kShort>
+template <typename T, bool kWide, bool kNoAlloc, int kBatch>
 __device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long long row, int lane, const int* s_tok,
                                                   const typename Coord<T>::type* s_wt) {
     using A = typename Elem<T>::acc;
     constexpr int V = Elem<T>::kVec;
     constexpr int kWords = kWide ? 2 : 1;
     A acc[kWords * V];
-    sample_row_sum<T, kWide, kNoAlloc, kShort>(a, row, lane, s_tok, s_wt, acc);
+    sample_row_sum<T, kWide, kNoAlloc, kBatch>(a, row, lane, s_tok, s_wt, acc);
     if (lane < a.G) {
 #pragma unroll
         for (int k = 0; k < kWords; ++k) store16<T>(a.out + row * a.D + (lane * kWords + k) * V, acc + k * V);
@@ -205,11 +213,10 @@ __device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long l
 // all issued together) -> corners -> (every corner row of the lane's group issued together) -> butterfly -> store.
 // When launched with programmatic serialization right after the projection kernel, everything before
 // grid_dependency_wait() overlaps that kernel; value is only read after it.
-// Registers: the 6-deep 16-byte form of the 16- and 32-bit types is held to 48 (five CTAs an SM: c3 33.0 -> 31.5 us
-// per call, c1h unchanged, no spills), the other 16- and 32-bit forms to 64 (four CTAs an SM; held to 48 the 8-deep
-// form spills, c4 92.5 -> 120 us, and so do the 32-byte forms), float64 to 85 (three CTAs an SM, no spills).
-template <typename T, bool kWide, bool kNoAlloc, bool kShort>
-__global__ void __launch_bounds__(kSampleWarps * 32, (kShort && !kWide && sizeof(T) < 8) ? 5 : (sizeof(T) == 8 ? 3 : 4))
+// Registers: the 16-byte forms of the 16- and 32-bit types are held to 48 (five CTAs an SM; no spills at any
+// depth), the 32-byte forms to 64 (four CTAs; held to 48 they spill), float64 to 85 (three CTAs, no spills).
+template <typename T, bool kWide, bool kNoAlloc, int kBatch>
+__global__ void __launch_bounds__(kSampleWarps * 32, (!kWide && sizeof(T) < 8) ? 5 : (sizeof(T) == 8 ? 3 : 4))
     sample_vec_kernel(const SampleArgs<T> a) {
     using CT = typename Coord<T>::type;
     // per warp: S corner tokens, then S corner weights (dynamic, sample_vec_smem bytes, so that the CTAs stay small
@@ -228,7 +235,7 @@ __global__ void __launch_bounds__(kSampleWarps * 32, (kShort && !kWide && sizeof
     __syncwarp();
     grid_dependency_wait();
     if (!live) return;
-    sample_row_gather<T, kWide, kNoAlloc, kShort>(a, row, lane, s_tok, s_wt);
+    sample_row_gather<T, kWide, kNoAlloc, kBatch>(a, row, lane, s_tok, s_wt);
 }
 
 // Generic kernel: lanes over the head's D channels, scalar loads.

@@ -164,18 +164,24 @@ int launch_sampler(const T* value, long long s_img, long long s_tok, long long s
     const size_t smem = sample_vec_smem<T>(int(L), int(P));
     // corner loads without L1 allocation when the value is large against L2 (more than 64 MB)
     const bool no_alloc = vec && B * H * N * D * (long long)sizeof(T) > (64LL << 20);
-    // corner rows in flight per lane: the batch depth that leaves fewer empty slots for this row's corners
-    const bool sh = vec && sample_short_batch(int(4 * L * P), a.G, wide);
-    auto vec_launch = [&](auto k_long, auto k_short) {
-        return sh ? launch_kernel(k_short, dim3(grid), dim3(kSampleWarps * 32), smem, stream, after_producer, a)
-                  : launch_kernel(k_long, dim3(grid), dim3(kSampleWarps * 32), smem, stream, after_producer, a);
+    // corner rows in flight per lane (sample_batch_depth)
+    int depth = 4;
+    if (vec) {
+        DeviceFacts f;
+        if (int rc = device_facts(&f, err, err_len)) return rc;
+        depth = sample_batch_depth(int(4 * L * P), a.G, wide, a.rows, f.sm_count);
+    }
+    auto vec_launch = [&](auto k_wide, auto k_noalloc) -> cudaError_t {
+        constexpr bool W = decltype(k_wide)::value, NA = decltype(k_noalloc)::value;
+        const dim3 g(grid), blk(kSampleWarps * 32);
+        if (depth == 3) return launch_kernel(sample_vec_kernel<T, W, NA, 3>, g, blk, smem, stream, after_producer, a);
+        if (depth == 4) return launch_kernel(sample_vec_kernel<T, W, NA, 4>, g, blk, smem, stream, after_producer, a);
+        if constexpr (!W) return launch_kernel(sample_vec_kernel<T, W, NA, 6>, g, blk, smem, stream, after_producer, a);
+        return cudaErrorInvalidValue;
     };
-    cudaError_t e = wide       ? vec_launch(sample_vec_kernel<T, true, true, false>,
-                                            sample_vec_kernel<T, true, true, true>)
-                    : no_alloc ? vec_launch(sample_vec_kernel<T, false, true, false>,
-                                            sample_vec_kernel<T, false, true, true>)
-                    : vec      ? vec_launch(sample_vec_kernel<T, false, false, false>,
-                                            sample_vec_kernel<T, false, false, true>)
+    cudaError_t e = wide       ? vec_launch(std::true_type{}, std::true_type{})
+                    : no_alloc ? vec_launch(std::false_type{}, std::true_type{})
+                    : vec      ? vec_launch(std::false_type{}, std::false_type{})
                           : launch_kernel(sample_generic_kernel<T>, dim3(grid), dim3(kSampleWarps * 32), 0, stream,
                                           after_producer, a);
     if (e != cudaSuccess) return fail(err, err_len, TD_ERR_CUDA, "sampler launch: %s", cudaGetErrorString(e));
@@ -249,16 +255,19 @@ int launch_sample_outproj(const T* value, long long s_img, long long s_tok, long
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = after_producer ? 2 : 1;
-    const bool sh = sample_short_batch(int(4 * L * P), a.G, wide);
-    auto op_launch = [&](auto k_long, auto k_short) {
-        return sh ? cudaLaunchKernelEx(&cfg, k_short, a, o) : cudaLaunchKernelEx(&cfg, k_long, a, o);
+    DeviceFacts f;
+    if (int rc = device_facts(&f, err, err_len)) return rc;
+    const int depth = sample_batch_depth(int(4 * L * P), a.G, wide, a.rows, f.sm_count);
+    auto op_launch = [&](auto k_wide, auto k_noalloc) -> cudaError_t {
+        constexpr bool W = decltype(k_wide)::value, NA = decltype(k_noalloc)::value;
+        if (depth == 3) return cudaLaunchKernelEx(&cfg, sample_outproj_kernel<T, W, NA, CS, 3>, a, o);
+        if (depth == 4) return cudaLaunchKernelEx(&cfg, sample_outproj_kernel<T, W, NA, CS, 4>, a, o);
+        if constexpr (!W) return cudaLaunchKernelEx(&cfg, sample_outproj_kernel<T, W, NA, CS, 6>, a, o);
+        return cudaErrorInvalidValue;
     };
-    const cudaError_t e = wide ? op_launch(sample_outproj_kernel<T, true, true, CS, false>,
-                                           sample_outproj_kernel<T, true, true, CS, true>)
-                          : no_alloc ? op_launch(sample_outproj_kernel<T, false, true, CS, false>,
-                                                 sample_outproj_kernel<T, false, true, CS, true>)
-                                     : op_launch(sample_outproj_kernel<T, false, false, CS, false>,
-                                                 sample_outproj_kernel<T, false, false, CS, true>);
+    const cudaError_t e = wide       ? op_launch(std::true_type{}, std::true_type{})
+                          : no_alloc ? op_launch(std::false_type{}, std::true_type{})
+                                     : op_launch(std::false_type{}, std::false_type{});
     if (e != cudaSuccess)
         return fail(err, err_len, TD_ERR_CUDA, "sample_outproj_kernel launch: %s", cudaGetErrorString(e));
     g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -1578,17 +1587,21 @@ int td_project_forward_peer(int dtype, const void* memory, const void* value_wei
         if (a.rows > 0) {
             const unsigned grid = unsigned((a.rows + kSampleWarps - 1) / kSampleWarps);
             const size_t smem = sample_vec_smem<T>(int(L), int(P));
-            const bool sh = sample_short_batch(int(4 * L * P), a.G, wide);
-            auto peer_launch = [&](auto k_long, auto k_short) {
-                return sh ? launch_kernel(k_short, dim3(grid), dim3(kSampleWarps * 32), smem, s, project, a, po)
-                          : launch_kernel(k_long, dim3(grid), dim3(kSampleWarps * 32), smem, s, project, a, po);
+            DeviceFacts f;
+            if (int rc = device_facts(&f, err, err_len)) return rc;
+            const int depth = sample_batch_depth(int(4 * L * P), a.G, wide, a.rows, f.sm_count);
+            auto peer_launch = [&](auto k_wide, auto k_noalloc) -> cudaError_t {
+                constexpr bool W = decltype(k_wide)::value, NA = decltype(k_noalloc)::value;
+                const dim3 g(grid), blk(kSampleWarps * 32);
+                if (depth == 3) return launch_kernel(sample_peer_kernel<T, W, NA, 3>, g, blk, smem, s, project, a, po);
+                if (depth == 4) return launch_kernel(sample_peer_kernel<T, W, NA, 4>, g, blk, smem, s, project, a, po);
+                if constexpr (!W)
+                    return launch_kernel(sample_peer_kernel<T, W, NA, 6>, g, blk, smem, s, project, a, po);
+                return cudaErrorInvalidValue;
             };
-            const cudaError_t ce = wide ? peer_launch(sample_peer_kernel<T, true, true, false>,
-                                                      sample_peer_kernel<T, true, true, true>)
-                                   : no_alloc ? peer_launch(sample_peer_kernel<T, false, true, false>,
-                                                            sample_peer_kernel<T, false, true, true>)
-                                              : peer_launch(sample_peer_kernel<T, false, false, false>,
-                                                            sample_peer_kernel<T, false, false, true>);
+            const cudaError_t ce = wide       ? peer_launch(std::true_type{}, std::true_type{})
+                                   : no_alloc ? peer_launch(std::false_type{}, std::true_type{})
+                                              : peer_launch(std::false_type{}, std::false_type{});
             if (ce != cudaSuccess)
                 return fail(err, err_len, TD_ERR_CUDA, "sample_peer_kernel launch: %s", cudaGetErrorString(ce));
             g_launches.fetch_add(1, std::memory_order_relaxed);
