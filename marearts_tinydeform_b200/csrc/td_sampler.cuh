@@ -112,8 +112,8 @@ __device__ __forceinline__ void sample_row_corners(const SampleArgs<T>& a, long 
 // smallest depth win, as smaller batches need fewer registers and so more resident CTAs: 48 corners in two passes of
 // 3 (c3 31.5 -> 30.5 us), 64 in two of 4 (c4 93.4 -> 84.2 us, against one pass of 8 at 64 registers). The 32-byte
 // forms (rows of 128 bytes and more) take 3 or 4, whichever leaves fewer empty slots.
-inline int sample_batch_depth(int S, int G, bool wide, long long rows, int sm_count) {
-    const int groups = 32 / G;
+inline int sample_batch_depth(int S, int G, bool wide, long long rows, int sm_count, int lanes = 32) {
+    const int groups = lanes / G;
     auto passes = [&](int b) { return (S + b * groups - 1) / (b * groups); };
     auto slots = [&](int b) { return passes(b) * b * groups; };
     if (wide) return slots(3) < slots(4) ? 3 : 4;
@@ -130,9 +130,10 @@ inline int sample_batch_depth(int S, int G, bool wide, long long rows, int sm_co
 // The sum over the row's corners of weight * value[token] (head slice): G lanes per corner row, each loading
 // 16 bytes of it (kWide: 32 bytes, for rows of 128 bytes and more -- half the load instructions, which measured 16 %
 // faster on the stress shape's 128-byte rows and made no difference on 64-byte rows), kBatch corner rows in flight
-// per lane, the lanes' groups summed with an xor butterfly. On return every lane holds the finished sum of its
+// per lane, the lanes' groups summed with an xor butterfly. The row takes kLanes lanes (32, or 16 when a warp holds
+// two rows; lane is then the index within the row's half). On return every lane holds the finished sum of its
 // slice: head channels [(v * kWords + k) * V, + V) in acc[k * V ..], v = lane % G.
-template <typename T, bool kWide, bool kNoAlloc, int kBatch>
+template <typename T, bool kWide, bool kNoAlloc, int kBatch, int kLanes = 32>
 __device__ __forceinline__ void sample_row_sum(const SampleArgs<T>& a, long long row, int lane, const int* s_tok,
                                                const typename Coord<T>::type* s_wt,
                                                typename Elem<T>::acc (&acc)[(kWide ? 2 : 1) * Elem<T>::kVec]) {
@@ -151,7 +152,7 @@ __device__ __forceinline__ void sample_row_sum(const SampleArgs<T>& a, long long
         b = row / ((long long)a.Q * a.H);
     }
     const T* vb = a.value + b * a.s_img + (long long)h * a.s_head;
-    const int G = a.G, CG = 32 / G, cg = lane / G, v = lane - cg * G;
+    const int G = a.G, CG = kLanes / G, cg = lane / G, v = lane - cg * G;
 #pragma unroll
     for (int i = 0; i < kWords * V; ++i) acc[i] = A(0);
     for (int s0 = cg; s0 < S; s0 += kBatch * CG) {
@@ -180,7 +181,7 @@ __device__ __forceinline__ void sample_row_sum(const SampleArgs<T>& a, long long
             }
         }
     }
-    for (int o = G; o < 32; o <<= 1) {
+    for (int o = G; o < kLanes; o <<= 1) {
 #pragma unroll
         for (int i = 0; i < kWords * V; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
     }
@@ -215,27 +216,78 @@ __device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long l
 // grid_dependency_wait() overlaps that kernel; value is only read after it.
 // Registers: the 16-byte forms of the 16- and 32-bit types are held to 48 (five CTAs an SM; no spills at any
 // depth), the 32-byte forms to 64 (four CTAs; held to 48 they spill), float64 to 85 (three CTAs, no spills).
-template <typename T, bool kWide, bool kNoAlloc, int kBatch>
+// The corners of a warp's two rows in one pass (kRW = 2): 16 lanes a row, a lane per sampling point (L * P <= 16,
+// locations and weights read from the tensors); a row past the last one samples nothing. The corner prologue is most
+// of a row's instructions (level geometry, locations, clamps, four tokens and their bounds tests): a pass per row
+// keeps only 12 of 32 lanes busy at the RT-DETR shapes' 12 points, this one 24.
+template <typename T>
+__device__ __forceinline__ void sample_pair_corners(const SampleArgs<T>& a, long long row0, int lane, int* s_tok,
+                                                    typename Coord<T>::type* s_wt) {
+    using CT = typename Coord<T>::type;
+    const int LP = a.L * a.P, S = 4 * LP;
+    const int r = lane >> 4, j = lane & 15;
+    const long long row = row0 + r;
+    if (j >= LP) return;
+    int* tk = s_tok + r * S + 4 * j;
+    CT* wt = s_wt + r * S + 4 * j;
+    if (row < a.rows) {
+        const Level lv = level_at(a.shapes, a.starts, j / a.P);
+        const uint8_t* mask_b = a.mask != nullptr ? a.mask + row / ((long long)a.Q * a.H) * a.n_tok : nullptr;
+        const long long i = row * LP + j;
+        corners4<CT>(CT(to_acc(a.loc[2 * i])), CT(to_acc(a.loc[2 * i + 1])), CT(to_acc(a.attn[i])), lv, a.n_tok, tk,
+                     wt, mask_b);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            tk[k] = -1;
+            wt[k] = CT(0);
+        }
+    }
+}
+
+// kRW rows per warp: 1, or 2 over several waves of CTAs (throughput-bound) when the rows' points fit 16 lanes and
+// come from the tensors -- the corner prologue in one pass for both rows, and each row's corner groups in one half
+// of the warp (c3 30.6 -> 27.1 us per call, c4 83.4 -> 72.7 us on B200).
+template <typename T, bool kWide, bool kNoAlloc, int kBatch, int kRW = 1>
 __global__ void __launch_bounds__(kSampleWarps * 32, (!kWide && sizeof(T) < 8) ? 5 : (sizeof(T) == 8 ? 3 : 4))
     sample_vec_kernel(const SampleArgs<T> a) {
+    using A = typename Elem<T>::acc;
     using CT = typename Coord<T>::type;
-    // per warp: S corner tokens, then S corner weights (dynamic, sample_vec_smem bytes, so that the CTAs stay small
-    // enough to become resident beside a running projection kernel)
+    constexpr int V = Elem<T>::kVec;
+    constexpr int kWords = kWide ? 2 : 1;
+    // per warp: kRW x S corner tokens, then kRW x S corner weights (dynamic, kRW x sample_vec_smem bytes, so that
+    // the CTAs stay small enough to become resident beside a running projection kernel)
     extern __shared__ __align__(16) unsigned char smem_raw[];
 
     // the next call's projection may be scheduled now; it waits for this grid before touching memory
     launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long row = (long long)blockIdx.x * kSampleWarps + warp;
-    const bool live = row < a.rows;  // dead warps still reach grid_dependency_wait
     const int S = 4 * a.L * a.P;
-    int* s_tok = reinterpret_cast<int*>(smem_raw) + warp * S;
-    CT* s_wt = reinterpret_cast<CT*>(smem_raw + kSampleWarps * S * sizeof(int)) + warp * S;
-    if (live) sample_row_corners<T>(a, row, lane, s_tok, s_wt);
-    __syncwarp();
-    grid_dependency_wait();
-    if (!live) return;
-    sample_row_gather<T, kWide, kNoAlloc, kBatch>(a, row, lane, s_tok, s_wt);
+    int* s_tok = reinterpret_cast<int*>(smem_raw) + warp * kRW * S;
+    CT* s_wt = reinterpret_cast<CT*>(smem_raw + kSampleWarps * kRW * S * sizeof(int)) + warp * kRW * S;
+    if constexpr (kRW == 1) {
+        const long long row = (long long)blockIdx.x * kSampleWarps + warp;
+        const bool live = row < a.rows;  // dead warps still reach grid_dependency_wait
+        if (live) sample_row_corners<T>(a, row, lane, s_tok, s_wt);
+        __syncwarp();
+        grid_dependency_wait();
+        if (!live) return;
+        sample_row_gather<T, kWide, kNoAlloc, kBatch>(a, row, lane, s_tok, s_wt);
+    } else {
+        static_assert(kRW == 2, "one or two rows a warp");
+        const long long row0 = ((long long)blockIdx.x * kSampleWarps + warp) * 2;
+        sample_pair_corners<T>(a, row0, lane, s_tok, s_wt);
+        __syncwarp();
+        grid_dependency_wait();
+        if (row0 >= a.rows) return;
+        const int r = lane >> 4, hl = lane & 15;
+        A acc[kWords * V];
+        sample_row_sum<T, kWide, kNoAlloc, kBatch, 16>(a, row0 + r, hl, s_tok + r * S, s_wt + r * S, acc);
+        if (row0 + r < a.rows && hl < a.G) {
+#pragma unroll
+            for (int k = 0; k < kWords; ++k) store16<T>(a.out + (row0 + r) * a.D + (hl * kWords + k) * V, acc + k * V);
+        }
+    }
 }
 
 // Generic kernel: lanes over the head's D channels, scalar loads.

@@ -166,14 +166,29 @@ int launch_sampler(const T* value, long long s_img, long long s_tok, long long s
     const bool no_alloc = vec && B * H * N * D * (long long)sizeof(T) > (64LL << 20);
     // corner rows in flight per lane (sample_batch_depth)
     int depth = 4;
+    bool pair = false;
     if (vec) {
         DeviceFacts f;
         if (int rc = device_facts(&f, err, err_len)) return rc;
-        depth = sample_batch_depth(int(4 * L * P), a.G, wide, a.rows, f.sm_count);
+        // Two rows a warp (sample_vec_kernel's kRW = 2) when the rows take more than one wave of CTAs and their
+        // points fit 16 lanes and come from the tensors: the corner prologue then runs once for both rows. In one
+        // wave (latency-bound) a row a warp keeps each warp's chain short.
+        const bool waves = a.rows > (long long)f.sm_count * 5 * kSampleWarps;
+        pair = waves && a.G <= 16 && prod.proj == nullptr && L * P <= 16;
+        depth = sample_batch_depth(int(4 * L * P), a.G, wide, a.rows, f.sm_count, pair ? 16 : 32);
     }
     auto vec_launch = [&](auto k_wide, auto k_noalloc) -> cudaError_t {
         constexpr bool W = decltype(k_wide)::value, NA = decltype(k_noalloc)::value;
-        const dim3 g(grid), blk(kSampleWarps * 32);
+        const dim3 blk(kSampleWarps * 32);
+        if (pair) {
+            const dim3 g2(unsigned((a.rows + 2 * kSampleWarps - 1) / (2 * kSampleWarps)));
+            if (depth == 3)
+                return launch_kernel(sample_vec_kernel<T, W, NA, 3, 2>, g2, blk, 2 * smem, stream, after_producer, a);
+            if (depth == 4)
+                return launch_kernel(sample_vec_kernel<T, W, NA, 4, 2>, g2, blk, 2 * smem, stream, after_producer, a);
+            return cudaErrorInvalidValue;
+        }
+        const dim3 g(grid);
         if (depth == 3) return launch_kernel(sample_vec_kernel<T, W, NA, 3>, g, blk, smem, stream, after_producer, a);
         if (depth == 4) return launch_kernel(sample_vec_kernel<T, W, NA, 4>, g, blk, smem, stream, after_producer, a);
         if constexpr (!W) return launch_kernel(sample_vec_kernel<T, W, NA, 6>, g, blk, smem, stream, after_producer, a);
