@@ -553,25 +553,26 @@ def sharded_record(args, world, dev, cfg_name='c3'):
             times[name] = barrier_max(time_graph(g, args.steps, reps=max(5, args.reps // 5)), world)
             del g
         out = step(0, gather)
-        # the all-gather fused into the sampler (rows stored into every rank's output over NVLink): PeerGather
-        peer = None
-        if world > 1:
-            from marearts_tinydeform_b200.shard import PeerGather
-            pg = PeerGather(Bg, cfg['Q'], cfg['H'], cfg['D'], cfg['dtype'])
-            try:
+        # the all-gather fused into the sampler (rows stored into every rank's output over NVLink): PeerGather; at
+        # one rank the same kernel storing into the one output (nothing crosses NVLink)
+        from marearts_tinydeform_b200.shard import PeerGather
+        pg = PeerGather(Bg, cfg['Q'], cfg['H'], cfg['D'], cfg['dtype'])
+        try:
+            if world > 1:
                 dist.barrier()
-                g, _ = graph_time_us(lambda i: pg(*pool[i % len(pool)][:1], W, bias, shapes, starts,
-                                                  *pool[i % len(pool)][1:]), args.steps, args.warmup)
+            g, _ = graph_time_us(lambda i: pg(*pool[i % len(pool)][:1], W, bias, shapes, starts,
+                                              *pool[i % len(pool)][1:]), args.steps, args.warmup)
+            if world > 1:
                 dist.barrier()
-                times['peer'] = barrier_max(time_graph(g, args.steps, reps=max(5, args.reps // 5)), world)
-                del g
-                torch.cuda.synchronize()
-                peer = torch.equal(pg(*pool[0][:1], W, bias, shapes, starts, *pool[0][1:]).clone(), out)
-                torch.cuda.synchronize()
-                if _native.device_error(clear=True) != 0:
-                    peer = False
-            finally:
-                pg.close()
+            times['peer'] = barrier_max(time_graph(g, args.steps, reps=max(5, args.reps // 5)), world)
+            del g
+            torch.cuda.synchronize()
+            peer = torch.equal(pg(*pool[0][:1], W, bias, shapes, starts, *pool[0][1:]).clone(), out)
+            torch.cuda.synchronize()
+            if _native.device_error(clear=True) != 0:
+                peer = False
+        finally:
+            pg.close()
     N, C, H, D, L, P, Q = base[0].shape[1], cfg['C'], cfg['H'], cfg['D'], len(cfg['levels']), cfg['P'], cfg['Q']
     e = base[0].element_size()
     hbm, _ = peaks()
@@ -586,7 +587,9 @@ def sharded_record(args, world, dev, cfg_name='c3'):
             'gathered_bytes_per_rank': out.numel() * out.element_size() if gather else 0,
             'per_gpu_roofline_frac': round(alg / (times['no_gather'] * 1e-6) / 1e9 / hbm, 4),
             **({'us_per_step_peer_gather': round(times['peer'], 3), 'peer_gather_equals_nccl': peer,
-                'peer_gather': 'rows stored into every rank\'s output over NVLink by the sampler (PeerGather)'}
+                'peer_gather': ('rows stored into every rank\'s output over NVLink by the sampler (PeerGather)'
+                                if world > 1 else 'the same sampler storing into the one output (PeerGather, '
+                                                  'one rank: nothing crosses NVLink)')}
                if 'peer' in times else {}),
             'timing': 'CUDA graph of K steps (NCCL all-gather captured), median of replays, max over ranks'}
 

@@ -41,8 +41,9 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     return v;
 }
 
-// sample_vec_kernel's rows, each stored into all `world` copies of the gathered output.
-template <typename T, bool kWide, bool kNoAlloc, int kBatch>
+// sample_vec_kernel's rows (one or two a warp, the same form and sums), each stored into all `world` copies of the
+// gathered output.
+template <typename T, bool kWide, bool kNoAlloc, int kBatch, int kRW = 1>
 __global__ void __launch_bounds__(kSampleWarps * 32) sample_peer_kernel(const SampleArgs<T> a, const PeerOut<T> p) {
     using A = typename Elem<T>::acc;
     using CT = typename Coord<T>::type;
@@ -53,19 +54,36 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_peer_kernel(const Sa
     // the completion kernel may be scheduled now: it waits for this grid before it signals
     launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long row = (long long)blockIdx.x * kSampleWarps + warp;
-    const bool live = row < a.rows;
     const int S = 4 * a.L * a.P;
-    int* s_tok = reinterpret_cast<int*>(smem_raw) + warp * S;
-    CT* s_wt = reinterpret_cast<CT*>(smem_raw + kSampleWarps * S * sizeof(int)) + warp * S;
-    if (live) sample_row_corners<T>(a, row, lane, s_tok, s_wt);
-    __syncwarp();
-    grid_dependency_wait();
-    if (!live) return;
+    int* s_tok = reinterpret_cast<int*>(smem_raw) + warp * kRW * S;
+    CT* s_wt = reinterpret_cast<CT*>(smem_raw + kSampleWarps * kRW * S * sizeof(int)) + warp * kRW * S;
     A acc[kWords * V];
-    sample_row_sum<T, kWide, kNoAlloc, kBatch>(a, row, lane, s_tok, s_wt, acc);
-    if (lane < a.G) {
-        const long long at = (p.row0 + row) * a.D + (lane * kWords) * V;
+    long long row;
+    int hl;
+    if constexpr (kRW == 1) {
+        row = (long long)blockIdx.x * kSampleWarps + warp;
+        const bool live = row < a.rows;
+        if (live) sample_row_corners<T>(a, row, lane, s_tok, s_wt);
+        __syncwarp();
+        grid_dependency_wait();
+        if (!live) return;
+        hl = lane;
+        sample_row_sum<T, kWide, kNoAlloc, kBatch>(a, row, lane, s_tok, s_wt, acc);
+    } else {
+        static_assert(kRW == 2, "one or two rows a warp");
+        const long long row0 = ((long long)blockIdx.x * kSampleWarps + warp) * 2;
+        sample_pair_corners<T>(a, row0, lane, s_tok, s_wt);
+        __syncwarp();
+        grid_dependency_wait();
+        if (row0 >= a.rows) return;
+        const int r = lane >> 4;
+        hl = lane & 15;
+        row = row0 + r;
+        sample_row_sum<T, kWide, kNoAlloc, kBatch, 16>(a, row, hl, s_tok + r * S, s_wt + r * S, acc);
+        if (row >= a.rows) return;
+    }
+    if (hl < a.G) {
+        const long long at = (p.row0 + row) * a.D + (hl * kWords) * V;
         for (int r = 0; r < p.world; ++r) {
 #pragma unroll
             for (int k = 0; k < kWords; ++k) store16<T>(p.out[r] + at + k * V, acc + k * V);

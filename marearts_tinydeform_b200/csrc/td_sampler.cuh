@@ -245,6 +245,12 @@ __device__ __forceinline__ void sample_pair_corners(const SampleArgs<T>& a, long
     }
 }
 
+// Whether a grid of `rows` sampler rows takes two rows a warp: more than one wave of CTAs (five CTAs of kSampleWarps
+// rows on every SM), value rows of at most 16 load lanes, and points that fit 16 lanes and come from the tensors.
+inline bool sample_pair_form(long long rows, int G, long long L, long long P, bool producer, int sm_count) {
+    return rows > (long long)sm_count * 5 * kSampleWarps && G <= 16 && L * P <= 16 && !producer;
+}
+
 // kRW rows per warp: 1, or 2 over several waves of CTAs (throughput-bound) when the rows' points fit 16 lanes and
 // come from the tensors -- the corner prologue in one pass for both rows, and each row's corner groups in one half
 // of the warp (c3 30.6 -> 27.1 us per call, c4 83.4 -> 72.7 us on B200).

@@ -173,8 +173,7 @@ int launch_sampler(const T* value, long long s_img, long long s_tok, long long s
         // Two rows a warp (sample_vec_kernel's kRW = 2) when the rows take more than one wave of CTAs and their
         // points fit 16 lanes and come from the tensors: the corner prologue then runs once for both rows. In one
         // wave (latency-bound) a row a warp keeps each warp's chain short.
-        const bool waves = a.rows > (long long)f.sm_count * 5 * kSampleWarps;
-        pair = waves && a.G <= 16 && prod.proj == nullptr && L * P <= 16;
+        pair = sample_pair_form(a.rows, a.G, L, P, prod.proj != nullptr, f.sm_count);
         depth = sample_batch_depth(int(4 * L * P), a.G, wide, a.rows, f.sm_count, pair ? 16 : 32);
     }
     auto vec_launch = [&](auto k_wide, auto k_noalloc) -> cudaError_t {
@@ -1604,10 +1603,20 @@ int td_project_forward_peer(int dtype, const void* memory, const void* value_wei
             const size_t smem = sample_vec_smem<T>(int(L), int(P));
             DeviceFacts f;
             if (int rc = device_facts(&f, err, err_len)) return rc;
-            const int depth = sample_batch_depth(int(4 * L * P), a.G, wide, a.rows, f.sm_count);
+            // the same form and depth as launch_sampler's, so that the gathered rows equal the unfused path's
+            const bool pair = sample_pair_form(a.rows, a.G, L, P, false, f.sm_count);
+            const int depth = sample_batch_depth(int(4 * L * P), a.G, wide, a.rows, f.sm_count, pair ? 16 : 32);
             auto peer_launch = [&](auto k_wide, auto k_noalloc) -> cudaError_t {
                 constexpr bool W = decltype(k_wide)::value, NA = decltype(k_noalloc)::value;
                 const dim3 g(grid), blk(kSampleWarps * 32);
+                if (pair) {
+                    const dim3 g2(unsigned((a.rows + 2 * kSampleWarps - 1) / (2 * kSampleWarps)));
+                    if (depth == 3)
+                        return launch_kernel(sample_peer_kernel<T, W, NA, 3, 2>, g2, blk, 2 * smem, s, project, a, po);
+                    if (depth == 4)
+                        return launch_kernel(sample_peer_kernel<T, W, NA, 4, 2>, g2, blk, 2 * smem, s, project, a, po);
+                    return cudaErrorInvalidValue;
+                }
                 if (depth == 3) return launch_kernel(sample_peer_kernel<T, W, NA, 3>, g, blk, smem, s, project, a, po);
                 if (depth == 4) return launch_kernel(sample_peer_kernel<T, W, NA, 4>, g, blk, smem, s, project, a, po);
                 if constexpr (!W)

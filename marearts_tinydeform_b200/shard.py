@@ -115,6 +115,9 @@ class PeerGather:
     call ahead, since each call waits for every peer's rows). Under CUDA graph capture keep the number of captured
     calls a multiple of `buffers`. close() (collective) unmaps and frees.
 
+    Without an initialised process group (and group None) it is one rank holding the whole batch: the sampler stores
+    its rows into the one output and nothing is exchanged (the same kernels, for single-GPU use and profiling).
+
     Requirements: CUDA tensors, one GPU per rank, 1-8 ranks, the project order's vector sampler shapes (D * element
     size of 16 * 2^k bytes up to 512); the shards are batch_range's split of global_batch (shard_inputs)."""
 
@@ -122,8 +125,9 @@ class PeerGather:
         if buffers < 1:
             raise ValueError('buffers must be >= 1')
         self.group = group
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        self._dist = group is not None or (dist.is_available() and dist.is_initialized())
+        self.world = dist.get_world_size(group) if self._dist else 1
+        self.rank = dist.get_rank(group) if self._dist else 0
         if self.world > 8:
             raise ValueError('PeerGather takes at most 8 ranks')
         if device is None:
@@ -145,7 +149,10 @@ class PeerGather:
             self._own.append(ctrl)
             mine.append(handle)
             everyone = [None] * self.world
-            dist.all_gather_object(everyone, mine, group=group)
+            if self._dist:
+                dist.all_gather_object(everyone, mine, group=group)
+            else:
+                everyone[0] = mine
             # table[k][r]: buffer k (the last one is the control block) of rank r, as mapped in this process
             self._table = [[None] * self.world for _ in range(buffers + 1)]
             for r in range(self.world):
@@ -185,7 +192,8 @@ class PeerGather:
         with _on(self.device):
             for ptr in self._opened:
                 _native.peer_buffer_close(ptr, True)
-            dist.barrier(group=self.group)
+            if self._dist:
+                dist.barrier(group=self.group)
             for ptr in self._own:
                 _native.peer_buffer_close(ptr, False)
         self._own, self._opened, self.outputs = None, [], []

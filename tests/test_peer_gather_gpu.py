@@ -14,7 +14,7 @@ import pytest
 import torch
 
 from cases import make
-from marearts_tinydeform_b200 import _native
+from marearts_tinydeform_b200 import _native, ma_deform_attn
 
 pytestmark = pytest.mark.gpu
 
@@ -104,6 +104,28 @@ def test_peer_gather_on_two_gpus(cuda):
         msgs.append(errors.get())
     assert not msgs, msgs
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+
+def test_peer_gather_on_one_rank_without_a_process_group(cuda):
+    """No process group: one rank holding the whole batch, the peer sampler storing into the one output. Bit for bit
+    the operator's project order, in one wave (a row a warp) and over several waves (two rows a warp), over several
+    calls and both buffers."""
+    from marearts_tinydeform_b200.shard import PeerGather
+    for B, Q, dtype in ((2, 50, torch.float16), (8, 300, torch.bfloat16), (8, 300, torch.float16)):
+        H, D, C, levels, P = 8, 32, 256, [(80, 80), (40, 40), (20, 20)], 4
+        pg = PeerGather(B, Q, H, D, dtype)
+        try:
+            assert (pg.world, pg.rank) == (1, 0)
+            sets = [[t.cuda() for t in make(B, Q, H, D, C, levels, P, dtype=dtype, seed=60 + s)] for s in range(2)]
+            with torch.inference_mode():
+                for call in range(4):
+                    want = ma_deform_attn(*sets[call % 2], mode='project')
+                    got = pg(*sets[call % 2])
+                    torch.cuda.synchronize()
+                    assert torch.equal(got, want), f'B={B} {dtype} call {call}'
+            assert _native.device_error(clear=True) == 0
+        finally:
+            pg.close()
 
 
 def test_peer_wait_runs_out_on_a_silent_peer(cuda):
