@@ -60,7 +60,7 @@ __device__ __forceinline__ void backward_point(const BackArgs<T>& a, long long r
                                                Level& lv) {
     using CT = typename Coord<T>::type;
     const int LP = a.L * a.P;
-    lv = level_at(a.shapes, a.starts, j / a.P);
+    lv = level_at(a.shapes, a.starts, level_of(j, a.P));
     const long long i = row * LP + j;
     const CT lx = CT(to_acc(a.loc[2 * i])), ly = CT(to_acc(a.loc[2 * i + 1]));
     att = CT(to_acc(a.attn[i]));
@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(kBackWarps * 32) sample_backward_vec_kernel(co
     const long long b = row / ((long long)a.Q * a.H);
     const int h = int(row % a.H);
     // the point's geometry, location, weight and grad_out slice, all loads issued together
-    const Level lv = level_at(a.shapes, a.starts, live ? j / a.P : 0);
+    const Level lv = level_at(a.shapes, a.starts, live ? level_of(j, a.P) : 0);
     const long long i = row * LP + (live ? j : 0);
     const CT lx = live ? CT(to_acc(a.loc[2 * i])) : CT(-1e4), ly = live ? CT(to_acc(a.loc[2 * i + 1])) : CT(-1e4);
     const CT att = live ? CT(to_acc(a.attn[i])) : CT(0);

@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(kFtcThreads, 1)
             const int r = i / LP, j = i - r * LP;
             const bool g = r >= n0;
             const int q = g ? r - n0 : q00 + r;
-            const Level lv = level_at(a.shapes, a.starts, j / a.P);
+            const Level lv = level_at(a.shapes, a.starts, level_of(j, a.P));
             const int bimg = g ? b1 : b0;
             const long long k = (((long long)bimg * a.Q + q) * a.H + (g ? h1 : h0)) * LP + j;
             corners4<float>(to_acc(a.loc[2 * k]), to_acc(a.loc[2 * k + 1]), to_acc(a.attn[k]), lv, a.n_tok,

@@ -95,7 +95,7 @@ __global__ void __launch_bounds__(kFwWarps * 32, 10) fused_warp_kernel(const Fus
         const unsigned char* mb = reinterpret_cast<const unsigned char*>(a.memory + b * a.n_tok * a.C);
         const long long base = ((b * a.Q + q) * a.H + h) * LP;
         for (int j = lane; j < LP; j += 32) {
-            const Level lv = level_at(a.shapes, a.starts, j / a.P);
+            const Level lv = level_at(a.shapes, a.starts, level_of(j, a.P));
             const long long i = base + j;
             int tk[4];
             float w4[4];

@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(kProducerWarps * 32) sampling_producer_backwar
     for (int k = 0; k < 2; ++k) {
         const int j = lane + 32 * k;
         const bool on = j < LP;
-        const int l = on ? j / a.P : 0;
+        const int l = on ? level_of(j, a.P) : 0;
         if (a.ref_dim == 2) {  // the offset normaliser (w_l, h_l)
             sx[k] = on ? A(a.shapes[2 * l + 1]) : A(1);
             sy[k] = on ? A(a.shapes[2 * l]) : A(1);

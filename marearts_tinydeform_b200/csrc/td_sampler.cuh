@@ -84,7 +84,7 @@ __device__ __forceinline__ void sample_row_corners(const SampleArgs<T>& a, long 
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
             const int j = lane + 32 * k;
-            lv[k] = level_at(a.shapes, a.starts, j < LP ? j / a.P : 0);
+            lv[k] = level_at(a.shapes, a.starts, j < LP ? level_of(j, a.P) : 0);
         }
         A lx[2], ly[2], w[2];
         produce_row<T, A>(a.prod, a.shapes, row, a.H, a.L, a.P, lane, lx, ly, w);
@@ -97,7 +97,7 @@ __device__ __forceinline__ void sample_row_corners(const SampleArgs<T>& a, long 
         return;
     }
     for (int j = lane; j < LP; j += 32) {
-        const Level lv = level_at(a.shapes, a.starts, j / a.P);
+        const Level lv = level_at(a.shapes, a.starts, level_of(j, a.P));
         const long long i = row * LP + j;
         corners4<CT>(CT(to_acc(a.loc[2 * i])), CT(to_acc(a.loc[2 * i + 1])), CT(to_acc(a.attn[i])), lv, a.n_tok,
                      &s_tok[4 * j], &s_wt[4 * j], mask_b);
@@ -165,7 +165,7 @@ __device__ __forceinline__ void sample_row_sum(const SampleArgs<T>& a, long long
             const int s = s0 + u * CG;
             int t = s < S ? s_tok[s] : -1;
             TD_BOUNDS_TOKEN(t, a.n_tok);
-            w[u] = t < 0 ? A(0) : A(s_wt[s]);
+            w[u] = s < S ? A(s_wt[s]) : A(0);  // a corner outside the map already carries weight 0
             const void* src = t < 0 ? static_cast<const void*>(g_zero32)
                                     : static_cast<const void*>(vb + (long long)t * a.s_tok + v * kWords * V);
             ld_corner<kNoAlloc>(src, raw[u]);
@@ -231,7 +231,7 @@ __device__ __forceinline__ void sample_pair_corners(const SampleArgs<T>& a, long
     int* tk = s_tok + r * S + 4 * j;
     CT* wt = s_wt + r * S + 4 * j;
     if (row < a.rows) {
-        const Level lv = level_at(a.shapes, a.starts, j / a.P);
+        const Level lv = level_at(a.shapes, a.starts, level_of(j, a.P));
         const uint8_t* mask_b = a.mask != nullptr ? a.mask + row / ((long long)a.Q * a.H) * a.n_tok : nullptr;
         const long long i = row * LP + j;
         corners4<CT>(CT(to_acc(a.loc[2 * i])), CT(to_acc(a.loc[2 * i + 1])), CT(to_acc(a.attn[i])), lv, a.n_tok, tk,
@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_generic_kernel(const
         for (int k = 0; k < 2; ++k) {
             const int j = lane + 32 * k;
             if (j < LP)
-                corners4<CT>(CT(lx[k]), CT(ly[k]), CT(w[k]), lv[j / a.P], a.n_tok, &s_tok[warp][4 * j],
+                corners4<CT>(CT(lx[k]), CT(ly[k]), CT(w[k]), lv[level_of(j, a.P)], a.n_tok, &s_tok[warp][4 * j],
                              &s_wt[warp][4 * j], mask_b);
         }
     } else {
