@@ -54,7 +54,7 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_peer_kernel(const Sa
     // the completion kernel may be scheduled now: it waits for this grid before it signals
     launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int S = 4 * a.L * a.P;
+    const int S = kRW == 1 ? 4 * a.L * a.P : a.S_pad;  // list slots a row
     int* s_tok = reinterpret_cast<int*>(smem_raw) + warp * kRW * S;
     CT* s_wt = reinterpret_cast<CT*>(smem_raw + kSampleWarps * kRW * S * sizeof(int)) + warp * kRW * S;
     A acc[kWords * V];
@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_peer_kernel(const Sa
         const int r = lane >> 4;
         hl = lane & 15;
         row = row0 + r;
-        sample_row_sum<T, kWide, kNoAlloc, kBatch, 16>(a, row, hl, s_tok + r * S, s_wt + r * S, acc);
+        sample_row_sum<T, kWide, kNoAlloc, kBatch, 16, true>(a, row, hl, s_tok + r * S, s_wt + r * S, acc);
         if (row >= a.rows) return;
     }
     if (hl < a.G) {

@@ -33,6 +33,8 @@ struct SampleArgs {
     ProducerIn<T> prod;             // prod.proj set: locations and weights come from the query projection
     int Q, H, D, L, P;
     int G;                          // lanes per corner row = D * sizeof(T) / 16 (vector kernel only)
+    int S_pad = 0;                  // two rows a warp: corner slots a row's lists hold, 4 L P rounded up to whole
+                                    // batches (kBatch x 16 / G); the tail slots sample nothing
 };
 
 constexpr int kSampleWarps = 8;
@@ -131,10 +133,11 @@ inline int sample_batch_depth(int S, int G, bool wide, long long rows, int sm_co
 // 16 bytes of it (kWide: 32 bytes, for rows of 128 bytes and more -- half the load instructions, which measured 16 %
 // faster on the stress shape's 128-byte rows and made no difference on 64-byte rows), kBatch corner rows in flight
 // per lane, the lanes' groups summed with an xor butterfly. The row takes kLanes lanes (32, or 16 when a warp holds
-// two rows; lane is then the index within the row's half). On return every lane holds the finished sum of its
-// slice: head channels [(v * kWords + k) * V, + V) in acc[k * V ..], v = lane % G.
-template <typename T, bool kWide, bool kNoAlloc, int kBatch, int kLanes = 32>
-__device__ __forceinline__ void sample_row_sum(const SampleArgs<T>& a, long long row, int lane, const int* s_tok,
+// two rows; lane is then the index within the row's half). kPadded: the row's lists hold a.S_pad slots, whole
+// batches, so no slot needs a bounds test. On return every lane holds the finished sum of its slice: head channels
+// [(v * kWords + k) * V, + V) in acc[k * V ..], v = lane % G.
+template <typename T, bool kWide, bool kNoAlloc, int kBatch, int kLanes = 32, bool kPadded = false>
+__device__ __forceinline__ void sample_row_sum(const SampleArgs<T>& a, long long row, int lane, const int* s_tok_l,
                                                const typename Coord<T>::type* s_wt,
                                                typename Elem<T>::acc (&acc)[(kWide ? 2 : 1) * Elem<T>::kVec]) {
     using A = typename Elem<T>::acc;
@@ -155,7 +158,11 @@ __device__ __forceinline__ void sample_row_sum(const SampleArgs<T>& a, long long
     const int G = a.G, CG = kLanes / G, cg = lane / G, v = lane - cg * G;
 #pragma unroll
     for (int i = 0; i < kWords * V; ++i) acc[i] = A(0);
-    for (int s0 = cg; s0 < S; s0 += kBatch * CG) {
+    const int s_end = kPadded ? a.S_pad : S;
+    // the value stride of a token fits 32 bits (the host takes the vector kernels only then): a 32 x 32 -> 64-bit
+    // product per corner
+    const int s_tok = int(a.s_tok);
+    for (int s0 = cg; s0 < s_end; s0 += kBatch * CG) {
         uint4 raw[kBatch][kWords];
         A w[kBatch];
         // every load of the batch is issued unconditionally (no branch between them, so they are all in flight
@@ -163,11 +170,11 @@ __device__ __forceinline__ void sample_row_sum(const SampleArgs<T>& a, long long
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) {
             const int s = s0 + u * CG;
-            int t = s < S ? s_tok[s] : -1;
+            int t = kPadded || s < S ? s_tok_l[s] : -1;
             TD_BOUNDS_TOKEN(t, a.n_tok);
-            w[u] = s < S ? A(s_wt[s]) : A(0);  // a corner outside the map already carries weight 0
+            w[u] = kPadded || s < S ? A(s_wt[s]) : A(0);  // a corner outside the map already carries weight 0
             const void* src = t < 0 ? static_cast<const void*>(g_zero32)
-                                    : static_cast<const void*>(vb + (long long)t * a.s_tok + v * kWords * V);
+                                    : static_cast<const void*>(vb + (long long)t * s_tok + v * kWords * V);
             ld_corner<kNoAlloc>(src, raw[u]);
         }
 #pragma unroll
@@ -217,19 +224,24 @@ __device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long l
 // Registers: the 16-byte forms of the 16- and 32-bit types are held to 48 (five CTAs an SM; no spills at any
 // depth), the 32-byte forms to 64 (four CTAs; held to 48 they spill), float64 to 85 (three CTAs, no spills).
 // The corners of a warp's two rows in one pass (kRW = 2): 16 lanes a row, a lane per sampling point (L * P <= 16,
-// locations and weights read from the tensors); a row past the last one samples nothing. The corner prologue is most
+// locations and weights read from the tensors), into lists of a.S_pad slots a row; a row past the last one and the
+// tail slots sample nothing. The corner prologue is most
 // of a row's instructions (level geometry, locations, clamps, four tokens and their bounds tests): a pass per row
 // keeps only 12 of 32 lanes busy at the RT-DETR shapes' 12 points, this one 24.
 template <typename T>
 __device__ __forceinline__ void sample_pair_corners(const SampleArgs<T>& a, long long row0, int lane, int* s_tok,
                                                     typename Coord<T>::type* s_wt) {
     using CT = typename Coord<T>::type;
-    const int LP = a.L * a.P, S = 4 * LP;
+    const int LP = a.L * a.P, Sp = a.S_pad;
     const int r = lane >> 4, j = lane & 15;
     const long long row = row0 + r;
+    for (int i = 4 * LP + j; i < Sp; i += 16) {  // the tail slots of the last batch
+        s_tok[r * Sp + i] = -1;
+        s_wt[r * Sp + i] = CT(0);
+    }
     if (j >= LP) return;
-    int* tk = s_tok + r * S + 4 * j;
-    CT* wt = s_wt + r * S + 4 * j;
+    int* tk = s_tok + r * Sp + 4 * j;
+    CT* wt = s_wt + r * Sp + 4 * j;
     if (row < a.rows) {
         const Level lv = level_at(a.shapes, a.starts, level_of(j, a.P));
         const uint8_t* mask_b = a.mask != nullptr ? a.mask + row / ((long long)a.Q * a.H) * a.n_tok : nullptr;
@@ -243,6 +255,16 @@ __device__ __forceinline__ void sample_pair_corners(const SampleArgs<T>& a, long
             wt[k] = CT(0);
         }
     }
+}
+
+// Two rows a warp: corner slots a row's lists hold (whole batches of kBatch x 16 / G) and the dynamic shared memory.
+inline int sample_pair_slots(int L, int P, int G, int batch) {
+    const int step = batch * (16 / G);
+    return (4 * L * P + step - 1) / step * step;
+}
+template <typename T>
+inline size_t sample_pair_smem(int S_pad) {
+    return size_t(kSampleWarps) * 2 * S_pad * (sizeof(int) + sizeof(typename Coord<T>::type));
 }
 
 // Whether a grid of `rows` sampler rows takes two rows a warp: more than one wave of CTAs (five CTAs of kSampleWarps
@@ -261,14 +283,15 @@ __global__ void __launch_bounds__(kSampleWarps * 32, (!kWide && sizeof(T) < 8) ?
     using CT = typename Coord<T>::type;
     constexpr int V = Elem<T>::kVec;
     constexpr int kWords = kWide ? 2 : 1;
-    // per warp: kRW x S corner tokens, then kRW x S corner weights (dynamic, kRW x sample_vec_smem bytes, so that
-    // the CTAs stay small enough to become resident beside a running projection kernel)
+    // per warp: kRW lists of corner tokens, then kRW lists of corner weights (dynamic: sample_vec_smem bytes, or
+    // sample_pair_smem for two rows a warp, so that the CTAs stay small enough to become resident beside a running
+    // projection kernel)
     extern __shared__ __align__(16) unsigned char smem_raw[];
 
     // the next call's projection may be scheduled now; it waits for this grid before touching memory
     launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int S = 4 * a.L * a.P;
+    const int S = kRW == 1 ? 4 * a.L * a.P : a.S_pad;  // list slots a row
     int* s_tok = reinterpret_cast<int*>(smem_raw) + warp * kRW * S;
     CT* s_wt = reinterpret_cast<CT*>(smem_raw + kSampleWarps * kRW * S * sizeof(int)) + warp * kRW * S;
     if constexpr (kRW == 1) {
@@ -288,7 +311,7 @@ __global__ void __launch_bounds__(kSampleWarps * 32, (!kWide && sizeof(T) < 8) ?
         if (row0 >= a.rows) return;
         const int r = lane >> 4, hl = lane & 15;
         A acc[kWords * V];
-        sample_row_sum<T, kWide, kNoAlloc, kBatch, 16>(a, row0 + r, hl, s_tok + r * S, s_wt + r * S, acc);
+        sample_row_sum<T, kWide, kNoAlloc, kBatch, 16, true>(a, row0 + r, hl, s_tok + r * S, s_wt + r * S, acc);
         if (row0 + r < a.rows && hl < a.G) {
 #pragma unroll
             for (int k = 0; k < kWords; ++k) store16<T>(a.out + (row0 + r) * a.D + (hl * kWords + k) * V, acc + k * V);

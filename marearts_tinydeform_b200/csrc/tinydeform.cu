@@ -149,8 +149,9 @@ int launch_sampler(const T* value, long long s_img, long long s_tok, long long s
     const long long row_bytes = D * (long long)sizeof(T);
     a.G = int(row_bytes / 16);
     // the corner groups of a warp are summed with an xor butterfly, so G must be a power of two dividing 32
+    // (a token stride below 2^31 elements: the vector kernels form corner addresses with a 32 x 32-bit product)
     const bool vec = row_bytes % 16 == 0 && row_bytes <= 512 && (a.G & (a.G - 1)) == 0 && aligned16(value) &&
-                     aligned16(out) &&
+                     aligned16(out) && s_tok < (1LL << 31) &&
                      (s_img * (long long)sizeof(T)) % 16 == 0 && (s_tok * (long long)sizeof(T)) % 16 == 0 &&
                      (s_head * (long long)sizeof(T)) % 16 == 0;
     // 32-byte loads for rows of 128 bytes and more (G = row_bytes / 32 lanes a row, still a power of two)
@@ -181,10 +182,12 @@ int launch_sampler(const T* value, long long s_img, long long s_tok, long long s
         const dim3 blk(kSampleWarps * 32);
         if (pair) {
             const dim3 g2(unsigned((a.rows + 2 * kSampleWarps - 1) / (2 * kSampleWarps)));
+            a.S_pad = sample_pair_slots(int(L), int(P), a.G, depth);
+            const size_t ps = sample_pair_smem<T>(a.S_pad);
             if (depth == 3)
-                return launch_kernel(sample_vec_kernel<T, W, NA, 3, 2>, g2, blk, 2 * smem, stream, after_producer, a);
+                return launch_kernel(sample_vec_kernel<T, W, NA, 3, 2>, g2, blk, ps, stream, after_producer, a);
             if (depth == 4)
-                return launch_kernel(sample_vec_kernel<T, W, NA, 4, 2>, g2, blk, 2 * smem, stream, after_producer, a);
+                return launch_kernel(sample_vec_kernel<T, W, NA, 4, 2>, g2, blk, ps, stream, after_producer, a);
             return cudaErrorInvalidValue;
         }
         const dim3 g(grid);
@@ -1611,10 +1614,12 @@ int td_project_forward_peer(int dtype, const void* memory, const void* value_wei
                 const dim3 g(grid), blk(kSampleWarps * 32);
                 if (pair) {
                     const dim3 g2(unsigned((a.rows + 2 * kSampleWarps - 1) / (2 * kSampleWarps)));
+                    a.S_pad = sample_pair_slots(int(L), int(P), a.G, depth);
+                    const size_t ps = sample_pair_smem<T>(a.S_pad);
                     if (depth == 3)
-                        return launch_kernel(sample_peer_kernel<T, W, NA, 3, 2>, g2, blk, 2 * smem, s, project, a, po);
+                        return launch_kernel(sample_peer_kernel<T, W, NA, 3, 2>, g2, blk, ps, s, project, a, po);
                     if (depth == 4)
-                        return launch_kernel(sample_peer_kernel<T, W, NA, 4, 2>, g2, blk, 2 * smem, s, project, a, po);
+                        return launch_kernel(sample_peer_kernel<T, W, NA, 4, 2>, g2, blk, ps, s, project, a, po);
                     return cudaErrorInvalidValue;
                 }
                 if (depth == 3) return launch_kernel(sample_peer_kernel<T, W, NA, 3>, g, blk, smem, s, project, a, po);
