@@ -29,11 +29,14 @@ struct ProducerIn {
     int wait_first = 0;
 };
 
-// Locations (lx, ly) and softmax weight w of the points j = lane + 32 k (k = 0, 1) of row `row` = (b * Q + q) * H + h;
-// a lane with j >= L * P gets w = 0. Every lane of the warp must call it (the softmax is a warp reduction).
-// All global loads of the row are issued before the first shuffle (with wait_first, the reference points and level
-// sizes before the grid dependency wait, proj after it).
-template <typename T, typename A>
+// Locations (lx, ly) and softmax weight w of the points j = lane + kLanes k (k = 0, 1) of row `row` = (b * Q + q) * H
+// + h; a lane with j >= L * P gets w = 0. The row takes kLanes lanes: 32, or 16 when a warp holds two rows (lane is
+// then the index within the row's half, and L * P <= 32). Every lane of the warp must call it (the softmax is a
+// reduction over the row's lanes by xor shuffles; for L * P <= 16 the two widths give the same sums bit for bit, as
+// the upper half only adds -inf to the max and exact zeros to the sum). All global loads of the row are issued before
+// the first shuffle (with wait_first, the reference points and level sizes before the grid dependency wait, proj
+// after it).
+template <typename T, typename A, int kLanes = 32>
 __device__ __forceinline__ void produce_row(const ProducerIn<T>& in, const int64_t* __restrict__ shapes,
                                             long long row, int H, int L, int P, int lane, A (&lx)[2], A (&ly)[2],
                                             A (&w)[2]) {
@@ -46,7 +49,7 @@ __device__ __forceinline__ void produce_row(const ProducerIn<T>& in, const int64
     A x[2], ox[2], oy[2], rx[2], ry[2], sx[2], sy[2];
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
-        const int j = lane + 32 * k;
+        const int j = lane + kLanes * k;
         const bool on = j < LP;
         const int l = on ? j / P : 0;
         const T* __restrict__ r = in.ref + (bq * L + l) * in.ref_dim;
@@ -63,7 +66,7 @@ __device__ __forceinline__ void produce_row(const ProducerIn<T>& in, const int64
     if (in.wait_first) grid_dependency_wait();
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
-        const int j = lane + 32 * k;
+        const int j = lane + kLanes * k;
         const bool on = j < LP;
         x[k] = on ? to_acc(logit[j]) : A(-INFINITY);
         ox[k] = on ? to_acc(off[2 * j]) : A(0);
@@ -71,18 +74,18 @@ __device__ __forceinline__ void produce_row(const ProducerIn<T>& in, const int64
     }
     A m = x[0] > x[1] ? x[0] : x[1];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
+    for (int o = kLanes / 2; o > 0; o >>= 1) {
         const A y = __shfl_xor_sync(0xffffffffu, m, o);
         m = y > m ? y : m;
     }
     A e[2], sum = A(0);
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
-        e[k] = lane + 32 * k < LP ? exp(x[k] - m) : A(0);
+        e[k] = lane + kLanes * k < LP ? exp(x[k] - m) : A(0);
         sum += e[k];
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    for (int o = kLanes / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
         w[k] = e[k] / sum;

@@ -223,9 +223,9 @@ __device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long l
 // grid_dependency_wait() overlaps that kernel; value is only read after it.
 // Registers: the 16-byte forms of the 16- and 32-bit types are held to 48 (five CTAs an SM; no spills at any
 // depth), the 32-byte forms to 64 (four CTAs; held to 48 they spill), float64 to 85 (three CTAs, no spills).
-// The corners of a warp's two rows in one pass (kRW = 2): 16 lanes a row, a lane per sampling point (L * P <= 16,
-// locations and weights read from the tensors), into lists of a.S_pad slots a row; a row past the last one and the
-// tail slots sample nothing. The corner prologue is most
+// The corners of a warp's two rows in one pass (kRW = 2): 16 lanes a row, a lane per sampling point (L * P <= 16;
+// locations and weights read from the tensors, or produced from the query projection with a softmax over the row's
+// 16 lanes), into lists of a.S_pad slots a row; a row past the last one and the tail slots sample nothing. The corner prologue is most
 // of a row's instructions (level geometry, locations, clamps, four tokens and their bounds tests): a pass per row
 // keeps only 12 of 32 lanes busy at the RT-DETR shapes' 12 points, this one 24.
 template <typename T>
@@ -238,6 +238,28 @@ __device__ __forceinline__ void sample_pair_corners(const SampleArgs<T>& a, long
     for (int i = 4 * LP + j; i < Sp; i += 16) {  // the tail slots of the last batch
         s_tok[r * Sp + i] = -1;
         s_wt[r * Sp + i] = CT(0);
+    }
+    if (a.prod.proj != nullptr) {  // the producer's softmax and locations, straight from the query projection
+        using A = typename Elem<T>::acc;
+        const Level lv = level_at(a.shapes, a.starts, j < LP ? level_of(j, a.P) : 0);
+        A lx[2], ly[2], w[2];
+        // every lane takes part in its row's softmax; a row past the last one computes the last row's, unused
+        const long long prow = row < a.rows ? row : a.rows - 1;
+        produce_row<T, A, 16>(a.prod, a.shapes, prow, a.H, a.L, a.P, j, lx, ly, w);
+        if (j >= LP) return;
+        int* tk = s_tok + r * Sp + 4 * j;
+        CT* wt = s_wt + r * Sp + 4 * j;
+        if (row < a.rows) {
+            const uint8_t* mask_b = a.mask != nullptr ? a.mask + row / ((long long)a.Q * a.H) * a.n_tok : nullptr;
+            corners4<CT>(CT(lx[0]), CT(ly[0]), CT(w[0]), lv, a.n_tok, tk, wt, mask_b);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                tk[k] = -1;
+                wt[k] = CT(0);
+            }
+        }
+        return;
     }
     if (j >= LP) return;
     int* tk = s_tok + r * Sp + 4 * j;
@@ -268,13 +290,13 @@ inline size_t sample_pair_smem(int S_pad) {
 }
 
 // Whether a grid of `rows` sampler rows takes two rows a warp: more than one wave of CTAs (five CTAs of kSampleWarps
-// rows on every SM), value rows of at most 16 load lanes, and points that fit 16 lanes and come from the tensors.
-inline bool sample_pair_form(long long rows, int G, long long L, long long P, bool producer, int sm_count) {
-    return rows > (long long)sm_count * 5 * kSampleWarps && G <= 16 && L * P <= 16 && !producer;
+// rows on every SM), value rows of at most 16 load lanes, and points that fit 16 lanes.
+inline bool sample_pair_form(long long rows, int G, long long L, long long P, int sm_count) {
+    return rows > (long long)sm_count * 5 * kSampleWarps && G <= 16 && L * P <= 16;
 }
 
-// kRW rows per warp: 1, or 2 over several waves of CTAs (throughput-bound) when the rows' points fit 16 lanes and
-// come from the tensors -- the corner prologue in one pass for both rows, and each row's corner groups in one half
+// kRW rows per warp: 1, or 2 over several waves of CTAs (throughput-bound) when the rows' points fit 16 lanes -- the
+// corner prologue in one pass for both rows, and each row's corner groups in one half
 // of the warp (c3 30.6 -> 27.1 us per call, c4 83.4 -> 72.7 us on B200).
 template <typename T, bool kWide, bool kNoAlloc, int kBatch, int kRW = 1>
 __global__ void __launch_bounds__(kSampleWarps * 32, (!kWide && sizeof(T) < 8) ? 5 : (sizeof(T) == 8 ? 3 : 4))

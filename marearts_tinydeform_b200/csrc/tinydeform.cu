@@ -172,9 +172,9 @@ int launch_sampler(const T* value, long long s_img, long long s_tok, long long s
         DeviceFacts f;
         if (int rc = device_facts(&f, err, err_len)) return rc;
         // Two rows a warp (sample_vec_kernel's kRW = 2) when the rows take more than one wave of CTAs and their
-        // points fit 16 lanes and come from the tensors: the corner prologue then runs once for both rows. In one
-        // wave (latency-bound) a row a warp keeps each warp's chain short.
-        pair = sample_pair_form(a.rows, a.G, L, P, prod.proj != nullptr, f.sm_count);
+        // points fit 16 lanes: the corner prologue then runs once for both rows. In one wave (latency-bound) a row a
+        // warp keeps each warp's chain short.
+        pair = sample_pair_form(a.rows, a.G, L, P, f.sm_count);
         depth = sample_batch_depth(int(4 * L * P), a.G, wide, a.rows, f.sm_count, pair ? 16 : 32);
     }
     auto vec_launch = [&](auto k_wide, auto k_noalloc) -> cudaError_t {
@@ -1607,7 +1607,7 @@ int td_project_forward_peer(int dtype, const void* memory, const void* value_wei
             DeviceFacts f;
             if (int rc = device_facts(&f, err, err_len)) return rc;
             // the same form and depth as launch_sampler's, so that the gathered rows equal the unfused path's
-            const bool pair = sample_pair_form(a.rows, a.G, L, P, false, f.sm_count);
+            const bool pair = sample_pair_form(a.rows, a.G, L, P, f.sm_count);
             const int depth = sample_batch_depth(int(4 * L * P), a.G, wide, a.rows, f.sm_count, pair ? 16 : 32);
             auto peer_launch = [&](auto k_wide, auto k_noalloc) -> cudaError_t {
                 constexpr bool W = decltype(k_wide)::value, NA = decltype(k_noalloc)::value;

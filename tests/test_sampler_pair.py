@@ -2,15 +2,15 @@
 one pass, 16 lanes a row), which the library takes when the rows exceed one wave of CTAs (more than 40 rows per SM)
 and a row's points fit 16 lanes. Checked against the float64 oracle in every dtype, over the RT-DETR and DINO
 geometries, an odd row count (the last warp's second row past the end), 9 points a row (lanes without a point),
-16 points a row (every lane), 128- and 256-byte value rows, locations far outside the maps and a value padding mask;
-and against the one-row form, which the same images take one at a time (one wave each): both sum in the dtype's
+16 points a row (every lane), 128- and 256-byte value rows, locations far outside the maps, a value padding mask and
+the layer's project order (the producer's softmax over each row's 16 lanes); and against the one-row form, which the same images take one at a time (one wave each): both sum in the dtype's
 accumulator, in different orders, so they agree to one unit in the last place."""
 
 import pytest
 import torch
 
-from cases import make, to, upcast
-from marearts_tinydeform_b200 import ma_deform_attn
+from cases import make, make_layer, to, upcast
+from marearts_tinydeform_b200 import _native, ma_deform_attn
 from oracle import deform_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -80,3 +80,37 @@ def test_two_rows_a_warp_with_padding_mask(cuda):
         want = torch.from_numpy(O.ma_deform_attn_oracle(*upcast(args), value_padding_mask=mask.numpy()))
         atol, rtol = TOL[dtype]
         assert torch.allclose(got.double().cpu(), want, atol=atol, rtol=rtol), dtype
+
+
+@pytest.mark.parametrize('dtype', [torch.float16, torch.bfloat16, torch.float32])
+def test_two_rows_a_warp_in_the_layer(cuda, dtype):
+    """The layer's project order over several waves: the sampler's prologue runs the producer on each half-warp's row
+    (reference points and boxes, an odd row count, a padding mask), against the float64 oracle layer built from the
+    same query projection."""
+    wave = _rows_per_wave()
+    cases = [  # (B, Q, Cq, H, D, C, levels, P, ref_dim, mask)
+        (4, 300, 256, 8, 32, 256, [(40, 40), (20, 20), (10, 10)], 4, 2, False),
+        (4, 300, 256, 8, 32, 256, [(40, 40), (20, 20), (10, 10)], 4, 4, True),
+        (3, 600, 96, 3, 32, 96, [(12, 13), (6, 7), (3, 4)], 3, 4, False),
+    ]
+    for i, (B, Q, Cq, H, D, C, levels, P, ref_dim, with_mask) in enumerate(cases):
+        Q = max(Q, wave // (B * H) + 1)
+        if H % 2:
+            Q += (B * Q * H + 1) % 2  # an odd row count
+        assert B * Q * H > wave
+        args = make_layer(B, Q, Cq, H, D, C, levels, P, ref_dim=ref_dim, dtype=dtype, seed=840 + i)
+        q, ref, mem, shapes, starts, sw, sb, vw, vb = [None if t is None else t.cuda() for t in args]
+        N = sum(h * w for h, w in levels)
+        mask = (torch.rand(B, N, generator=torch.Generator().manual_seed(850 + i)) < 0.3) if with_mask else None
+        with torch.inference_mode():
+            got = _native.layer_forward(q, ref, mem, shapes, starts, H, P, sw, sb, vw, vb, None, None,
+                                        None if mask is None else mask.cuda(), order='project').double().cpu()
+            proj = _native.linear(q, sw, sb)
+        f64 = [None if t is None or t.dtype == torch.long else t.double() for t in args]
+        loc, attn = O.producer_from_proj(proj.double().cpu(), f64[1], args[3], H, P)
+        want = torch.from_numpy(O.ma_deform_attn_oracle(f64[2], f64[7], f64[8], args[3], args[4], loc, attn,
+                                                        None if mask is None else mask.numpy()))
+        atol, rtol = TOL[dtype]
+        assert torch.allclose(got, want, atol=atol, rtol=rtol), \
+            f'case {i} {dtype}: max |diff| {(got - want).abs().max().item():.3g}'
+    assert _native.device_error(clear=True) == 0
