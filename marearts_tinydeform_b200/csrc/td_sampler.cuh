@@ -289,13 +289,16 @@ inline size_t sample_pair_smem(int S_pad) {
     return size_t(kSampleWarps) * 2 * S_pad * (sizeof(int) + sizeof(typename Coord<T>::type));
 }
 
-// Whether a grid of `rows` sampler rows takes two rows a warp: more than one wave of CTAs (five CTAs of kSampleWarps
-// rows on every SM), value rows of at most 16 load lanes, and points that fit 16 lanes.
+// Whether a grid of `rows` sampler rows takes two rows a warp: the halved grid still gives every SM a CTA (2 x
+// kSampleWarps rows a CTA), value rows of at most 16 load lanes, and points that fit 16 lanes. Measured on B200: c3
+// 30.6 -> 27.1 us per call and c4 83.4 -> 72.7 (several waves, issue-bound), c1h 7.80 -> 7.66 (one wave); the layer
+// with the producer in the prologue, c1h 10.14 -> 8.91 and c3 41.0 -> 29.9. With fewer rows (800 at batch 1 with 100
+// queries: 50 CTAs) it measured slower, 7.25 -> 7.66 us.
 inline bool sample_pair_form(long long rows, int G, long long L, long long P, int sm_count) {
-    return rows > (long long)sm_count * 5 * kSampleWarps && G <= 16 && L * P <= 16;
+    return rows >= 2LL * kSampleWarps * sm_count && G <= 16 && L * P <= 16;
 }
 
-// kRW rows per warp: 1, or 2 over several waves of CTAs (throughput-bound) when the rows' points fit 16 lanes -- the
+// kRW rows per warp: 1, or 2 when the halved grid still fills the SMs and the rows' points fit 16 lanes -- the
 // corner prologue in one pass for both rows, and each row's corner groups in one half
 // of the warp (c3 30.6 -> 27.1 us per call, c4 83.4 -> 72.7 us on B200).
 template <typename T, bool kWide, bool kNoAlloc, int kBatch, int kRW = 1>

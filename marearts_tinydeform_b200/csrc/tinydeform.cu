@@ -171,9 +171,8 @@ int launch_sampler(const T* value, long long s_img, long long s_tok, long long s
     if (vec) {
         DeviceFacts f;
         if (int rc = device_facts(&f, err, err_len)) return rc;
-        // Two rows a warp (sample_vec_kernel's kRW = 2) when the rows take more than one wave of CTAs and their
-        // points fit 16 lanes: the corner prologue then runs once for both rows. In one wave (latency-bound) a row a
-        // warp keeps each warp's chain short.
+        // Two rows a warp (sample_vec_kernel's kRW = 2) when the halved grid still gives every SM a CTA and the
+        // rows' points fit 16 lanes (sample_pair_form): the corner prologue then runs once for both rows.
         pair = sample_pair_form(a.rows, a.G, L, P, f.sm_count);
         depth = sample_batch_depth(int(4 * L * P), a.G, wide, a.rows, f.sm_count, pair ? 16 : 32);
     }
@@ -188,6 +187,9 @@ int launch_sampler(const T* value, long long s_img, long long s_tok, long long s
                 return launch_kernel(sample_vec_kernel<T, W, NA, 3, 2>, g2, blk, ps, stream, after_producer, a);
             if (depth == 4)
                 return launch_kernel(sample_vec_kernel<T, W, NA, 4, 2>, g2, blk, ps, stream, after_producer, a);
+            if constexpr (!W)
+                if (depth == 6)
+                    return launch_kernel(sample_vec_kernel<T, W, NA, 6, 2>, g2, blk, ps, stream, after_producer, a);
             return cudaErrorInvalidValue;
         }
         const dim3 g(grid);
@@ -1620,6 +1622,9 @@ int td_project_forward_peer(int dtype, const void* memory, const void* value_wei
                         return launch_kernel(sample_peer_kernel<T, W, NA, 3, 2>, g2, blk, ps, s, project, a, po);
                     if (depth == 4)
                         return launch_kernel(sample_peer_kernel<T, W, NA, 4, 2>, g2, blk, ps, s, project, a, po);
+                    if constexpr (!W)
+                        if (depth == 6)
+                            return launch_kernel(sample_peer_kernel<T, W, NA, 6, 2>, g2, blk, ps, s, project, a, po);
                     return cudaErrorInvalidValue;
                 }
                 if (depth == 3) return launch_kernel(sample_peer_kernel<T, W, NA, 3>, g, blk, smem, s, project, a, po);

@@ -1,10 +1,11 @@
 """The project order's sampler with two rows a warp (sample_vec_kernel's kRW = 2: the corner prologue of both rows in
-one pass, 16 lanes a row), which the library takes when the rows exceed one wave of CTAs (more than 40 rows per SM)
-and a row's points fit 16 lanes. Checked against the float64 oracle in every dtype, over the RT-DETR and DINO
+one pass, 16 lanes a row), which the library takes when the halved grid still gives every SM a CTA (at least 16 rows
+per SM) and a row's points fit 16 lanes. Checked against the float64 oracle in every dtype, over the RT-DETR and DINO
 geometries, an odd row count (the last warp's second row past the end), 9 points a row (lanes without a point),
 16 points a row (every lane), 128- and 256-byte value rows, locations far outside the maps, a value padding mask and
-the layer's project order (the producer's softmax over each row's 16 lanes); and against the one-row form, which the same images take one at a time (one wave each): both sum in the dtype's
-accumulator, in different orders, so they agree to one unit in the last place."""
+the layer's project order (the producer's softmax over each row's 16 lanes); and against the same images run one at
+a time, which take the one-wave forms (one row a warp, or two at another corner batch depth): the sums run in
+different orders, so they agree to one unit in the last place."""
 
 import pytest
 import torch
@@ -60,7 +61,7 @@ def test_two_rows_a_warp_against_oracle_and_one_row_form(cuda, dtype):
         atol, rtol = TOL[dtype]
         err = (got.double().cpu() - want).abs().max().item()
         assert torch.allclose(got.double().cpu(), want, atol=atol, rtol=rtol), f'{name} {dtype}: max |diff| {err:.3g}'
-        if Q * H <= wave:  # one image is one wave: the one-row form
+        if Q * H <= wave:  # one image is one wave
             for b in range(B):
                 one = [dev[0][b:b + 1], *dev[1:5], dev[5][b:b + 1], dev[6][b:b + 1]]
                 with torch.inference_mode():
