@@ -108,10 +108,12 @@ def test_peer_gather_on_two_gpus(cuda):
 
 def test_peer_gather_on_one_rank_without_a_process_group(cuda):
     """No process group: one rank holding the whole batch, the peer sampler storing into the one output. Bit for bit
-    the operator's project order, in one wave (a row a warp) and over several waves (two rows a warp), over several
-    calls and both buffers."""
+    the operator's project order over several calls and both buffers: 800 rows (a row a warp), 2,400 (two rows a
+    warp, six corner rows in flight a lane: one image a rank in the eight-GPU split of c3) and 19,200 (two rows a warp
+    over several waves)."""
     from marearts_tinydeform_b200.shard import PeerGather
-    for B, Q, dtype in ((2, 50, torch.float16), (8, 300, torch.bfloat16), (8, 300, torch.float16)):
+    for B, Q, dtype in ((2, 50, torch.float16), (1, 300, torch.bfloat16), (8, 300, torch.bfloat16),
+                        (8, 300, torch.float16)):
         H, D, C, levels, P = 8, 32, 256, [(80, 80), (40, 40), (20, 20)], 4
         pg = PeerGather(B, Q, H, D, dtype)
         try:
