@@ -43,14 +43,22 @@ constexpr int kOpPad = 32;         // s_all row padding in elements: rows of 576
                                    // apart, so the two rows of each 8-lane phase of a 16-byte fragment load do not
                                    // share a bank
 
-// Queries per CTA: kSampleWarps rows of H heads each.
-__host__ __device__ inline int qpc_of(int H) { return kSampleWarps / H; }
+// Queries per CTA: rw x kSampleWarps rows (one or two a warp) of H heads each.
+__host__ __device__ inline int qpc_of(int H, int rw = 1) { return rw * kSampleWarps / H; }
 
-// Dynamic shared memory: the sampler's corner lists, the CTA's attention rows [kSampleWarps / H][HD] and the
+// The corner lists' bytes: a row a warp (sample_vec_smem), or two rows a warp of S_pad slots (S_pad > 0).
+template <typename T>
+__host__ __device__ inline size_t sample_outproj_lists(int L, int P, int S_pad) {
+    return S_pad > 0 ? size_t(kSampleWarps) * 2 * S_pad * (sizeof(int) + sizeof(typename Coord<T>::type))
+                     : sample_vec_smem<T>(L, P);
+}
+
+// Dynamic shared memory: the sampler's corner lists, the CTA's attention rows [queries per CTA][HD] and the
 // cluster's rows of one query slot [CS][HD + kOpPad], both of T.
 template <typename T>
-__host__ __device__ inline size_t sample_outproj_smem(int L, int P, int H, int HD, int CS) {
-    return sample_vec_smem<T>(L, P) + (size_t(qpc_of(H)) * size_t(HD) + size_t(CS) * size_t(HD + kOpPad)) * sizeof(T);
+__host__ __device__ inline size_t sample_outproj_smem(int L, int P, int H, int HD, int CS, int S_pad = 0) {
+    return sample_outproj_lists<T>(L, P, S_pad) +
+           (size_t(qpc_of(H, S_pad > 0 ? 2 : 1)) * size_t(HD) + size_t(CS) * size_t(HD + kOpPad)) * sizeof(T);
 }
 
 // D (+)= A * B for one m16n8k16 tile of 16-bit inputs with float32 accumulation (warp-level tensor-core MMA): A 16 x 16
@@ -71,7 +79,9 @@ __device__ __forceinline__ void mma_m16n8k16(float (&d)[4], uint32_t a0, uint32_
     }
 }
 
-template <typename T, bool kWide, bool kNoAlloc, int CS, int kBatch>
+// kRW rows a warp: 1, or 2 (sample_vec_kernel's two-row form: both rows' corner prologues in one pass, a row per
+// half-warp), so a CTA holds kRW x kSampleWarps rows = qpc_of(H, kRW) whole queries.
+template <typename T, bool kWide, bool kNoAlloc, int CS, int kBatch, int kRW = 1>
 __global__ void __launch_bounds__(kSampleWarps * 32) sample_outproj_kernel(const SampleArgs<T> a,
                                                                            const OutProjArgs<T> o) {
     using A = typename Elem<T>::acc;
@@ -82,18 +92,18 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_outproj_kernel(const
 
     launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long row = (long long)blockIdx.x * kSampleWarps + warp;
-    const bool live = row < a.rows;
-    const int S = 4 * a.L * a.P;
-    int* s_tok = reinterpret_cast<int*>(smem_raw) + warp * S;
-    CT* s_wt = reinterpret_cast<CT*>(smem_raw + kSampleWarps * S * sizeof(int)) + warp * S;
-    T* s_att = reinterpret_cast<T*>(smem_raw + sample_vec_smem<T>(a.L, a.P));
-    if (live) sample_row_corners<T>(a, row, lane, s_tok, s_wt);
-    __syncwarp();
-    grid_dependency_wait();
+    const int S = kRW == 1 ? 4 * a.L * a.P : a.S_pad;  // list slots a row
+    int* s_tok = reinterpret_cast<int*>(smem_raw) + warp * kRW * S;
+    CT* s_wt = reinterpret_cast<CT*>(smem_raw + kSampleWarps * kRW * S * sizeof(int)) + warp * kRW * S;
+    T* s_att = reinterpret_cast<T*>(smem_raw + sample_outproj_lists<T>(a.L, a.P, kRW == 1 ? 0 : a.S_pad));
 
-    // the row's attention values, rounded to T, into s_att[query of the CTA][h * D + d]
-    {
+    // the rows' attention values, rounded to T, into s_att[query of the CTA][h * D + d]
+    if constexpr (kRW == 1) {
+        const long long row = (long long)blockIdx.x * kSampleWarps + warp;
+        const bool live = row < a.rows;
+        if (live) sample_row_corners<T>(a, row, lane, s_tok, s_wt);
+        __syncwarp();
+        grid_dependency_wait();
         A acc[kWords * V];
         if (live) {
             sample_row_sum<T, kWide, kNoAlloc, kBatch>(a, row, lane, s_tok, s_wt, acc);
@@ -107,13 +117,28 @@ __global__ void __launch_bounds__(kSampleWarps * 32) sample_outproj_kernel(const
             for (int k = 0; k < kWords; ++k)
                 store16<T>(s_att + qi * o.HD + h * a.D + (lane * kWords + k) * V, acc + k * V);
         }
+    } else {
+        static_assert(kRW == 2, "one or two rows a warp");
+        const long long row0 = ((long long)blockIdx.x * kSampleWarps + warp) * 2;
+        sample_pair_corners<T>(a, row0, lane, s_tok, s_wt);  // rows past the end sample nothing: zero rows
+        __syncwarp();
+        grid_dependency_wait();
+        const int r = lane >> 4, hl = lane & 15;
+        A acc[kWords * V];
+        sample_row_sum<T, kWide, kNoAlloc, kBatch, 16, true>(a, row0 + r, hl, s_tok + r * S, s_wt + r * S, acc);
+        const int lr = 2 * warp + r, qi = lr / a.H, h = lr - qi * a.H;  // the row within the CTA
+        if (hl < a.G) {
+#pragma unroll
+            for (int k = 0; k < kWords; ++k)
+                store16<T>(s_att + qi * o.HD + h * a.D + (hl * kWords + k) * V, acc + k * V);
+        }
     }
 
     cluster_arrive();  // this CTA's attention rows are written (release)
 
     const uint32_t rank = cluster_ctarank();
     const int c0 = int(rank) * o.cols;                               // this CTA's first output column
-    const int qpc = qpc_of(a.H);
+    const int qpc = qpc_of(a.H, kRW);
     const long long first_q = ((long long)blockIdx.x - rank) * qpc;  // the cluster's first query
     T* s_all = s_att + qpc * o.HD;                                   // [CS][HD + kOpPad]
     const int HDP = o.HD + kOpPad;

@@ -257,9 +257,16 @@ int launch_sample_outproj(const T* value, long long s_img, long long s_tok, long
     // loads per CTA; of 16, slower from two images on)
     constexpr int CS = kOpCluster;
     o.cols = int((C_out + CS - 1) / CS);
-    const long long ctas = (B * Q * H + kSampleWarps - 1) / kSampleWarps;
+    DeviceFacts f;
+    if (int rc = device_facts(&f, err, err_len)) return rc;
+    // two rows a warp under the sampler's rule (sample_pair_form): a CTA then holds 16 rows, 16 / H whole queries
+    const bool pair = sample_pair_form(a.rows, a.G, L, P, f.sm_count) && (2 * kSampleWarps) % H == 0;
+    const int depth = sample_batch_depth(int(4 * L * P), a.G, wide, a.rows, f.sm_count, pair ? 16 : 32);
+    if (pair) a.S_pad = sample_pair_slots(int(L), int(P), a.G, depth);
+    const long long rows_per_cta = (pair ? 2 : 1) * kSampleWarps;
+    const long long ctas = (B * Q * H + rows_per_cta - 1) / rows_per_cta;
     const unsigned grid = unsigned((ctas + CS - 1) / CS * CS);
-    const size_t smem = sample_outproj_smem<T>(int(L), int(P), int(H), int(HD), CS);
+    const size_t smem = sample_outproj_smem<T>(int(L), int(P), int(H), int(HD), CS, pair ? a.S_pad : 0);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kSampleWarps * 32);
@@ -274,11 +281,14 @@ int launch_sample_outproj(const T* value, long long s_img, long long s_tok, long
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = after_producer ? 2 : 1;
-    DeviceFacts f;
-    if (int rc = device_facts(&f, err, err_len)) return rc;
-    const int depth = sample_batch_depth(int(4 * L * P), a.G, wide, a.rows, f.sm_count);
     auto op_launch = [&](auto k_wide, auto k_noalloc) -> cudaError_t {
         constexpr bool W = decltype(k_wide)::value, NA = decltype(k_noalloc)::value;
+        if (pair) {
+            if (depth == 3) return cudaLaunchKernelEx(&cfg, sample_outproj_kernel<T, W, NA, CS, 3, 2>, a, o);
+            if (depth == 4) return cudaLaunchKernelEx(&cfg, sample_outproj_kernel<T, W, NA, CS, 4, 2>, a, o);
+            if constexpr (!W) return cudaLaunchKernelEx(&cfg, sample_outproj_kernel<T, W, NA, CS, 6, 2>, a, o);
+            return cudaErrorInvalidValue;
+        }
         if (depth == 3) return cudaLaunchKernelEx(&cfg, sample_outproj_kernel<T, W, NA, CS, 3>, a, o);
         if (depth == 4) return cudaLaunchKernelEx(&cfg, sample_outproj_kernel<T, W, NA, CS, 4>, a, o);
         if constexpr (!W) return cudaLaunchKernelEx(&cfg, sample_outproj_kernel<T, W, NA, CS, 6>, a, o);
