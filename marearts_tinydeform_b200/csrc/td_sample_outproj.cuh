@@ -1,12 +1,12 @@
 // td_sample_outproj.cuh -- project order, sampling half with the decoder's output_proj in the same kernel:
 //   y[b, q, :] = Wo . attn[b, q, :] + bo,   attn[b, q, h*D + d] = sum_s w_s * value[b, tok_s, h, d]  (rounded to T)
 //
-// The attention half is sample_vec_kernel's (one warp per (batch, query, head) row, corners before the grid
+// The attention half is sample_vec_kernel's (one or two (batch, query, head) rows a warp, corners before the grid
 // dependency wait, one L2 round trip for the row's corner rows). What a chained output_proj costs at batch 1 is a
 // kernel boundary and a second grid, not arithmetic (300 x 256 x 256 at the RT-DETR shape). A CTA here holds whole
-// queries (kSampleWarps rows = kSampleWarps / H queries), and its cluster of CS = 8 CTAs splits the output columns:
-// after the gather every CTA writes its queries' attention rows (rounded to T, as the operator returns them) into
-// its shared memory, the cluster synchronises, each CTA copies the cluster's rows of one query slot out of its peers'
+// queries (kSampleWarps rows, or 2 x kSampleWarps with two rows a warp under the sampler's rule: rows / H queries),
+// and its cluster of CS = 8 CTAs splits the output columns: after the gather every CTA writes its queries' attention
+// rows (rounded to T, as the operator returns them) into its shared memory, the cluster synchronises, each CTA copies the cluster's rows of one query slot out of its peers'
 // shared memory (distributed shared memory, one 16-byte load per lane: each row crosses the cluster once) and
 // computes its C_out / CS output columns for the slot's CS queries. Each CTA thus reads 1 / CS of Wo (16 KB at
 // C_out = HD = 256 in 16-bit types), where a CTA computing every column of its own queries would read all 128 KB of
@@ -14,7 +14,8 @@
 // The product: 16-bit types as warp-level tensor-core tiles (mma.sync m16n8k16, float32 accumulation; the slot's
 // queries are A's rows, a warp takes an 8-column tile); float32 / float64 on CUDA cores (a lane per 16-byte chunk of
 // K, a reduce-scatter over the warp). At 8 queries per cluster a 64- or 128-row tcgen05 tile would be mostly padding.
-// The kernel keeps to 64 registers, so two of its CTAs still become resident beside a running projection CTA.
+// In 16- and 32-bit types the kernel keeps to 64 registers (both row forms), so two of its CTAs still become
+// resident beside a running projection CTA.
 // Requirements (the host checks them, else output_proj is chained): kSampleWarps % H == 0; HD * sizeof(T) = 512
 // (one 16-byte vector of K per lane: H * D = 256 in 16-bit types, 128 in float32); C_out <= 256; the sampler's
 // vector-kernel conditions; Wo 16-byte aligned.
