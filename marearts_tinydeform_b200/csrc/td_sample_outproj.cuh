@@ -6,9 +6,10 @@
 // kernel boundary and a second grid, not arithmetic (300 x 256 x 256 at the RT-DETR shape). A CTA here holds whole
 // queries (kSampleWarps rows, or 2 x kSampleWarps with two rows a warp under the sampler's rule: rows / H queries),
 // and its cluster of CS = 8 CTAs splits the output columns: after the gather every CTA writes its queries' attention
-// rows (rounded to T, as the operator returns them) into its shared memory, the cluster synchronises, each CTA copies the cluster's rows of one query slot out of its peers'
-// shared memory (distributed shared memory, one 16-byte load per lane: each row crosses the cluster once) and
-// computes its C_out / CS output columns for the slot's CS queries. Each CTA thus reads 1 / CS of Wo (16 KB at
+// rows (rounded to T, as the operator returns them) into its shared memory, the cluster synchronises, each CTA
+// copies the cluster's rows of one query slot out of its peers' shared memory (distributed shared memory, one
+// 16-byte load per lane: each row crosses the cluster once) and computes its C_out / CS output columns for the
+// slot's CS queries. Each CTA thus reads 1 / CS of Wo (16 KB at
 // C_out = HD = 256 in 16-bit types), where a CTA computing every column of its own queries would read all 128 KB of
 // it -- the cost that sank a per-CTA epilogue (39 MB of L2 reads at c1h).
 // The product: 16-bit types as warp-level tensor-core tiles (mma.sync m16n8k16, float32 accumulation; the slot's
