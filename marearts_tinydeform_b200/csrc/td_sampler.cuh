@@ -106,14 +106,17 @@ __device__ __forceinline__ void sample_row_corners(const SampleArgs<T>& a, long 
     }
 }
 
-// Corner rows in flight per lane (kBatch): a row's S = 4 L P corners are split over 32 / G lane groups, each lane
-// loading kBatch of its group's corners at once, in ceil(S / (kBatch * groups)) passes. In one wave of CTAs (every
+// Corner rows in flight per lane (kBatch): a row's S = 4 L P corners are split over lanes / G lane groups (lanes =
+// 32, or 16 for two rows a warp), each lane loading kBatch of its group's corners at once, in
+// ceil(S / (kBatch * groups)) passes. In one wave of CTAs (every
 // row resident at once, latency-bound) the fewest passes win: 48 corners over 8 groups in one pass of 6 (c1h 8.40 ->
 // 7.99 us per call, against 8 slots of which a quarter fetched a zero row); 64 corners in two passes of 4 (as fast as
 // one pass of 8 at DINO batch 1, 14.3 us). Over several waves (throughput-bound) the fewest empty slots at the
 // smallest depth win, as smaller batches need fewer registers and so more resident CTAs: 48 corners in two passes of
 // 3 (c3 31.5 -> 30.5 us), 64 in two of 4 (c4 93.4 -> 84.2 us, against one pass of 8 at 64 registers). The 32-byte
-// forms (rows of 128 bytes and more) take 3 or 4, whichever leaves fewer empty slots.
+// forms (rows of 128 bytes and more) take 3 or 4, whichever leaves fewer empty slots. Two rows a warp (four groups
+// of 64-byte rows) follow the same rule, which measured best there too: c1h 48 corners in two passes of 6; c3 in
+// three of 4 and c4 in four of 4 (2, 6 and 8 slower at both).
 inline int sample_batch_depth(int S, int G, bool wide, long long rows, int sm_count, int lanes = 32) {
     const int groups = lanes / G;
     auto passes = [&](int b) { return (S + b * groups - 1) / (b * groups); };
