@@ -228,9 +228,9 @@ __device__ __forceinline__ void sample_row_gather(const SampleArgs<T>& a, long l
 // depth), the 32-byte forms to 64 (four CTAs; held to 48 they spill), float64 to 85 (three CTAs, no spills).
 // The corners of a warp's two rows in one pass (kRW = 2): 16 lanes a row, a lane per sampling point (L * P <= 16;
 // locations and weights read from the tensors, or produced from the query projection with a softmax over the row's
-// 16 lanes), into lists of a.S_pad slots a row; a row past the last one and the tail slots sample nothing. The corner prologue is most
-// of a row's instructions (level geometry, locations, clamps, four tokens and their bounds tests): a pass per row
-// keeps only 12 of 32 lanes busy at the RT-DETR shapes' 12 points, this one 24.
+// 16 lanes), into lists of a.S_pad slots a row; a row past the last one and the tail slots sample nothing. The
+// corner prologue is most of a row's instructions (level geometry, locations, clamps, four tokens and their bounds
+// tests): a pass per row keeps only 12 of 32 lanes busy at the RT-DETR shapes' 12 points, this one 24.
 template <typename T>
 __device__ __forceinline__ void sample_pair_corners(const SampleArgs<T>& a, long long row0, int lane, int* s_tok,
                                                     typename Coord<T>::type* s_wt) {
