@@ -63,17 +63,22 @@ __device__ __forceinline__ uint4 ld_nc_no_l1(const void* p) {
 __device__ __align__(16) const uint4 g_fw_zero_row[128] = {};
 
 // CV: 16-byte vectors per lane per corner row (C * sizeof(T) = 512 * CV, CV = 1, 2 or 4). DW: outputs per lane
-// (D = 32 * DW). 96 registers a thread at 10 CTAs per SM, no spills.
-template <typename T, int CV, int DW>
-__global__ void __launch_bounds__(kFwWarps * 32, 10) fused_warp_kernel(const FusedWarpArgs<T> a) {
+// (D = 32 * DW). 96 registers a thread at 10 CTAs per SM, no spills. kDeep (512-byte rows, grids of at most 8 rows
+// per SM): 24 corner rows in flight per lane instead of 16, at 6 CTAs per SM -- with few rows an SM the kernel is a
+// chain of gather round trips, and 48 corners then take two instead of three (B200, float16, batch 1 with 100
+// queries: 6.19 -> 5.61 us per call); with more rows it measured slower (2,400 rows: 9.2 -> 10.4 us).
+template <typename T, int CV, int DW, bool kDeep = false>
+__global__ void __launch_bounds__(kFwWarps * 32, kDeep ? 6 : 10) fused_warp_kernel(const FusedWarpArgs<T> a) {
+    static_assert(!kDeep || CV == 1, "the deep batch is for 512-byte rows");
     constexpr int V = Elem<T>::kVec;      // elements per 16-byte vector
     constexpr int D = 32 * DW;
-    constexpr int kB = CV == 4 ? 2 : 16 / CV;  // corner rows in flight per lane
+    constexpr int kB = kDeep ? 24 : (CV == 4 ? 2 : 16 / CV);  // corner rows in flight per lane
     constexpr int kRowBytes = 512 * CV;
+    constexpr int kSlots = (kMaxCorners + kB - 1) / kB * kB;   // the longest padded list
     // per corner: the address of its memory row (or of the zero row) and its weight; the list is padded with
     // zero-weight entries on the zero row to a multiple of kB, so the gather loop needs no bounds test
-    __shared__ const unsigned char* s_ptr[kFwWarps][kMaxCorners];
-    __shared__ float s_wt[kFwWarps][kMaxCorners];
+    __shared__ const unsigned char* s_ptr[kFwWarps][kSlots];
+    __shared__ float s_wt[kFwWarps][kSlots];
 
     grid_dependency_wait();
     launch_dependents();

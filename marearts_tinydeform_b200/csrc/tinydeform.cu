@@ -390,11 +390,16 @@ int launch_fused_warp(const FusedWarpArgs<T>& a, int64_t C, int64_t D, cudaStrea
         g_launches.fetch_add(1, std::memory_order_relaxed);
         return check_launch(err, err_len, "fused_warp_kernel");
     };
-    if (D == 32)
-        return CV == 1 ? go(fused_warp_kernel<T, 1, 1>)
-                       : (CV == 2 ? go(fused_warp_kernel<T, 2, 1>) : go(fused_warp_kernel<T, 4, 1>));
-    return CV == 1 ? go(fused_warp_kernel<T, 1, 2>)
-                   : (CV == 2 ? go(fused_warp_kernel<T, 2, 2>) : go(fused_warp_kernel<T, 4, 2>));
+    // 512-byte rows in a grid of at most 8 rows per SM take the deeper corner batch (fused_warp_kernel's kDeep)
+    DeviceFacts f;
+    if (int rc = device_facts(&f, err, err_len)) return rc;
+    const bool deep = CV == 1 && a.rows <= 8LL * f.sm_count;
+    if (D == 32) {
+        if (CV == 1) return deep ? go(fused_warp_kernel<T, 1, 1, true>) : go(fused_warp_kernel<T, 1, 1>);
+        return CV == 2 ? go(fused_warp_kernel<T, 2, 1>) : go(fused_warp_kernel<T, 4, 1>);
+    }
+    if (CV == 1) return deep ? go(fused_warp_kernel<T, 1, 2, true>) : go(fused_warp_kernel<T, 1, 2>);
+    return CV == 2 ? go(fused_warp_kernel<T, 2, 2>) : go(fused_warp_kernel<T, 4, 2>);
 }
 
 template <typename T>
